@@ -1,0 +1,488 @@
+"""Paged-KV decode benchmark for B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one attention layer, bf16 K/V,
+14 query / 2 KV heads, head_dim 64, page size 16, a pool of 65 536 pages,
+64 sequences with context lengths U[256, 4096] (seed 2) whose block tables
+are a random permutation of the free page ids (seed 3), Q/K/V ~ N(0, 1)
+(seed 4).  One step = append one token per sequence (KV append kernel),
+then paged decode attention over every sequence (decode kernel).
+
+  value  decode tokens/s over all ranks, device-timed with CUDA events, inputs
+         resident in HBM, L2 flushed (256 MiB write) before every step.
+  e2e    the same step through the C ABI with pinned HOST buffers: Q, new
+         K/V, slots and seq_lens copied host->device and the output copied
+         back inside the timed region.
+  roofline  the decode kernel: algorithmic bytes per launch / its mean
+         CUDA-event time, against MEASURED_PEAKS.json hbm_gbs.
+  cpu_baseline  the reference algorithm on the host cores (oracle port of
+         the cat-grown contiguous cache decode step), bounded sample.
+
+Multi-GPU: replicas only.  Every rank runs its own pool and sequences; no
+data-path collective.  torch.distributed (NCCL) only provides the barrier
+and the max-over-ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s & paged-attn KV-read HBM GB/s vs peak"
+N_SEQS, HQ, HKV, D, PS, NUM_PAGES = 64, 14, 2, 64, 16, 65536
+L_LO, L_HI = 256, 4096
+B_TOK = 2 * HKV * D * 2  # K+V bytes per token per layer (bf16)
+
+
+def workload_config(extra=None):
+    cfg = {
+        "workload": "BASELINE config 2: isolated paged-KV microbench, 1 layer, bf16 K/V, GQA 14q/2kv, head_dim 64, "
+                    "page 16, pool 65536 pages, 64 seqs, ctx U[256,4096]; step = append 1 token/seq + decode",
+        "n_seqs": N_SEQS, "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D, "page_size": PS,
+        "num_pages": NUM_PAGES, "ctx_range": [L_LO, L_HI], "seeds": {"lens": 2, "tables": 3, "qkv": 4},
+        "l2": "flushed before every step by a 256 MiB device write (per-step KV read ~71 MB < 126 MB L2)",
+    }
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+def make_lens(n=N_SEQS):
+    rng = np.random.default_rng(2)
+    return rng.integers(L_LO, L_HI + 1, size=n).astype(np.int64)
+
+
+def decode_bytes(seq_lens: np.ndarray) -> int:
+    """Algorithmic bytes of one decode launch (K+V read once, Q in, O out, page ids, lens/indptr)."""
+    pages = np.ceil(seq_lens / PS).astype(np.int64)
+    return int(seq_lens.sum() * B_TOK + N_SEQS * HQ * D * 2 * 2 + 4 * pages.sum() + 8 * N_SEQS)
+
+
+def append_bytes(n_tok: int) -> int:
+    return int(2 * n_tok * HKV * D * 2 + 8 * n_tok)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (one GPU)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.tmp,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.tmp.flush()
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ------------------------------------------------------------ distributed
+def dist_setup(n_gpus: int):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def barrier(pg):
+    import torch
+
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(pg, x: float) -> float:
+    if pg is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(pg, x: float) -> float:
+    if pg is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- our arm
+def build_state(steps_total: int, device):
+    import torch
+
+    from mitten_b200 import paged
+
+    lens0 = make_lens()
+    rng = np.random.default_rng(3)
+    perm = rng.permutation(NUM_PAGES).astype(np.int32)
+    need = [(int(L) + steps_total + 1 + PS - 1) // PS for L in lens0]
+    assert sum(need) <= NUM_PAGES
+    indptr = np.zeros(N_SEQS + 1, np.int32)
+    indptr[1:] = np.cumsum(need)
+    tables = perm[: indptr[-1]]
+    pool = paged.PagedKVPool(1, NUM_PAGES, PS, HKV, D, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4)
+    # initial context: L_s tokens per sequence, written with the append kernel
+    slots = np.concatenate([tables[indptr[s] + np.arange(L) // PS].astype(np.int64) * PS + np.arange(L) % PS
+                            for s, L in enumerate(lens0)])
+    n0 = len(slots)
+    for lo in range(0, n0, 1 << 18):
+        hi = min(n0, lo + (1 << 18))
+        k = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+        v = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+        pool.append(0, k, v, torch.from_numpy(slots[lo:hi]).to(device))
+    torch.cuda.synchronize()
+    st = {
+        "pool": pool, "lens0": lens0, "indptr": torch.from_numpy(indptr).to(device),
+        "indices": torch.from_numpy(tables.copy()).to(device), "max_pages": int(max(need)), "gen": gen,
+        "tables": tables, "indptr_np": indptr,
+    }
+    return st
+
+
+def step_inputs(st, step: int, device):
+    """Slots and seq_lens for step `step` (host numpy)."""
+    pos = st["lens0"] + step  # position of the appended token
+    tables, indptr = st["tables"], st["indptr_np"]
+    slots = (tables[indptr[:-1] + pos // PS].astype(np.int64) * PS + pos % PS).astype(np.int64)
+    return slots, (pos + 1).astype(np.int32)
+
+
+def run_ours(args, rank, world, local, pg):
+    import torch
+
+    from mitten_b200 import _lib, paged
+
+    device = torch.device("cuda", local)
+    total_steps = args.warmup + args.steps
+    st = build_state(total_steps + 1, device)
+    pool = st["pool"]
+    split = paged.default_split(pool, N_SEQS, int(st["indptr_np"][-1]), st["max_pages"], HQ)
+    ws = paged.DecodeWorkspace.for_shape(pool, N_SEQS, HQ, st["max_pages"], split)
+    gen = st["gen"]
+    q_all = torch.randn((total_steps, N_SEQS, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    k_all = torch.randn((total_steps, N_SEQS, HKV, D), generator=gen, device=device).to(torch.bfloat16)
+    v_all = torch.randn((total_steps, N_SEQS, HKV, D), generator=gen, device=device).to(torch.bfloat16)
+    slots_np, lens_np = zip(*[step_inputs(st, i, device) for i in range(total_steps)])
+    slots_all = torch.from_numpy(np.stack(slots_np)).to(device)
+    lens_all = torch.from_numpy(np.stack(lens_np)).to(device)
+    out = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream()
+    scale = D ** -0.5
+
+    def step(i, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        pool.append(0, k_all[i], v_all[i], slots_all[i])
+        if ev is not None:
+            ev[1].record(stream)
+        paged.paged_decode(pool, 0, q_all[i], st["indptr"], st["indices"], lens_all[i], st["max_pages"],
+                           scale=scale, phantom=False, pages_per_split=split, out=out, workspace=ws)
+        if ev is not None:
+            ev[2].record(stream)
+
+    # correctness spot-check of the last warm-up step happens in tests; here: run warm-up
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    barrier(pg)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        barrier(pg)
+        for j in range(args.steps):
+            flush.zero_()
+            step(args.warmup + j, evs[j])
+        torch.cuda.synchronize()
+    barrier(pg)
+    t_append = [evs[j][0].elapsed_time(evs[j][1]) * 1e-3 for j in range(args.steps)]
+    t_decode = [evs[j][1].elapsed_time(evs[j][2]) * 1e-3 for j in range(args.steps)]
+    t_step = sum(t_append) + sum(t_decode)
+    code, detail = paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail}) during the bench")
+    dec_bytes = [decode_bytes(lens_np[args.warmup + j].astype(np.int64)) for j in range(args.steps)]
+    kv_bytes = sum(int(lens_np[args.warmup + j].sum()) * B_TOK for j in range(args.steps))
+
+    # ---- e2e through the C ABI with pinned host buffers
+    e2e = run_e2e(args, st, pool, split, ws, device, stream, total_steps)
+
+    t_max = max_over_ranks(pg, t_step)
+    dec_max = max_over_ranks(pg, sum(t_decode))
+    tokens = sum_over_ranks(pg, float(N_SEQS * args.steps))
+    e2e_t = max_over_ranks(pg, e2e["t"])
+    e2e_tokens = sum_over_ranks(pg, float(N_SEQS * e2e["steps"]))
+    peaks = load_peaks()
+    achieved = (sum(dec_bytes) / len(dec_bytes)) / (sum(t_decode) / len(t_decode)) / 1e9
+    res = {
+        "metric": METRIC, "value": tokens / t_max, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q/K/V)",
+        "config": workload_config({"parallelism": f"replicas{world}", "pages_per_split": split}),
+        "kv_read_gbs": sum_over_ranks(pg, kv_bytes) / t_max / 1e9,
+        "decode_us_per_step": 1e6 * dec_max / args.steps,
+        "append_us_per_step": 1e6 * sum(t_append) / args.steps,
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<64,7>", "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_source": peaks["source"], "traffic": traffic_from_profile(),
+                     "algorithmic_bytes_per_launch": sum(dec_bytes) / len(dec_bytes)},
+        "e2e": {"value": e2e_tokens / e2e_t, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
+                "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"]},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    return res
+
+
+def run_e2e(args, st, pool, split, ws, device, stream, total_steps):
+    """Append + decode through the C ABI with host inputs/outputs copied inside the timed region."""
+    import ctypes as C
+
+    import torch
+
+    from mitten_b200 import _lib
+
+    lib = _lib.lib()
+    steps = args.steps
+    gen = torch.Generator()
+    gen.manual_seed(5)
+    q_h = torch.randn((N_SEQS, HQ, D), generator=gen).to(torch.bfloat16).pin_memory()
+    k_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
+    v_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
+    o_h = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory()
+    slot_h = [torch.from_numpy(step_inputs(st, i, device)[0]).pin_memory() for i in range(total_steps)]
+    len_h = [torch.from_numpy(step_inputs(st, i, device)[1]).pin_memory() for i in range(total_steps)]
+    q_d, k_d, v_d = (torch.empty_like(x, device=device) for x in (q_h, k_h, v_h))
+    o_d = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
+    s_d = torch.empty(N_SEQS, dtype=torch.int64, device=device)
+    l_d = torch.empty(N_SEQS, dtype=torch.int32, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    sp = int(stream.cuda_stream)
+    scale = D ** -0.5
+
+    def one(i):
+        q_d.copy_(q_h, non_blocking=True)
+        k_d.copy_(k_h, non_blocking=True)
+        v_d.copy_(v_h, non_blocking=True)
+        s_d.copy_(slot_h[i], non_blocking=True)
+        l_d.copy_(len_h[i], non_blocking=True)
+        _lib.check(lib.mtn_kv_append(C.byref(pool.layout), 0, k_d.data_ptr(), v_d.data_ptr(), _lib.MTN_DTYPE_BF16,
+                                     HKV * D, s_d.data_ptr(), N_SEQS, sp))
+        _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_d.data_ptr(), _lib.MTN_DTYPE_BF16,
+                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
+                                        st["indices"].data_ptr(), l_d.data_ptr(), st["max_pages"], split, scale, 0,
+                                        ws.buf.data_ptr(), ws.nbytes, sp))
+        o_h.copy_(o_d, non_blocking=True)
+
+    # the pool already holds warm-up + timed appends of the device arm: rewrite the same slots
+    for i in range(min(3, total_steps)):
+        one(i)
+    torch.cuda.synchronize()
+    t = 0.0
+    for j in range(steps):
+        i = j % total_steps
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        one(i)
+        b.record(stream)
+        b.synchronize()
+        t += a.elapsed_time(b) * 1e-3
+    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, slot_h[0], len_h[0]))
+    d2h = o_h.numel() * o_h.element_size()
+    return {"t": t, "steps": steps, "h2d": h2d, "d2h": d2h}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_workload(n_steps_cap: int, seconds: float, threads_note: str):
+    """Time the oracle port of the reference decode step (cat-grown caches) on the host."""
+    import oracle
+
+    lens = make_lens()
+    rng = np.random.default_rng(4)
+    kp, vp = [], []
+    for L in lens:
+        k = np.zeros((HKV, int(L) + 1, D), np.float32)
+        v = np.zeros((HKV, int(L) + 1, D), np.float32)
+        k[:, 1:] = rng.standard_normal((HKV, int(L), D), dtype=np.float32)
+        v[:, 1:] = rng.standard_normal((HKV, int(L), D), dtype=np.float32)
+        kp.append(k)
+        vp.append(v)
+    dec = oracle.CatGrownDecode(kp, vp, HQ, D ** -0.5)
+    done, t = 0, 0.0
+    while done < n_steps_cap and t < seconds:
+        q = rng.standard_normal((N_SEQS, HQ, D), dtype=np.float32)
+        kn = rng.standard_normal((N_SEQS, HKV, D), dtype=np.float32)
+        vn = rng.standard_normal((N_SEQS, HKV, D), dtype=np.float32)
+        t0 = time.perf_counter()
+        dec.step(q, kn, vn)
+        t += time.perf_counter() - t0
+        done += 1
+    dec.close()
+    return done, t
+
+
+def cpu_baseline(seconds: float) -> dict:
+    import oracle
+
+    oracle.build()
+    cores = oracle.num_threads()
+    done, t = cpu_workload(10 ** 9, seconds, "")
+    return {"value": N_SEQS * done / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{done} decode steps of the full config-2 batch (64 seqs) through the oracle port of the "
+                      f"reference cat-grown f32 decode (Tensor::cat growth, GQA repeat, -1e10 mask, softmax), "
+                      f"{t:.1f} s, OpenMP {cores} threads"}
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU algorithm (oracle port; the Rust reference cannot be built here)."""
+    import oracle
+
+    oracle.build()
+    cores = oracle.num_threads()
+    # bounded: every step is the whole 64-sequence decode step; cap total time
+    warm, _ = cpu_workload(max(args.warmup, 0), 60.0, "")
+    done, t = cpu_workload(args.steps, args.ref_seconds, "")
+    value = N_SEQS * done / t
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": done,
+        "warmup": args.warmup, "ms_per_step": 1e3 * t / max(done, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V)",
+        "config": workload_config({"parallelism": "host cores"}), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{done} of {args.steps} requested steps of the full config-2 batch "
+                                   f"(cap {args.ref_seconds:.0f} s); the Rust reference cannot be built here"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def traffic_from_profile():
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "decode_traffic.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, rank, world)), flush=True)
+        return 0
+    rank, world, local, pg = dist_setup(args.gpus)
+    try:
+        res = run_ours(args, rank, world, local, pg)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if pg is not None:
+            pg.barrier()
+            pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,339 @@
+/*
+ * mitten_kv.h -- C ABI of the B200 (sm_100a) paged-KV library.
+ *
+ * One shared library (libmitten_kv.so) exports everything below.  Plain C:
+ * opaque handles, plain pointers and sizes, int status codes, no callbacks,
+ * no exceptions across the boundary.  Every device-pointer argument is
+ * caller-owned and must stay alive until the given stream reaches the call.
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *
+ * Reference interfaces replaced (paths inside tianhaoz95/mitten):
+ *   - page pool / allocator ........ inference-engine/src/kv_pool.rs:4-69
+ *   - radix prefix cache ........... inference-engine/src/radix_cache.rs:37-303
+ *   - admission / chunked prefill .. inference-engine/src/prefill.rs:6-115
+ *   - decode collection ............ inference-engine/src/decode.rs:6-47
+ *   - batch assembly / transition .. inference-engine/src/scheduler.rs:8-223
+ *   - Batch record ................. inference-backend/src/batch.rs:7-36
+ *   - BackendHandle::forward ....... inference-backend/src/backend.rs:16-21,
+ *                                    inference-backend/src/burn_backend.rs:31-80
+ *   - KVCacheState::Attention ...... inference-model-common/src/lib.rs:5-13
+ *   - KV append (Tensor::cat) ...... inference-model-qwen/src/model.rs:390-392
+ *   - attention core ............... inference-model-qwen/src/model.rs:394-416
+ *   - causal mask .................. inference-model-qwen/src/model.rs:542-555
+ *   - phantom zero KV row .......... inference-model-qwen/src/model.rs:207-220
+ *
+ * Status codes map onto inference-backend/src/error.rs:3-13:
+ *   MTN_ENOMEM -> EngineError::OutOfKvPages; every other non-zero code ->
+ *   EngineError::Backend(mtn_last_error()).
+ */
+#ifndef MITTEN_KV_H
+#define MITTEN_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MTN_API __attribute__((visibility("default")))
+#else
+#define MTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status and errors                                                        */
+/* ------------------------------------------------------------------------ */
+
+enum {
+  MTN_OK = 0,
+  MTN_EINVAL = 1,    /* invalid argument; nothing was launched            */
+  MTN_ENOMEM = 2,    /* out of KV pages (or of device memory)            */
+  MTN_ECUDA = 3,     /* CUDA runtime error                                */
+  MTN_ETIMEOUT = 4,  /* a bounded device-side wait ran out                */
+  MTN_EDEVICE = 5    /* a kernel flagged bad metadata (see device error)  */
+};
+
+/* Message for the last non-zero status returned on the calling thread.
+ * Replaces the String inside EngineError::Backend (error.rs:5). */
+MTN_API const char* mtn_last_error(void);
+MTN_API const char* mtn_version(void);
+
+/* Device-side error word written by kernels that meet out-of-range metadata
+ * (page id >= num_pages, seq_len beyond its pages, ...).  Kernels never trap:
+ * they clamp, finish, and record the first error here.  Reading it
+ * synchronises `device`.  Returns MTN_OK and stores the code (0 = none)
+ * and the kernel-specific detail word; `clear` resets it. */
+MTN_API int mtn_device_error(int device, int clear, int32_t* code, int32_t* detail);
+
+/* ------------------------------------------------------------------------ */
+/* Device KV pool layout                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Pool memory: bf16 [num_layers][2 (K,V)][num_pages][num_kv_heads][page_size][head_dim].
+ * One page of one layer is the [num_kv_heads, page_size, head_dim] slice of
+ * the reference's per-request KVCacheState::Attention tensor
+ * [1, heads, seq, head_dim] (model-common lib.rs:5-13), so each
+ * (page, kv head) is one contiguous page_size*head_dim*2-byte slab. */
+typedef struct {
+  void* base;            /* device pointer, 256-byte aligned               */
+  int64_t num_pages;
+  int32_t num_layers;
+  int32_t page_size;     /* tokens per page                                */
+  int32_t num_kv_heads;
+  int32_t head_dim;      /* 64, 128 or 256                                 */
+} mtn_kv_layout;
+
+/* KvCachePool::required_bytes (kv_pool.rs:58-68):
+ * 2 * num_layers * num_pages * page_size * num_kv_heads * head_dim * dtype_bytes. */
+MTN_API size_t mtn_kv_required_bytes(int64_t num_pages, int64_t page_size, int64_t num_layers,
+                             int64_t num_kv_heads, int64_t head_dim, int64_t dtype_bytes);
+
+/* Allocate (cudaMalloc on `device`) and zero a pool; fills `out`.  The
+ * caller may instead point `base` at its own allocation of
+ * mtn_kv_required_bytes(..., 2) bytes. */
+MTN_API int mtn_kv_pool_alloc(int device, mtn_kv_layout* out);
+MTN_API int mtn_kv_pool_free(mtn_kv_layout* pool);
+
+/* Element offset helpers (host-side, no device access). */
+MTN_API int64_t mtn_kv_page_offset(const mtn_kv_layout* pool, int32_t layer, int32_t kv, int64_t page);
+
+/* ------------------------------------------------------------------------ */
+/* Kernels                                                                  */
+/* ------------------------------------------------------------------------ */
+
+enum {
+  MTN_DTYPE_BF16 = 0,
+  MTN_DTYPE_F32 = 1
+};
+
+/* Attention flags. */
+enum {
+  /* Add the reference's all-zero first K/V row (qwen model.rs:207-220) to
+   * every softmax: one key with score 0 and a zero value. */
+  MTN_ATTN_PHANTOM_ZERO_SLOT = 1u << 0
+};
+
+/* Per-token pool slot for a batch (Batch -> slot map; batch.rs:7-36):
+ *   token t of sequence r (qo_indptr[r] <= t < qo_indptr[r+1]) at absolute
+ *   position positions[t] goes to
+ *   slot = kv_indices[kv_indptr[r] + pos / page_size] * page_size + pos % page_size.
+ * Positions past a sequence's pages give slot -1 and a device error. */
+MTN_API int mtn_build_slot_mapping(const int32_t* qo_indptr, const int32_t* positions,
+                           const int32_t* kv_indptr, const int32_t* kv_indices,
+                           int32_t n_seqs, int64_t n_tokens, int32_t page_size,
+                           int64_t* slots, void* stream);
+
+/* KV append: the paged replacement for the per-layer Tensor::cat of
+ * qwen model.rs:390-392.  k/v: [n_tokens][num_kv_heads][head_dim], element
+ * type `src_dtype` (bf16 copied bit-exact, f32 rounded to nearest even),
+ * token rows `src_stride` elements apart (>= num_kv_heads*head_dim; lets a
+ * caller pass a slice of a fused QKV projection).  slot < 0 skips a token. */
+MTN_API int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer,
+                  const void* k, const void* v, int32_t src_dtype, int64_t src_stride,
+                  const int64_t* slots, int64_t n_tokens, void* stream);
+
+/* Page copy for copy-on-write and prefix forks: for i < n_pages copy page
+ * src[i] onto page dst[i] in every layer, K and V, every head. */
+MTN_API int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages,
+                  const int32_t* dst_pages, int64_t n_pages, void* stream);
+
+/* Gather sequences back into the reference's contiguous cache layout
+ * KVCacheState::Attention [num_kv_heads][seq_len][head_dim] (bf16):
+ * sequence r lands at out + out_offsets[r]*num_kv_heads*head_dim, where
+ * out_offsets is the exclusive prefix sum of seq_lens. */
+MTN_API int mtn_kv_gather(const mtn_kv_layout* pool, int32_t layer,
+                  const int32_t* kv_indptr, const int32_t* kv_indices,
+                  const int32_t* seq_lens, const int64_t* out_offsets, int32_t n_seqs,
+                  void* out_k, void* out_v, int64_t total_tokens, void* stream);
+
+/* Paged decode attention (one query token per sequence), split-KV.
+ *   q: [n_seqs][num_q_heads][head_dim] (q_dtype), o: same shape (o_dtype).
+ *   Sequence r reads pages kv_indices[kv_indptr[r] .. kv_indptr[r+1]) and its
+ *   first seq_lens[r] tokens (the query's own K/V already appended).
+ *   q head h uses kv head h / (num_q_heads / num_kv_heads) (model.rs:398-408).
+ *   scale multiplies q.k (model.rs:298, 413).
+ *   pages_per_split: KV pages per CTA (0 = choose from max_pages_per_seq);
+ *   the workspace must hold mtn_paged_decode_workspace_bytes(...) bytes and
+ *   must be zeroed once before its first use (the kernels leave it reusable).
+ *   Concurrent calls must not share a workspace. */
+MTN_API size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                                        int32_t head_dim, int32_t max_pages_per_seq,
+                                        int32_t pages_per_split);
+MTN_API int32_t mtn_paged_decode_default_split(const mtn_kv_layout* pool, int32_t n_seqs,
+                                       int64_t total_pages, int32_t max_pages_per_seq,
+                                       int32_t num_q_heads);
+MTN_API int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer,
+                     const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
+                     int32_t n_seqs, int32_t num_q_heads,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
+                     int32_t max_pages_per_seq, int32_t pages_per_split,
+                     float scale, uint32_t flags,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Chunked-prefill attention over paged KV (tcgen05 / TMEM tensor cores).
+ *   q: [total_q][num_q_heads][head_dim] bf16; o: same shape (o_dtype).
+ *   Sequence r owns query rows qo_indptr[r] .. qo_indptr[r+1]; those are its
+ *   LAST q_len = qo_indptr[r+1]-qo_indptr[r] tokens out of seq_lens[r]
+ *   (their K/V already appended), so query i sits at position
+ *   seq_lens[r] - q_len + i and sees keys at positions <= its own
+ *   (generate_causal_mask, model.rs:542-555). */
+MTN_API size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
+                                         int32_t num_kv_heads, int32_t head_dim);
+MTN_API int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer,
+                      const void* q, void* o, int32_t o_dtype,
+                      int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
+                      const int32_t* qo_indptr, const int32_t* kv_indptr,
+                      const int32_t* kv_indices, const int32_t* seq_lens,
+                      int32_t max_q_len, float scale, uint32_t flags,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Greedy sampling on the device (scheduler.rs:186-199 temperature <= 0):
+ * out[r] = index of the first strict maximum of logits row r. */
+MTN_API int mtn_argmax_rows(const float* logits, int64_t n_rows, int64_t vocab, int32_t* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Host mirror: page allocator (kv_pool.rs:4-69) + refcount extension       */
+/* ------------------------------------------------------------------------ */
+
+typedef struct mtn_page_pool mtn_page_pool;
+
+/* KvCachePool::new (kv_pool.rs:18-27): free stack 0..n reversed, so the
+ * first allocations are 0, 1, 2, ... */
+MTN_API int mtn_page_pool_create(int64_t num_pages, int32_t page_size, mtn_page_pool** out);
+MTN_API void mtn_page_pool_destroy(mtn_page_pool* pool);
+/* KvCachePool::allocate (kv_pool.rs:30-37); MTN_ENOMEM when exhausted.
+ * owner is the 128-bit RequestId as two halves.  The page starts with
+ * reference count 1. */
+MTN_API int mtn_page_pool_allocate(mtn_page_pool* pool, uint64_t owner_hi, uint64_t owner_lo, uint32_t* page);
+/* KvCachePool::free (kv_pool.rs:40-47): MTN_EINVAL for a page that is not
+ * in use (the reference's debug_assert), leaving the pool unchanged. */
+MTN_API int mtn_page_pool_free(mtn_page_pool* pool, uint32_t page);
+MTN_API int64_t mtn_page_pool_free_pages(const mtn_page_pool* pool);
+MTN_API int64_t mtn_page_pool_total_pages(const mtn_page_pool* pool);
+MTN_API int32_t mtn_page_pool_page_size(const mtn_page_pool* pool);
+/* 0 = Free, 1 = InUse (owner halves stored when non-NULL). */
+MTN_API int mtn_page_pool_state(const mtn_page_pool* pool, uint32_t page, int32_t* in_use,
+                        uint64_t* owner_hi, uint64_t* owner_lo);
+/* Extension (no counterpart in the reference): shared pages.  retain adds a
+ * reference; release drops one and returns the page to the free stack when
+ * the count reaches zero (*freed = 1). */
+MTN_API int mtn_page_pool_retain(mtn_page_pool* pool, uint32_t page);
+MTN_API int mtn_page_pool_release(mtn_page_pool* pool, uint32_t page, int32_t* freed);
+MTN_API int32_t mtn_page_pool_refcount(const mtn_page_pool* pool, uint32_t page);
+
+/* ------------------------------------------------------------------------ */
+/* Host mirror: radix prefix cache (radix_cache.rs:37-303)                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct mtn_radix mtn_radix;
+
+MTN_API int mtn_radix_create(int32_t page_size, int64_t max_pages, mtn_radix** out);
+MTN_API void mtn_radix_destroy(mtn_radix* r);
+/* match_prefix (radix_cache.rs:64-117).  Writes up to *n_pages page ids and
+ * *n_nodes node ids (capacities in, counts out; MTN_EINVAL if too small). */
+MTN_API int mtn_radix_match_prefix(mtn_radix* r, const uint32_t* tokens, int64_t n_tokens,
+                           int64_t* matched_len, uint32_t* pages, int64_t* n_pages,
+                           uint64_t* nodes, int64_t* n_nodes);
+/* insert_prefix (radix_cache.rs:123-187).  Pages evicted to make room are
+ * reported in evicted (capacity/count in *n_evicted; may be NULL to drop
+ * them, as the reference does at radix_cache.rs:133). */
+MTN_API int mtn_radix_insert_prefix(mtn_radix* r, const uint32_t* tokens, int64_t n_tokens,
+                            const uint32_t* pages, int64_t n_pages,
+                            uint32_t* evicted, int64_t* n_evicted);
+MTN_API int mtn_radix_unlock_nodes(mtn_radix* r, const uint64_t* nodes, int64_t n_nodes);
+/* evict_pages (radix_cache.rs:243-282): frees LRU unlocked leaves until
+ * target pages are collected or nothing is evictable. */
+MTN_API int mtn_radix_evict_pages(mtn_radix* r, int64_t target, uint32_t* freed, int64_t* n_freed);
+/* promote_request (radix_cache.rs:287-294). */
+MTN_API int mtn_radix_promote(mtn_radix* r, const uint32_t* input_ids, int64_t n_input,
+                      int64_t device_len, const uint32_t* kv_pages, int64_t n_kv_pages);
+MTN_API int64_t mtn_radix_total_cached_pages(const mtn_radix* r);
+MTN_API int64_t mtn_radix_num_nodes(const mtn_radix* r);
+
+/* ------------------------------------------------------------------------ */
+/* Host mirror: scheduler (prefill.rs, decode.rs, scheduler.rs)             */
+/* ------------------------------------------------------------------------ */
+
+typedef struct mtn_sched mtn_sched;
+
+enum {
+  /* Exactly the reference's page lifecycle: a finished request frees every
+   * page it lists, radix-shared ones included (scheduler.rs:164-172). */
+  MTN_SCHED_REFERENCE = 0,
+  /* Refcounted pages: radix-shared pages stay alive while the tree holds
+   * them; decode grows a request by one page when its last page fills;
+   * a partially filled shared page is copied before the first append. */
+  MTN_SCHED_REFCOUNT = 1
+};
+
+typedef struct {
+  int64_t num_pages;
+  int32_t page_size;
+  int32_t max_prefill_tokens_per_iter;  /* EngineConfig, config.rs:3-16 */
+  int32_t max_decode_batch_size;
+  int64_t radix_max_pages;
+  int32_t mode;                         /* MTN_SCHED_REFERENCE / _REFCOUNT */
+  int32_t n_eos;
+  const uint32_t* eos_token_ids;        /* ModelConfig::eos_token_ids     */
+} mtn_sched_config;
+
+enum {
+  MTN_REQ_WAITING = 0,
+  MTN_REQ_PREFILLING = 1,
+  MTN_REQ_DECODING = 2,
+  MTN_REQ_DONE = 3,
+  MTN_REQ_ABORTED = 4
+};
+
+enum { MTN_PHASE_PREFILL_ONLY = 0, MTN_PHASE_DECODE_ONLY = 1, MTN_PHASE_MIXED = 2 };
+
+/* A scheduled batch (Batch, batch.rs:7-36) in CSR form.  Arrays are owned
+ * by the scheduler and valid until its next schedule call. */
+typedef struct {
+  int32_t phase;
+  int32_t n_reqs;              /* prefill rows first, then decode rows     */
+  int32_t n_prefill;
+  int64_t n_tokens;
+  const uint64_t* req_ids;     /* [n_reqs]                                 */
+  const uint32_t* input_ids;   /* [n_tokens]                               */
+  const int32_t* position_ids; /* [n_tokens]                               */
+  const int32_t* qo_indptr;    /* [n_reqs+1] token ranges                  */
+  const int32_t* kv_indptr;    /* [n_reqs+1] page ranges (page_table CSR)  */
+  const int32_t* kv_indices;   /* [kv_indptr[n_reqs]]                      */
+  const int32_t* seq_lens;     /* [n_reqs] KV tokens after this step       */
+  int64_t n_cow;               /* copy-on-write page pairs to run first   */
+  const int32_t* cow_src;
+  const int32_t* cow_dst;
+} mtn_batch_view;
+
+MTN_API int mtn_sched_create(const mtn_sched_config* cfg, mtn_sched** out);
+MTN_API void mtn_sched_destroy(mtn_sched* s);
+/* Queue a request (Request::new, request.rs:85-101; engine_loop.rs:36-39).
+ * temperature <= 0 selects greedy sampling (scheduler.rs:186-199). */
+MTN_API int mtn_sched_add_request(mtn_sched* s, uint64_t req_id, const uint32_t* input_ids, int64_t n_input,
+                          float temperature, int32_t max_new_tokens);
+/* schedule_batch (scheduler.rs:8-27).  *has_batch = 0 when nothing runs. */
+MTN_API int mtn_sched_schedule(mtn_sched* s, mtn_batch_view* out, int32_t* has_batch);
+/* process_and_transition (scheduler.rs:79-184) with host logits, one row
+ * per batch request: [n_rows][vocab] f32. */
+MTN_API int mtn_sched_process_logits(mtn_sched* s, const float* logits, int64_t n_rows, int64_t vocab);
+/* Same transition with tokens already sampled on the device. */
+MTN_API int mtn_sched_process_tokens(mtn_sched* s, const uint32_t* tokens, int64_t n_rows);
+/* Abort every request of the last batch (engine_loop.rs:47-57). */
+MTN_API int mtn_sched_abort_batch(mtn_sched* s);
+MTN_API int mtn_sched_request_info(const mtn_sched* s, uint64_t req_id, int32_t* state,
+                           int64_t* device_len, int64_t* cached_len, int64_t* n_pages,
+                           int64_t* n_output);
+MTN_API int mtn_sched_request_pages(const mtn_sched* s, uint64_t req_id, uint32_t* pages, int64_t* n_pages);
+MTN_API int mtn_sched_request_output(const mtn_sched* s, uint64_t req_id, uint32_t* out, int64_t* n_out);
+MTN_API int64_t mtn_sched_free_pages(const mtn_sched* s);
+MTN_API int64_t mtn_sched_cached_pages(const mtn_sched* s);
+MTN_API int32_t mtn_sched_num_active(const mtn_sched* s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MITTEN_KV_H */

@@ -1,0 +1,363 @@
+// Data-movement kernels of the paged-KV path:
+//   - slot mapping  (Batch CSR -> per-token pool slot, batch.rs:7-36)
+//   - KV append     (paged replacement of Tensor::cat, qwen model.rs:390-392)
+//   - page copy     (copy-on-write / prefix fork; no reference counterpart)
+//   - gather        (pages -> KVCacheState::Attention layout, model-common lib.rs:5-13)
+//   - row argmax    (greedy sample_token, scheduler.rs:186-199)
+// All are HBM-bound byte movers: 16-byte vector accesses, several loads in
+// flight per thread before the matching stores, grids sized in multiples of
+// the SM count.
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace mtn {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+int grid_for(int64_t work_items, int64_t items_per_block) {
+  const int sms = sm_count();
+  int64_t blocks = (work_items + items_per_block - 1) / items_per_block;
+  const int64_t cap = static_cast<int64_t>(sms) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+// Largest r in [0, n) with offs[r] <= t (offs non-decreasing, offs[0] <= t).
+__device__ __forceinline__ int upper_index(const int32_t* offs, int n, int64_t t) {
+  int lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (offs[mid] <= t) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ int upper_index64(const int64_t* offs, int n, int64_t t) {
+  int lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (offs[mid] <= t) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void slot_mapping_kernel(const int32_t* __restrict__ qo_indptr, const int32_t* __restrict__ positions,
+                                    const int32_t* __restrict__ kv_indptr, const int32_t* __restrict__ kv_indices,
+                                    int n_seqs, int64_t n_tokens, int page_size, int64_t* __restrict__ slots,
+                                    int* err) {
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n_tokens;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = upper_index(qo_indptr, n_seqs, t);
+    const int pos = positions[t];
+    const int pidx = pos >= 0 ? pos / page_size : -1;
+    const int np = kv_indptr[r + 1] - kv_indptr[r];
+    if (pos < 0 || pidx >= np) {
+      slots[t] = -1;
+      record_error(err, kDevErrBadPosition, static_cast<int>(t));
+    } else {
+      slots[t] = static_cast<int64_t>(kv_indices[kv_indptr[r] + pidx]) * page_size + (pos % page_size);
+    }
+  }
+}
+
+// One work item = 16 output bytes (8 bf16) of one (token, kv head) row of K
+// and the same chunk of V.
+template <typename SrcT>
+__device__ __forceinline__ uint4 load_chunk(const SrcT* p);
+
+template <>
+__device__ __forceinline__ uint4 load_chunk<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+
+template <>
+__device__ __forceinline__ uint4 load_chunk<float>(const float* p) {
+  const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+  uint4 r;
+  r.x = f2_to_bf2(a.x, a.y);
+  r.y = f2_to_bf2(a.z, a.w);
+  r.z = f2_to_bf2(b.x, b.y);
+  r.w = f2_to_bf2(b.z, b.w);
+  return r;
+}
+
+template <typename SrcT>
+__global__ void __launch_bounds__(kThreads) kv_append_kernel(
+    __nv_bfloat16* __restrict__ kdst, __nv_bfloat16* __restrict__ vdst, int64_t num_pages, int hkv, int ps,
+    int d, const SrcT* __restrict__ k, const SrcT* __restrict__ v, int64_t src_stride,
+    const int64_t* __restrict__ slots, int64_t n_tokens, int* err) {
+  const int chunks = d >> 3;
+  const int64_t per_tok = static_cast<int64_t>(hkv) * chunks;
+  const int64_t total = n_tokens * per_tok;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * kUnroll) {
+    uint4 kv[kUnroll], vv[kUnroll];
+    int64_t dst[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      dst[u] = -1;
+      if (i < total) {
+        const int64_t t = i / per_tok;
+        const int rem = static_cast<int>(i - t * per_tok);
+        const int h = rem / chunks;
+        const int c = rem - h * chunks;
+        const int64_t slot = slots[t];
+        if (slot >= 0) {
+          const int64_t page = slot / ps;
+          const int off = static_cast<int>(slot - page * ps);
+          if (page < num_pages) {
+            const int64_t so = t * src_stride + static_cast<int64_t>(h) * d + c * 8;
+            kv[u] = load_chunk<SrcT>(k + so);
+            vv[u] = load_chunk<SrcT>(v + so);
+            dst[u] = ((page * hkv + h) * ps + off) * static_cast<int64_t>(d) + c * 8;
+          } else {
+            record_error(err, kDevErrBadSlot, static_cast<int>(t));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (dst[u] >= 0) {
+        *reinterpret_cast<uint4*>(kdst + dst[u]) = kv[u];
+        *reinterpret_cast<uint4*>(vdst + dst[u]) = vv[u];
+      }
+    }
+  }
+}
+
+// One work item = 16 bytes of one (pair, layer, K|V) page block.
+__global__ void __launch_bounds__(kThreads) page_copy_kernel(__nv_bfloat16* __restrict__ pool, int64_t num_pages,
+                                                             int num_layers, int64_t page_vecs,
+                                                             const int32_t* __restrict__ src,
+                                                             const int32_t* __restrict__ dst, int64_t n_pairs,
+                                                             int* err) {
+  uint4* p4 = reinterpret_cast<uint4*>(pool);
+  const int64_t units = n_pairs * num_layers * 2;
+  const int64_t total = units * page_vecs;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * kUnroll) {
+    uint4 val[kUnroll];
+    int64_t to[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      to[u] = -1;
+      if (i < total) {
+        const int64_t unit = i / page_vecs;
+        const int64_t w = i - unit * page_vecs;
+        const int64_t pair = unit / (num_layers * 2);
+        const int64_t lk = unit - pair * (num_layers * 2);  // layer * 2 + kv
+        const int64_t s = src[pair], t = dst[pair];
+        if (s < 0 || s >= num_pages || t < 0 || t >= num_pages) {
+          record_error(err, kDevErrBadPage, static_cast<int>(pair));
+        } else if (s != t) {
+          val[u] = p4[(lk * num_pages + s) * page_vecs + w];
+          to[u] = (lk * num_pages + t) * page_vecs + w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (to[u] >= 0) p4[to[u]] = val[u];
+    }
+  }
+}
+
+// One work item = 16 bytes (8 elements) of one (token, kv head) row.
+__global__ void __launch_bounds__(kThreads) gather_kernel(
+    const __nv_bfloat16* __restrict__ kpool, const __nv_bfloat16* __restrict__ vpool, int64_t num_pages, int hkv,
+    int ps, int d, const int32_t* __restrict__ kv_indptr, const int32_t* __restrict__ kv_indices,
+    const int32_t* __restrict__ seq_lens, const int64_t* __restrict__ out_offsets, int n_seqs,
+    __nv_bfloat16* __restrict__ out_k, __nv_bfloat16* __restrict__ out_v, int64_t total_tokens, int* err) {
+  const int chunks = d >> 3;
+  const int64_t per_tok = static_cast<int64_t>(hkv) * chunks;
+  const int64_t total = total_tokens * per_tok;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / per_tok;
+    const int rem = static_cast<int>(i - t * per_tok);
+    const int h = rem / chunks;
+    const int c = rem - h * chunks;
+    const int r = upper_index64(out_offsets, n_seqs, t);
+    const int64_t j = t - out_offsets[r];
+    const int len = seq_lens[r];
+    if (j >= len) continue;
+    const int pidx = static_cast<int>(j / ps);
+    if (pidx >= kv_indptr[r + 1] - kv_indptr[r]) {
+      record_error(err, kDevErrBadSeqLen, r);
+      continue;
+    }
+    const int64_t page = kv_indices[kv_indptr[r] + pidx];
+    if (page < 0 || page >= num_pages) {
+      record_error(err, kDevErrBadPage, r);
+      continue;
+    }
+    const int64_t src = ((page * hkv + h) * ps + (j - static_cast<int64_t>(pidx) * ps)) * d + c * 8;
+    const int64_t dst = (out_offsets[r] * hkv + static_cast<int64_t>(h) * len + j) * d + c * 8;
+    *reinterpret_cast<uint4*>(out_k + dst) = *reinterpret_cast<const uint4*>(kpool + src);
+    *reinterpret_cast<uint4*>(out_v + dst) = *reinterpret_cast<const uint4*>(vpool + src);
+  }
+}
+
+// First strict maximum of each row, NaN never wins (scheduler.rs:188-199:
+// `if val > max_val` starting from -inf at index 0).
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int64_t vocab,
+                                                      int32_t* __restrict__ out) {
+  const float* row = logits + blockIdx.x * vocab;
+  float best = -INFINITY;
+  int64_t idx = INT64_MAX;
+  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float x = row[i];
+    if (x > best) { best = x; idx = i; }
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    idx = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    if (lane == 0) out[blockIdx.x] = (best == -INFINITY || idx == INT64_MAX) ? 0 : static_cast<int32_t>(idx);
+  }
+}
+
+int check_layout(const mtn_kv_layout* pool, int layer, const char* who) {
+  MTN_CHECK_ARG(pool != nullptr && pool->base != nullptr, "%s: null pool", who);
+  MTN_CHECK_ARG(pool->num_pages > 0 && pool->num_layers > 0 && pool->page_size > 0 && pool->num_kv_heads > 0,
+                "%s: non-positive pool dimension", who);
+  MTN_CHECK_ARG(pool->head_dim == 64 || pool->head_dim == 128 || pool->head_dim == 256,
+                "%s: head_dim %d not in {64,128,256}", who, pool->head_dim);
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(pool->base) & 255) == 0, "%s: pool base not 256-byte aligned", who);
+  MTN_CHECK_ARG(layer >= 0 && layer < pool->num_layers, "%s: layer %d outside [0,%d)", who, layer, pool->num_layers);
+  return MTN_OK;
+}
+
+}  // namespace
+
+int validate_layout(const mtn_kv_layout* pool, int layer, const char* who) { return check_layout(pool, layer, who); }
+
+}  // namespace mtn
+
+using mtn::set_error;
+
+extern "C" {
+
+int mtn_build_slot_mapping(const int32_t* qo_indptr, const int32_t* positions, const int32_t* kv_indptr,
+                           const int32_t* kv_indices, int32_t n_seqs, int64_t n_tokens, int32_t page_size,
+                           int64_t* slots, void* stream) {
+  MTN_CHECK_ARG(n_seqs >= 0 && n_tokens >= 0 && page_size > 0, "mtn_build_slot_mapping: bad sizes");
+  if (n_tokens == 0) return MTN_OK;
+  MTN_CHECK_ARG(n_seqs > 0, "mtn_build_slot_mapping: tokens without sequences");
+  MTN_CHECK_ARG(qo_indptr && positions && kv_indptr && kv_indices && slots, "mtn_build_slot_mapping: null pointer");
+  const int grid = mtn::grid_for(n_tokens, mtn::kThreads);
+  mtn::slot_mapping_kernel<<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      qo_indptr, positions, kv_indptr, kv_indices, n_seqs, n_tokens, page_size, slots, mtn::device_error_ptr());
+  return mtn::check_launch("slot_mapping_kernel");
+}
+
+int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer, const void* k, const void* v, int32_t src_dtype,
+                  int64_t src_stride, const int64_t* slots, int64_t n_tokens, void* stream) {
+  int st = mtn::check_layout(pool, layer, "mtn_kv_append");
+  if (st != MTN_OK) return st;
+  MTN_CHECK_ARG(n_tokens >= 0, "mtn_kv_append: n_tokens < 0");
+  if (n_tokens == 0) return MTN_OK;
+  MTN_CHECK_ARG(k && v && slots, "mtn_kv_append: null pointer");
+  const int64_t row = static_cast<int64_t>(pool->num_kv_heads) * pool->head_dim;
+  MTN_CHECK_ARG(src_stride >= row, "mtn_kv_append: src_stride %lld < heads*dim %lld", (long long)src_stride,
+                (long long)row);
+  MTN_CHECK_ARG(src_dtype == MTN_DTYPE_BF16 || src_dtype == MTN_DTYPE_F32, "mtn_kv_append: bad src dtype");
+  const int esz = src_dtype == MTN_DTYPE_BF16 ? 2 : 4;
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(k) % 16) == 0 && (reinterpret_cast<uintptr_t>(v) % 16) == 0 &&
+                    (src_stride * esz) % 16 == 0,
+                "mtn_kv_append: k/v rows must be 16-byte aligned");
+  const int64_t page_elems = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * pool->head_dim;
+  auto* base = static_cast<__nv_bfloat16*>(pool->base);
+  __nv_bfloat16* kd = base + (static_cast<int64_t>(layer) * 2 + 0) * pool->num_pages * page_elems;
+  __nv_bfloat16* vd = base + (static_cast<int64_t>(layer) * 2 + 1) * pool->num_pages * page_elems;
+  const int64_t work = n_tokens * pool->num_kv_heads * (pool->head_dim / 8);
+  const int grid = mtn::grid_for(work, mtn::kThreads * mtn::kUnroll);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (src_dtype == MTN_DTYPE_BF16) {
+    mtn::kv_append_kernel<__nv_bfloat16><<<grid, mtn::kThreads, 0, s>>>(
+        kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim,
+        static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), src_stride, slots, n_tokens,
+        mtn::device_error_ptr());
+  } else {
+    mtn::kv_append_kernel<float><<<grid, mtn::kThreads, 0, s>>>(
+        kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, static_cast<const float*>(k),
+        static_cast<const float*>(v), src_stride, slots, n_tokens, mtn::device_error_ptr());
+  }
+  return mtn::check_launch("kv_append_kernel");
+}
+
+int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages, const int32_t* dst_pages, int64_t n_pages,
+                  void* stream) {
+  int st = mtn::check_layout(pool, 0, "mtn_page_copy");
+  if (st != MTN_OK) return st;
+  MTN_CHECK_ARG(n_pages >= 0, "mtn_page_copy: n_pages < 0");
+  if (n_pages == 0) return MTN_OK;
+  MTN_CHECK_ARG(src_pages && dst_pages, "mtn_page_copy: null pointer");
+  const int64_t page_vecs = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * pool->head_dim / 8;
+  const int64_t work = n_pages * pool->num_layers * 2 * page_vecs;
+  const int grid = mtn::grid_for(work, mtn::kThreads * mtn::kUnroll);
+  mtn::page_copy_kernel<<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
+      n_pages, mtn::device_error_ptr());
+  return mtn::check_launch("page_copy_kernel");
+}
+
+int mtn_kv_gather(const mtn_kv_layout* pool, int32_t layer, const int32_t* kv_indptr, const int32_t* kv_indices,
+                  const int32_t* seq_lens, const int64_t* out_offsets, int32_t n_seqs, void* out_k, void* out_v,
+                  int64_t total_tokens, void* stream) {
+  int st = mtn::check_layout(pool, layer, "mtn_kv_gather");
+  if (st != MTN_OK) return st;
+  MTN_CHECK_ARG(n_seqs >= 0 && total_tokens >= 0, "mtn_kv_gather: bad sizes");
+  if (total_tokens == 0 || n_seqs == 0) return MTN_OK;
+  MTN_CHECK_ARG(kv_indptr && kv_indices && seq_lens && out_offsets && out_k && out_v, "mtn_kv_gather: null pointer");
+  const int64_t page_elems = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * pool->head_dim;
+  auto* base = static_cast<const __nv_bfloat16*>(pool->base);
+  const __nv_bfloat16* kp = base + (static_cast<int64_t>(layer) * 2 + 0) * pool->num_pages * page_elems;
+  const __nv_bfloat16* vp = base + (static_cast<int64_t>(layer) * 2 + 1) * pool->num_pages * page_elems;
+  const int64_t work = total_tokens * pool->num_kv_heads * (pool->head_dim / 8);
+  const int grid = mtn::grid_for(work, mtn::kThreads);
+  mtn::gather_kernel<<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      kp, vp, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kv_indptr, kv_indices, seq_lens,
+      out_offsets, n_seqs, static_cast<__nv_bfloat16*>(out_k), static_cast<__nv_bfloat16*>(out_v), total_tokens,
+      mtn::device_error_ptr());
+  return mtn::check_launch("gather_kernel");
+}
+
+int mtn_argmax_rows(const float* logits, int64_t n_rows, int64_t vocab, int32_t* out, void* stream) {
+  MTN_CHECK_ARG(n_rows >= 0 && vocab > 0 && vocab <= INT32_MAX, "mtn_argmax_rows: bad sizes");
+  if (n_rows == 0) return MTN_OK;
+  MTN_CHECK_ARG(logits && out, "mtn_argmax_rows: null pointer");
+  MTN_CHECK_ARG(n_rows <= INT32_MAX, "mtn_argmax_rows: too many rows");
+  mtn::argmax_kernel<<<static_cast<unsigned>(n_rows), 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, vocab,
+                                                                                                    out);
+  return mtn::check_launch("argmax_kernel");
+}
+
+}  // extern "C"
