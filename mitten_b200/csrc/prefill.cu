@@ -1,5 +1,353 @@
-// Chunked-prefill attention over paged KV (tcgen05 / TMEM) -- in progress.
+// Chunked-prefill attention over paged KV on the sm_100a tensor cores.
+//
+// Replaces the prefill-chunk attention of qwen model.rs:394-416 for a chunk
+// of q_len new tokens appended after P cached ones: scores q.k * scale
+// (model.rs:298, 413), causal mask -1e10 for keys after the query
+// (generate_causal_mask, model.rs:542-555), softmax over every key plus the
+// optional all-zero first row (model.rs:207-220), output P.V (model.rs:416),
+// q head h reading kv head h / n_rep (model.rs:398-408).
+//
+// CTA = (128-row query tile, query head, sequence); 6 warps in 3 roles:
+//   warps 0-3  softmax: one TMEM lane (= one query row) per thread; online
+//              softmax in the exp2 domain, rescale of the TMEM O accumulator,
+//              bf16 P written to shared memory in the 128B-swizzled K-major
+//              layout, final normalisation and store.
+//   warp 4     TMA producer: Q tile once, then K and V pages of each KV tile
+//              (one 2-D box per page per 64-wide head-dim block) into a
+//              2-stage ring; pages come straight from the block table.
+//   warp 5     MMA issuer (one thread): S = Q K^T and O += P V with
+//              tcgen05.mma (M=128, kind::f16, f32 accumulators in TMEM),
+//              completion signalled with tcgen05.commit on mbarriers.
+// Every wait is bounded (~1 s); a timeout records kDevErrTimeout, releases
+// the other roles, frees TMEM and returns.
+#include <mutex>
+
 #include "common.cuh"
+#include "tc.cuh"
+
+namespace mtn {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kBM = 128;   // query rows per CTA (TMEM lanes)
+constexpr int kThreads = 192;
+
+struct PrefillParams {
+  const int32_t* qo_indptr;
+  const int32_t* kv_indptr;
+  const int32_t* kv_indices;
+  const int32_t* seq_lens;
+  void* o;
+  int o_f32;
+  int hq;
+  int hkv;
+  int ps;
+  int64_t num_pages;
+  int64_t row_k;  // row (of the pool's [rows, head_dim] view) of layer K, page 0, head 0, token 0
+  int64_t row_v;
+  float qscale;
+  int phantom;
+  int* err;
+};
+
+template <int D>
+struct PCfg {
+  static constexpr int kBN = D <= 128 ? 128 : 64;       // kv tokens per tile
+  static constexpr int kDB = D / 64;                    // 64-wide head-dim blocks
+  static constexpr int kQBytes = kBM * D * 2;
+  static constexpr int kKVBytes = kBN * D * 2;          // one of K or V per stage
+  static constexpr int kPBytes = kBM * kBN * 2;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;         // [2][kKVBytes]
+  static constexpr int kOffV = kOffK + 2 * kKVBytes;
+  static constexpr int kOffP = kOffV + 2 * kKVBytes;
+  static constexpr int kOffBar = kOffP + kPBytes;       // 10 mbarriers
+  static constexpr int kOffMisc = kOffBar + 16 * 8;     // tmem base, abort flag
+  static constexpr int kSmem = kOffMisc + 64 + 1024;    // + slack for 1024-byte alignment
+  static constexpr int kTmemS = 0;
+  static constexpr int kTmemO = kBN;
+  static constexpr int kTmemCols = (kBN + D) <= 256 ? 256 : 512;
+  static_assert(kBN + D <= kTmemCols, "TMEM budget");
+};
+
+enum Bar { kQFull = 0, kKVFull0 = 1, kKVFull1 = 2, kKVEmpty0 = 3, kKVEmpty1 = 4, kSFull = 5, kPFull = 6, kODone = 7 };
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
+                         const __grid_constant__ PrefillParams p) {
+  using C = PCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int q0 = p.qo_indptr[s];
+  const int q_len = p.qo_indptr[s + 1] - q0;
+  if (tile * kBM >= q_len) return;
+  const int kv_beg = p.kv_indptr[s];
+  const int npages = p.kv_indptr[s + 1] - kv_beg;
+  int kv_len = p.seq_lens[s];
+  if (kv_len < q_len || kv_len > npages * p.ps) {
+    if (tile == 0 && h == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
+    kv_len = max(q_len, min(kv_len, npages * p.ps));
+    if (kv_len > npages * p.ps) return;  // not even the chunk fits its pages
+  }
+  const int nrows = min(kBM, q_len - tile * kBM);
+  const int pos0 = kv_len - q_len + tile * kBM;  // position of row 0
+  const int last_pos = pos0 + nrows - 1;
+  const int n_tiles = last_pos / C::kBN + 1;
+  const int g = h / (p.hq / p.hkv);
+  const int pages_per_tile = C::kBN / p.ps;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == kPFull ? kBM : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_q);
+      tc::prefetch_tmap(&tm_kv);
+      mbar_arrive_expect_tx(&bars[kQFull], C::kQBytes);
+      for (int b = 0; b < C::kDB; ++b)
+        tc::tma_load_3d(smem + C::kOffQ + b * kBM * 128, &tm_q, b * 64, h, q0 + tile * kBM, &bars[kQFull]);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !tc::wait_bounded(&bars[kKVEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 10)) break;
+        mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
+        uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
+        uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
+        for (int pi = 0; pi < pages_per_tile; ++pi) {
+          int pidx = min(j * pages_per_tile + pi, npages - 1);  // past the end: any valid page, masked later
+          int64_t page = p.kv_indices[kv_beg + pidx];
+          if (page < 0 || page >= p.num_pages) {
+            record_error(p.err, kDevErrBadPage, s);
+            page = 0;
+          }
+          const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
+          const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
+          for (int b = 0; b < C::kDB; ++b) {
+            const int off = b * C::kBN * 128 + pi * p.ps * 128;
+            tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
+            tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = tc::idesc_bf16(kBM, C::kBN, false);
+      constexpr uint32_t idO = tc::idesc_bf16(kBM, D, true);
+      const uint32_t q_s = smem_u32(smem + C::kOffQ);
+      const uint32_t p_s = smem_u32(smem + C::kOffP);
+      bool ok = tc::wait_bounded(&bars[kQFull], 0, abort_flag, p.err, 20);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j >> 1) & 1, abort_flag, p.err, 21)) break;
+        tc::fence_after_sync();
+        const uint32_t k_s = smem_u32(smem + C::kOffK + st * C::kKVBytes);
+        const uint32_t v_s = smem_u32(smem + C::kOffV + st * C::kKVBytes);
+        // S = Q K^T: K-major A and B; 16-wide k steps walk 32 bytes inside a
+        // 128-byte swizzle row, then the next 64-wide head-dim block.
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t koff = (k >> 2) * 0 + (k & 3) * 32;
+          const uint64_t a = tc::sdesc_sw128(q_s + (k >> 2) * kBM * 128 + koff, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(k_s + (k >> 2) * C::kBN * 128 + koff, 16, 1024);
+          tc::mma_bf16(tmem + C::kTmemS, a, b, idS, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&bars[kSFull]);
+        if (!tc::wait_bounded(&bars[kPFull], j & 1, abort_flag, p.err, 22)) break;
+        tc::fence_after_sync();
+        // O += P V: P K-major (kv tokens contiguous), V MN-major (head dim
+        // contiguous): 16 kv rows = 2048 bytes per k step; 64-wide head-dim
+        // blocks kBN*128 bytes apart (LBO).
+#pragma unroll
+        for (int k = 0; k < C::kBN / 16; ++k) {
+          const uint64_t a = tc::sdesc_sw128(p_s + (k >> 2) * kBM * 128 + (k & 3) * 32, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(v_s + k * 16 * 128, C::kBN * 128, 1024);
+          tc::mma_bf16(tmem + C::kTmemO, a, b, idO, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&bars[kODone]);
+        tc::mma_commit(&bars[kKVEmpty0 + st]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int row = threadIdx.x;  // 0..127 == TMEM lane
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int row_pos = min(pos0 + row, last_pos);
+    float m_run = -INFINITY, l_run = 0.0f;
+    uint8_t* p_tile = smem + C::kOffP;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      ok = tc::wait_bounded(&bars[kSFull], j & 1, abort_flag, p.err, 30);
+      if (!ok) break;
+      tc::fence_after_sync();
+      float sv[C::kBN];
+#pragma unroll
+      for (int c = 0; c < C::kBN / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(lane_base + C::kTmemS + c * 32, r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int key0 = j * C::kBN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < C::kBN; ++c) {
+        sv[c] = (key0 + c <= row_pos) ? sv[c] * p.qscale : -INFINITY;
+        mt = fmaxf(mt, sv[c]);
+      }
+      const float mn = fmaxf(m_run, mt);  // finite: key 0 is visible to every row
+      const float alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - mn);
+      float psum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < C::kBN; ++c) {
+        sv[c] = exp2f(sv[c] - mn);
+        psum += sv[c];
+      }
+      l_run = l_run * alpha + psum;
+      m_run = mn;
+      if (j > 0) {
+        // O and the P buffer are busy until the previous P V finishes.
+        ok = tc::wait_bounded(&bars[kODone], (j - 1) & 1, abort_flag, p.err, 31);
+        if (!ok) break;
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tc::tmem_st32(lane_base + C::kTmemO + c * 32, r);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      // P (bf16) into the 128B-swizzled K-major tile: 64-key sub-tiles of
+      // 128 rows x 128 bytes; 16-byte chunk index XOR (row % 8).
+#pragma unroll
+      for (int c8 = 0; c8 < C::kBN / 8; ++c8) {
+        const int sub = c8 >> 3, chunk = c8 & 7;
+        uint4 w;
+        w.x = f2_to_bf2(sv[c8 * 8 + 0], sv[c8 * 8 + 1]);
+        w.y = f2_to_bf2(sv[c8 * 8 + 2], sv[c8 * 8 + 3]);
+        w.z = f2_to_bf2(sv[c8 * 8 + 4], sv[c8 * 8 + 5]);
+        w.w = f2_to_bf2(sv[c8 * 8 + 6], sv[c8 * 8 + 7]);
+        *reinterpret_cast<uint4*>(p_tile + sub * kBM * 128 + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+      }
+      fence_proxy_async_shared();
+      tc::fence_before_sync();
+      tc::mbar_arrive(&bars[kPFull]);
+    }
+    // ---- epilogue: O / l (phantom key folded in), one row per thread.
+    if (ok) ok = tc::wait_bounded(&bars[kODone], (n_tiles - 1) & 1, abort_flag, p.err, 32);
+    tc::fence_after_sync();
+    if (ok) {
+      float l = l_run, a = 1.0f;
+      if (p.phantom) {
+        const float mf = fmaxf(m_run, 0.0f);
+        a = exp2f(m_run - mf);
+        l = l * a + exp2f(-mf);
+      }
+      const float inv = l > 0.0f ? a / l : 0.0f;
+      const bool valid = row < nrows;
+      const int64_t orow = (static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
+        tc::tmem_ld_wait();
+        if (valid) {
+          if (p.o_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * D + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                   __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * D + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 w;
+              w.x = f2_to_bf2(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+              w.y = f2_to_bf2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+              w.z = f2_to_bf2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+              w.w = f2_to_bf2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+              dst[i] = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------- host side
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled get_encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(f);
+  });
+  return fn;
+}
+
+template <int D>
+int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
+                   cudaStream_t stream) {
+  using C = PCfg<D>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    MTN_CUDA_TRY(cudaFuncSetAttribute(paged_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem),
+                 "cudaFuncSetAttribute(prefill)");
+    configured[dev] = true;
+  }
+  dim3 grid(n_tiles, prm.hq, n_seqs);
+  paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tq, tkv, prm);
+  return check_launch("paged_prefill_kernel");
+}
+
+}  // namespace
+}  // namespace mtn
 
 using mtn::set_error;
 
@@ -8,14 +356,85 @@ extern "C" {
 size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads, int32_t num_kv_heads,
                                          int32_t head_dim) {
   (void)n_seqs; (void)total_q; (void)num_q_heads; (void)num_kv_heads; (void)head_dim;
-  return 0;
+  return 0;  // the prefill kernel keeps all state on chip
 }
 
 int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, void* o, int32_t o_dtype,
                       int32_t n_seqs, int64_t total_q, int32_t num_q_heads, const int32_t* qo_indptr,
                       const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens, int32_t max_q_len,
                       float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
-  return set_error(MTN_EINVAL, "mtn_paged_prefill: not built yet");
+  (void)workspace;
+  (void)workspace_bytes;
+  int st = mtn::validate_layout(pool, layer, "mtn_paged_prefill");
+  if (st != MTN_OK) return st;
+  MTN_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65535, "mtn_paged_prefill: n_seqs %d outside [0, 65535]", n_seqs);
+  MTN_CHECK_ARG(total_q >= 0 && total_q < (int64_t(1) << 31), "mtn_paged_prefill: bad total_q");
+  if (n_seqs == 0 || total_q == 0) return MTN_OK;
+  MTN_CHECK_ARG(q && o && qo_indptr && kv_indptr && kv_indices && seq_lens, "mtn_paged_prefill: null pointer");
+  MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_prefill: bad o dtype");
+  MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads <= 65535 && num_q_heads % pool->num_kv_heads == 0,
+                "mtn_paged_prefill: %d query heads not a multiple of %d kv heads", num_q_heads, pool->num_kv_heads);
+  MTN_CHECK_ARG(max_q_len > 0, "mtn_paged_prefill: max_q_len must be positive");
+  const int D = pool->head_dim;
+  const int bn = D <= 128 ? 128 : 64;
+  MTN_CHECK_ARG(pool->page_size <= bn && bn % pool->page_size == 0 && pool->page_size % 8 == 0,
+                "mtn_paged_prefill: page_size %d must be a multiple of 8 dividing %d", pool->page_size, bn);
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
+                "mtn_paged_prefill: q/o must be 16-byte aligned");
+  const int64_t rows = static_cast<int64_t>(pool->num_layers) * 2 * pool->num_pages * pool->num_kv_heads *
+                       pool->page_size;
+  MTN_CHECK_ARG(rows < (int64_t(1) << 31), "mtn_paged_prefill: pool has %lld rows; TMA coordinates need < 2^31",
+                (long long)rows);
+  auto enc = mtn::get_encoder();
+  if (enc == nullptr) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+
+  CUtensorMap tq, tkv;
+  {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(num_q_heads),
+                                static_cast<cuuint64_t>(total_q)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(num_q_heads) * D * 2};
+    const cuuint32_t box[3] = {64, 1, mtn::kBM};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled(q) failed: %d", (int)r);
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(pool->page_size)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pool->base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled(kv) failed: %d", (int)r);
+  }
+  mtn::PrefillParams prm{};
+  prm.qo_indptr = qo_indptr;
+  prm.kv_indptr = kv_indptr;
+  prm.kv_indices = kv_indices;
+  prm.seq_lens = seq_lens;
+  prm.o = o;
+  prm.o_f32 = o_dtype == MTN_DTYPE_F32;
+  prm.hq = num_q_heads;
+  prm.hkv = pool->num_kv_heads;
+  prm.ps = pool->page_size;
+  prm.num_pages = pool->num_pages;
+  const int64_t rows_per_block = pool->num_pages * pool->num_kv_heads * pool->page_size;
+  prm.row_k = (static_cast<int64_t>(layer) * 2 + 0) * rows_per_block;
+  prm.row_v = (static_cast<int64_t>(layer) * 2 + 1) * rows_per_block;
+  prm.qscale = scale * mtn::kLog2e;
+  prm.phantom = (flags & MTN_ATTN_PHANTOM_ZERO_SLOT) ? 1 : 0;
+  prm.err = mtn::device_error_ptr();
+  const int n_tiles = (max_q_len + mtn::kBM - 1) / mtn::kBM;
+  MTN_CHECK_ARG(n_tiles <= 65535 * 32, "mtn_paged_prefill: max_q_len too large");
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (D) {
+    case 64: return mtn::launch_prefill<64>(tq, tkv, prm, n_tiles, n_seqs, s);
+    case 128: return mtn::launch_prefill<128>(tq, tkv, prm, n_tiles, n_seqs, s);
+    default: return mtn::launch_prefill<256>(tq, tkv, prm, n_tiles, n_seqs, s);
+  }
 }
 
-}
+}  // extern "C"

@@ -1,0 +1,88 @@
+"""Chunked-prefill attention (tcgen05 / TMEM) on the GPU against the f32 oracle.
+
+Each case appends a chunk of q_len tokens after P cached tokens, then runs
+the prefill kernel over the paged cache.  Tolerances as for decode: 2e-2
+max-abs against the oracle fed unrounded f32 inputs (the spec's bar), and
+a tighter bound against the oracle fed the bf16 values the kernel reads
+(P is rounded to bf16 before the P.V product, hence 1e-2).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from mitten_b200 import paged
+from tests.paged_case import make_case
+
+pytestmark = pytest.mark.gpu
+
+TOL_SPEC = 2e-2
+TOL_KERNEL = 1e-2
+
+
+def run_prefill(kv_lens, q_lens, hq, hkv, d, phantom=True, seed=0, out_dtype=torch.float32, page_size=16):
+    case = make_case(kv_lens, hkv, d, page_size=page_size, seed=seed)
+    rng = np.random.default_rng(seed + 100)
+    total_q = sum(q_lens)
+    q = rng.standard_normal((total_q, hq, d)).astype(np.float32)
+    qt = torch.from_numpy(q).to("cuda").to(torch.bfloat16)
+    qo = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32), device="cuda")
+    out = paged.paged_prefill(case.pool, 0, qt, qo, case.kv_indptr, case.kv_indices, case.seq_lens,
+                              max(q_lens), phantom=phantom, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return case, q, qt.float().cpu().numpy(), out.float().cpu().numpy()
+
+
+def check(case, q_lens, q, q_used, out, d, phantom=True):
+    off = 0
+    e_spec = e_kernel = 0.0
+    for r, ql in enumerate(q_lens):
+        if ql == 0:
+            continue
+        k32, v32 = case.oracle_cache(r, layer_round=False, phantom=phantom)
+        want = oracle.attention(q[off:off + ql], k32, v32, d ** -0.5)
+        kb, vb = case.oracle_cache(r, layer_round=True, phantom=phantom)
+        want_b = oracle.attention(q_used[off:off + ql], kb, vb, d ** -0.5)
+        got = out[off:off + ql]
+        e_spec = max(e_spec, float(np.abs(got - want).max()))
+        e_kernel = max(e_kernel, float(np.abs(got - want_b).max()))
+        off += ql
+    assert e_spec <= TOL_SPEC, e_spec
+    assert e_kernel <= TOL_KERNEL, e_kernel
+    return e_spec, e_kernel
+
+
+def test_prefill_single_tile(cuda_device):
+    case, q, qu, out = run_prefill([128], [128], 14, 2, 64)
+    check(case, [128], q, qu, out, 64)
+    assert paged.device_error(0) == (0, 0)
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(14, 2, 64), (28, 4, 128), (8, 1, 256), (4, 4, 64)])
+def test_prefill_chunks_over_cached_prefix(cuda_device, hq, hkv, d):
+    # (kv_len, q_len): chunk after a cached prefix, ragged and multi-tile.
+    kv_lens = [200, 77, 512 + 300, 1, 640]
+    q_lens = [72, 77, 300, 1, 130]
+    case, q, qu, out = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=hq + d)
+    check(case, q_lens, q, qu, out, d)
+    assert paged.device_error(0) == (0, 0)
+
+
+def test_prefill_without_phantom_bf16_out(cuda_device):
+    kv_lens, q_lens = [300, 129], [300, 2]
+    case, q, qu, out = run_prefill(kv_lens, q_lens, 14, 2, 64, phantom=False, out_dtype=torch.bfloat16, seed=5)
+    check(case, q_lens, q, qu, out, 64, phantom=False)
+
+
+def test_prefill_page_size_32(cuda_device):
+    kv_lens, q_lens = [100, 257], [40, 257]
+    case, q, qu, out = run_prefill(kv_lens, q_lens, 14, 2, 64, page_size=32, seed=9)
+    check(case, q_lens, q, qu, out, 64)
+
+
+def test_prefill_empty_chunk_rows(cuda_device):
+    kv_lens, q_lens = [10, 50, 20], [0, 50, 0]
+    case, q, qu, out = run_prefill(kv_lens, q_lens, 14, 2, 64, seed=3)
+    check(case, q_lens, q, qu, out, 64)
