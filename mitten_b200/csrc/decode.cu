@@ -4,41 +4,46 @@
 // mapping h -> h / n_rep (model.rs:398-408), scores q.k * scale
 // (model.rs:298, 413), softmax over every key including the reference's
 // all-zero first row (model.rs:207-220, flag MTN_ATTN_PHANTOM_ZERO_SLOT),
-// output P.V (model.rs:416).  No causal mask is needed for one query token:
-// generate_causal_mask (model.rs:542-555) masks nothing on the last row.
+// output P.V (model.rs:416).  One query token sees every key, so
+// generate_causal_mask (model.rs:542-555) masks nothing here.
 //
-// Design (HBM-bound, CUDA cores):
-//   - grid = (split, kv head, sequence).  A CTA owns `pages_per_split`
-//     consecutive pages of one sequence for one KV head and all n_rep query
-//     heads that share it, so every K/V byte is read from HBM once.
-//   - Pages are staged into shared memory by the TMA engine with 1-D bulk
-//     copies (cp.async.bulk, one per page per K/V: the pool keeps each
-//     (page, kv head) slab contiguous), STAGES tiles in flight, completion
-//     tracked by mbarrier transaction counts.
-//   - QK: lane = token; the lane walks the head dim in 16-byte chunks
-//     starting at chunk (lane mod chunks) so the 8 lanes of a shared-memory
-//     phase hit 8 different bank groups; Q (pre-scaled by scale*log2 e) is
-//     read as a broadcast; packed f32x2 FMAs (FFMA2).
-//   - Online softmax per warp in the exp2 domain (warp-shuffle max), P is
-//     written once per tile to shared memory.
-//   - PV: lane = (16-byte dim chunk, token group); FFMA2 over bf16 V rows.
-//   - Fixed-order combine: warps of a CTA merge in warp order; splits of a
-//     sequence write (m, l, O) partials to the workspace and the last CTA
-//     to arrive (atomic ticket, no spinning) merges them in split order, so
-//     the result does not depend on CTA scheduling.
+// Design.  The step is HBM-bound (every K/V byte is read once) but at GQA
+// n_rep = 7 the arithmetic is 3.5 FMA per byte, more than the CUDA cores can
+// issue at HBM speed, so both contractions run on the tensor cores with the
+// n_rep query heads of one KV head as the narrow N dimension:
+//   S^T[128 tokens][16] = K_tile[128][D] . Q^T            (tcgen05, M=128, N=16)
+//   O^T[D][16]         += V_tile^T[D][128] . P^T[128][16] (tcgen05, M=D (64|128), N=16)
+// grid = (split, kv head, sequence); a CTA owns `pages_per_split` pages of
+// one sequence for one KV head.  6 warps:
+//   warps 0-3  softmax: TMEM lane = token; online softmax in the exp2 domain
+//              with a CTA-wide running max per query head, P^T (bf16) written
+//              to shared memory, O^T rescaled in TMEM, epilogue.
+//   warp 4     TMA producer: each page of each 128-token tile is one 2-D box
+//              (page_size rows x 64 columns, 128B swizzle) straight from the
+//              block table into a STAGES-deep ring.
+//   warp 5     MMA issuer (one thread), completion through tcgen05.commit.
+// Splits of one sequence write (m, l, O) partials to the workspace; the last
+// CTA to arrive (atomic ticket, no spinning) merges them in split order, so
+// the result does not depend on CTA scheduling.  Every wait is bounded.
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
+#include "tc.cuh"
+#include "tmaps.hpp"
 
 namespace mtn {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kTile = 128;    // tokens per tile = MMA1 M = TMEM lanes
+constexpr int kThreads = 192;
+constexpr int kN = 16;        // query heads per KV head, padded (MMA N)
 
 struct DecodeParams {
-  const __nv_bfloat16* kpool;  // K block of the layer: [num_pages][hkv][ps][D]
-  const __nv_bfloat16* vpool;  // V block of the layer
   int64_t num_pages;
+  int64_t row_k;  // pool-view row of (layer K, page 0, head 0, token 0)
+  int64_t row_v;
   int hkv;
   int ps;
   int hq;
@@ -53,32 +58,35 @@ struct DecodeParams {
   int max_splits;
   float qscale;  // scale * log2(e)
   int phantom;
-  float* ws_o;         // [n_seqs][hq][max_splits][D]
-  float* ws_ml;        // [n_seqs][hq][max_splits][2]
+  float* ws_o;           // [n_seqs][hq][max_splits][D]
+  float* ws_ml;          // [n_seqs][hq][max_splits][2]
   unsigned int* ws_cnt;  // [n_seqs][hkv]
   int* err;
 };
 
-template <int D, int NREP, int NWARPS, int TILE_TOK, int STAGES>
-struct DecodeCfg {
-  static constexpr int kThreads = NWARPS * 32;
-  static constexpr int kChunks = D / 8;             // 16-byte chunks per row
-  static constexpr int kTokPerWarp = TILE_TOK / NWARPS;
-  static constexpr int kTT = kTokPerWarp / 32;       // tokens per lane in QK
-  static constexpr int kTG = 32 / kChunks > 0 ? 32 / kChunks : 1;  // token groups in PV
-  static constexpr int kNrep2 = (NREP + 1) & ~1;
-  static constexpr int kStageBytes = TILE_TOK * D * 2;  // one of K or V
-  static constexpr int kOffQ = STAGES * 2 * kStageBytes;
-  static constexpr int kOffP = kOffQ + NREP * D * 4;
-  static constexpr int kOffBar = (kOffP + NWARPS * kTokPerWarp * kNrep2 * 8 + 15) & ~15;
-  static constexpr int kOffFlag = kOffBar + STAGES * 8;
-  static constexpr int kSmem = kOffFlag + 16;
-  // Cross-warp combine buffers alias the stage area after the main loop.
-  static constexpr int kCombBytes = NWARPS * NREP * (D + 2) * 4;
-  static_assert(kCombBytes <= STAGES * 2 * kStageBytes, "combine buffer must fit in the stage area");
-  static_assert(kTokPerWarp % 32 == 0, "tile must give each lane whole tokens");
-  static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
+template <int D>
+struct DCfg {
+  static constexpr int kDB = D / 64;                       // 64-wide head-dim blocks
+  static constexpr int kStages = D == 256 ? 1 : 2;
+  static constexpr int kQBytes = kN * D * 2;               // Q^T operand: 16 rows x D
+  static constexpr int kKVBytes = kTile * D * 2;           // one of K or V per stage
+  static constexpr int kPBytes = kN * kTile * 2;           // P^T operand: 16 rows x 128 tokens
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffV = kOffK + kStages * kKVBytes;
+  static constexpr int kOffP = kOffV + kStages * kKVBytes;
+  static constexpr int kOffRed = kOffP + kPBytes;          // [2][4][16] maxima, [4][16] sums
+  static constexpr int kOffBar = kOffRed + (2 * 4 * kN + 4 * kN) * 4;
+  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort flag, last-CTA flag
+  static constexpr int kSmem = kOffMisc + 64 + 1024;       // + slack for 1024-byte alignment
+  static constexpr int kMO = D == 64 ? 64 : 128;           // MMA2 M
+  static constexpr int kTmemS = 0;                          // 16 columns
+  static constexpr int kTmemO = 16;                         // 16 (D <= 128) or 32 (D = 256) columns
+  static constexpr int kTmemCols = 64;
+  static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KiB alignment");
 };
+
+enum Bar { kKVFull0 = 0, kKVFull1 = 1, kKVEmpty0 = 2, kKVEmpty1 = 3, kSFull = 4, kPFull = 5, kODone = 6 };
 
 // Final normalisation of one output element: o/l with the phantom key folded in.
 __device__ __forceinline__ float finalize(float o, float l, float m, int phantom) {
@@ -91,21 +99,47 @@ __device__ __forceinline__ float finalize(float o, float l, float m, int phantom
   return l > 0.0f ? o / l : 0.0f;
 }
 
-template <int D, int NREP, int NWARPS, int TILE_TOK, int STAGES>
-__global__ void __launch_bounds__(NWARPS * 32)
-    paged_decode_kernel(const __grid_constant__ DecodeParams p) {
-  using C = DecodeCfg<D, NREP, NWARPS, TILE_TOK, STAGES>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  float4* q_s = reinterpret_cast<float4*>(smem + C::kOffQ);  // [NREP][2][kChunks]
-  float2* p_s = reinterpret_cast<float2*>(smem + C::kOffP);  // [NWARPS][kTokPerWarp][kNrep2]
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  tc::tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+template <int D, int NREP>
+__global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv,
+                                                                const __grid_constant__ DecodeParams p) {
+  using C = DCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  int* flag = reinterpret_cast<int*>(smem + C::kOffFlag);
+  float* red_max = reinterpret_cast<float*>(smem + C::kOffRed);    // [2][4][16]
+  float* red_sum = red_max + 2 * 4 * kN;                           // [4][16]
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int split = blockIdx.x;
-  const int g = blockIdx.y;
-  const int s = blockIdx.z;
+  const int split = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
 
   const int pbeg = p.kv_indptr[s];
   const int ntab = p.kv_indptr[s + 1] - pbeg;
@@ -124,298 +158,289 @@ __global__ void __launch_bounds__(NWARPS * 32)
   }
   const int n_splits = max(1, (npages + p.pages_per_split - 1) / p.pages_per_split);
   if (split >= n_splits) return;
-
   const int pg0 = split * p.pages_per_split;
   const int pg1 = min(npages, pg0 + p.pages_per_split);
   const int tok_begin = pg0 * p.ps;
-  const int tok_end = min(seq_len, pg1 * p.ps);
-  const int ntok = max(0, tok_end - tok_begin);
-  const int ntiles = (ntok + TILE_TOK - 1) / TILE_TOK;
-  const int tile_pages = TILE_TOK / p.ps;
-  const int page_elems = p.ps * D;
-  const uint32_t page_bytes = static_cast<uint32_t>(page_elems) * 2u;
+  const int ntok = max(0, min(seq_len, pg1 * p.ps) - tok_begin);
+  const int ntiles = (ntok + kTile - 1) / kTile;
+  const int tile_pages = kTile / p.ps;
 
-  // Producer: warp 0 stages tile `i` (all its pages, K and V) into stage i % STAGES.
-  auto issue_tile = [&](int i) {
-    const int st = i % STAGES;
-    const int tp0 = pg0 + i * tile_pages;
-    const int tp1 = min(pg1, tp0 + tile_pages);
-    if (lane == 0) mbar_arrive_expect_tx(&bars[st], static_cast<uint32_t>(tp1 - tp0) * page_bytes * 2u);
-    __syncwarp();
-    __nv_bfloat16* kst = reinterpret_cast<__nv_bfloat16*>(smem + st * 2 * C::kStageBytes);
-    __nv_bfloat16* vst = kst + TILE_TOK * D;
-    for (int j = tp0 + lane; j < tp1; j += 32) {
-      int64_t page = p.kv_indices[pbeg + j];
-      if (page < 0 || page >= p.num_pages) {
-        record_error(p.err, kDevErrBadPage, s);
-        page = 0;
-      }
-      const int64_t off = (page * p.hkv + g) * page_elems;
-      bulk_g2s(kst + (j - tp0) * page_elems, p.kpool + off, page_bytes, &bars[st]);
-      bulk_g2s(vst + (j - tp0) * page_elems, p.vpool + off, page_bytes, &bars[st]);
-    }
-  };
-
+  // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], i == kPFull ? 128 : 1);
+    *abort_flag = 0;
     fence_barrier_init();
   }
-  __syncthreads();
   if (warp == 0) {
-    for (int i = 0; i < min(STAGES, ntiles); ++i) issue_tile(i);
+    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
   }
-
-  // Q for the n_rep heads of this KV head, pre-scaled, as f32 [h][half][chunk].
-  for (int e = threadIdx.x; e < NREP * C::kChunks * 2; e += C::kThreads) {
-    const int h = e / (C::kChunks * 2);
-    const int rem = e - h * C::kChunks * 2;
-    const int c = rem >> 1, half = rem & 1;
-    const int64_t qoff = (static_cast<int64_t>(s) * p.hq + g * NREP + h) * D + c * 8 + half * 4;
-    float4 v;
-    if (p.q_f32) {
-      v = *reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + qoff);
-    } else {
-      const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.q) + qoff);
-      const float2 a = bf2_to_f2(w.x), b = bf2_to_f2(w.y);
-      v = make_float4(a.x, a.y, b.x, b.y);
-    }
-    v.x *= p.qscale; v.y *= p.qscale; v.z *= p.qscale; v.w *= p.qscale;
-    q_s[(h * 2 + half) * C::kChunks + c] = v;
-  }
-  __syncthreads();
-
-  // Per-warp online-softmax state (m is warp-uniform).
-  float m_run[NREP], l_run[NREP];
-  float2 oacc[NREP][4];
-#pragma unroll
-  for (int h = 0; h < NREP; ++h) {
-    m_run[h] = -INFINITY;
-    l_run[h] = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) oacc[h][k] = make_float2(0.0f, 0.0f);
-  }
-  const int dc = lane % C::kChunks;  // PV: this lane's 16-byte dim chunk
-  const int tg = lane / C::kChunks;  // PV: this lane's token group
-  float2* pw = p_s + warp * C::kTokPerWarp * C::kNrep2;
-
-  for (int i = 0; i < ntiles; ++i) {
-    const int st = i % STAGES;
-    mbar_wait_bounded(&bars[st], static_cast<uint32_t>((i / STAGES) & 1), p.err, 1);
-    const uint4* kt = reinterpret_cast<const uint4*>(smem + st * 2 * C::kStageBytes);
-    const uint4* vt = reinterpret_cast<const uint4*>(smem + st * 2 * C::kStageBytes + C::kStageBytes);
-    const int nvalid = min(TILE_TOK, ntok - i * TILE_TOK);
-    const int wt0 = warp * C::kTokPerWarp;
-
-    // ---- S = Q K^T for this lane's tokens.
-    float2 acc[C::kTT][NREP];
-#pragma unroll
-    for (int j = 0; j < C::kTT; ++j)
-#pragma unroll
-      for (int h = 0; h < NREP; ++h) acc[j][h] = make_float2(0.0f, 0.0f);
-
-#pragma unroll 4
-    for (int c = 0; c < C::kChunks; ++c) {
-      const int cc = (c + lane) & (C::kChunks - 1);
-      float2 kf[C::kTT][4];
-#pragma unroll
-      for (int j = 0; j < C::kTT; ++j) {
-        const uint4 kw = kt[(wt0 + lane + 32 * j) * C::kChunks + cc];
-        kf[j][0] = bf2_to_f2(kw.x);
-        kf[j][1] = bf2_to_f2(kw.y);
-        kf[j][2] = bf2_to_f2(kw.z);
-        kf[j][3] = bf2_to_f2(kw.w);
+  // Q^T operand (16 rows, rows >= NREP zero) in the 128B-swizzled K-major
+  // layout, and a zeroed P^T operand (its rows >= NREP stay zero).
+  {
+    uint8_t* q_s = smem + C::kOffQ;
+    const int64_t qrow0 = static_cast<int64_t>(s) * p.hq + g * NREP;
+    for (int e = threadIdx.x; e < kN * (D / 8); e += kThreads) {
+      const int r = e / (D / 8), c = e - r * (D / 8);
+      const int b = c >> 3, cc = c & 7;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (r < NREP) {
+        const int64_t off = (qrow0 + r) * D + c * 8;
+        if (p.q_f32) {
+          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off);
+          const float4 bb = *(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off) + 1);
+          w = make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(bb.x, bb.y), f2_to_bf2(bb.z, bb.w));
+        } else {
+          w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + off);
+        }
       }
+      *reinterpret_cast<uint4*>(q_s + b * (kN * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
+    }
+    uint4* pz = reinterpret_cast<uint4*>(smem + C::kOffP);
+    for (int e = threadIdx.x; e < C::kPBytes / 16; e += kThreads) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_shared();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_kv);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % C::kStages;
+        if (j >= C::kStages &&
+            !tc::wait_bounded(&bars[kKVEmpty0 + st], ((j / C::kStages) - 1) & 1, abort_flag, p.err, 10))
+          break;
+        mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
+        uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
+        uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
+        for (int pi = 0; pi < tile_pages; ++pi) {
+          // Past the split's last page: reload that page (finite data, masked).
+          const int pidx = min(pg0 + j * tile_pages + pi, pg1 - 1);
+          int64_t page = p.kv_indices[pbeg + pidx];
+          if (page < 0 || page >= p.num_pages) {
+            record_error(p.err, kDevErrBadPage, s);
+            page = 0;
+          }
+          const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
+          const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
+#pragma unroll
+          for (int b = 0; b < C::kDB; ++b) {
+            const int off = b * kTile * 128 + pi * p.ps * 128;
+            tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
+            tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = tc::idesc_bf16(kTile, kN, false, false);
+      constexpr uint32_t idO = tc::idesc_bf16(C::kMO, kN, false, true);
+      const uint32_t q_s = smem_u32(smem + C::kOffQ);
+      const uint32_t p_s = smem_u32(smem + C::kOffP);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % C::kStages;
+        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j / C::kStages) & 1, abort_flag, p.err, 20)) break;
+        tc::fence_after_sync();
+        const uint32_t k_s = smem_u32(smem + C::kOffK + st * C::kKVBytes);
+        const uint32_t v_s = smem_u32(smem + C::kOffV + st * C::kKVBytes);
+        // S^T = K Q^T: both K-major; 16-wide k steps walk 32 bytes inside a
+        // 128-byte swizzle row, then jump to the next 64-wide head-dim block.
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t a = tc::sdesc_sw128(k_s + (k >> 2) * kTile * 128 + (k & 3) * 32, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(q_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
+          tc::mma_bf16(tmem + C::kTmemS, a, b, idS, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&bars[kSFull]);
+        if (!tc::wait_bounded(&bars[kPFull], j & 1, abort_flag, p.err, 21)) break;
+        tc::fence_after_sync();
+        // O^T += V^T P^T: A = V^T (MN-major: head dim contiguous; 64-wide
+        // blocks kTile*128 bytes apart), B = P^T (K-major over tokens).
+#pragma unroll
+        for (int k = 0; k < kTile / 16; ++k) {
+          const uint64_t b = tc::sdesc_sw128(p_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
+#pragma unroll
+          for (int mb = 0; mb < D / C::kMO; ++mb) {
+            const uint64_t a = tc::sdesc_sw128(v_s + mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128, kTile * 128, 1024);
+            tc::mma_bf16(tmem + C::kTmemO + mb * kN, a, b, idO, (j > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+        tc::mma_commit(&bars[kODone]);
+        tc::mma_commit(&bars[kKVEmpty0 + st]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = threadIdx.x;  // token row of the tile == TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float m_run[NREP], l_tok[NREP];
+#pragma unroll
+    for (int h = 0; h < NREP; ++h) {
+      m_run[h] = -INFINITY;
+      l_tok[h] = 0.0f;
+    }
+    uint8_t* p_s = smem + C::kOffP;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      ok = tc::wait_bounded(&bars[kSFull], j & 1, abort_flag, p.err, 30);
+      if (!ok) break;
+      tc::fence_after_sync();
+      float sv[16];
+      tmem_ld16(lane_addr + C::kTmemS, sv);
+      const bool valid = j * kTile + t < ntok;
+      float* rm = red_max + (j & 1) * 4 * kN;
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
-        const float4 qa = q_s[(h * 2 + 0) * C::kChunks + cc];
-        const float4 qb = q_s[(h * 2 + 1) * C::kChunks + cc];
+        sv[h] = valid ? sv[h] * p.qscale : -INFINITY;
+        const float wm = warp_max(sv[h]);
+        if (lane == 0) rm[warp * kN + h] = wm;
+      }
+      tc::named_sync(1, 128);
+      float alpha[NREP];
+      bool rescale = false;
 #pragma unroll
-        for (int j = 0; j < C::kTT; ++j) {
-          acc[j][h] = ffma2(make_float2(qa.x, qa.y), kf[j][0], acc[j][h]);
-          acc[j][h] = ffma2(make_float2(qa.z, qa.w), kf[j][1], acc[j][h]);
-          acc[j][h] = ffma2(make_float2(qb.x, qb.y), kf[j][2], acc[j][h]);
-          acc[j][h] = ffma2(make_float2(qb.z, qb.w), kf[j][3], acc[j][h]);
+      for (int h = 0; h < NREP; ++h) {
+        const float mt = fmaxf(fmaxf(rm[h], rm[kN + h]), fmaxf(rm[2 * kN + h], rm[3 * kN + h]));
+        const float mn = fmaxf(m_run[h], mt);  // finite: every tile holds a valid token
+        alpha[h] = (m_run[h] == -INFINITY) ? 0.0f : exp2f(m_run[h] - mn);
+        rescale |= alpha[h] != 1.0f;
+        sv[h] = exp2f(sv[h] - mn);  // masked tokens: exp2(-inf) = 0
+        l_tok[h] = l_tok[h] * alpha[h] + sv[h];
+        m_run[h] = mn;
+      }
+      if (j > 0) {
+        // O^T and the P^T buffer are busy until the previous P V finishes.
+        ok = tc::wait_bounded(&bars[kODone], (j - 1) & 1, abort_flag, p.err, 31);
+        if (!ok) break;
+        tc::fence_after_sync();
+        if (rescale) {  // alpha is uniform over the CTA, so is this branch
+#pragma unroll
+          for (int mb = 0; mb < D / C::kMO; ++mb) {
+            float ov[16];
+            tmem_ld16(lane_addr + C::kTmemO + mb * kN, ov);
+#pragma unroll
+            for (int h = 0; h < NREP; ++h) ov[h] *= alpha[h];
+            tmem_st16(lane_addr + C::kTmemO + mb * kN, ov);
+          }
+          tc::tmem_st_wait();
         }
       }
+      // P^T[h][t] (bf16) in the K-major swizzled layout: 64-token sub-tiles
+      // of 16 rows x 128 bytes; 16-byte chunk index XOR (row % 8).
+      {
+        const int sub = t >> 6, col = t & 63;
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+          const int off = sub * (kN * 128) + h * 128 + ((((col >> 3) ^ (h & 7))) << 4) + (col & 7) * 2;
+          *reinterpret_cast<__nv_bfloat16*>(p_s + off) = __float2bfloat16_rn(sv[h]);
+        }
+      }
+      fence_proxy_async_shared();
+      tc::fence_before_sync();
+      tc::mbar_arrive(&bars[kPFull]);
     }
 
-    // ---- online softmax (exp2 domain; scores already carry scale*log2 e).
-    float alpha[NREP];
+    // ---- epilogue: l per head over the CTA; O^T rows of this thread's lane.
+    if (ok && ntiles > 0) ok = tc::wait_bounded(&bars[kODone], (ntiles - 1) & 1, abort_flag, p.err, 32);
+    tc::fence_after_sync();
+    const bool have_o = __all_sync(0xffffffffu, ok) && ntiles > 0;  // warp-uniform for tcgen05.ld
 #pragma unroll
     for (int h = 0; h < NREP; ++h) {
-      float sc[C::kTT];
-      float mt = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < C::kTT; ++j) {
-        const bool valid = (wt0 + lane + 32 * j) < nvalid;
-        sc[j] = valid ? acc[j][h].x + acc[j][h].y : -INFINITY;
-        mt = fmaxf(mt, sc[j]);
-      }
-      mt = warp_max(mt);
-      const float mn = fmaxf(m_run[h], mt);
-      float psum = 0.0f;
-      if (mn == -INFINITY) {
-        alpha[h] = 1.0f;
-#pragma unroll
-        for (int j = 0; j < C::kTT; ++j) pw[(lane + 32 * j) * C::kNrep2 + h] = make_float2(0.0f, 0.0f);
-      } else {
-        alpha[h] = exp2f(m_run[h] - mn);
-#pragma unroll
-        for (int j = 0; j < C::kTT; ++j) {
-          const float pv = exp2f(sc[j] - mn);
-          psum += pv;
-          pw[(lane + 32 * j) * C::kNrep2 + h] = make_float2(pv, pv);
-        }
-      }
-      l_run[h] = l_run[h] * alpha[h] + psum;
-      m_run[h] = mn;
+      const float ws = warp_sum(l_tok[h]);
+      if (lane == 0) red_sum[warp * kN + h] = ws;
     }
-    __syncwarp();
-
-    // ---- O = alpha * O + P V over this warp's tokens.
-#pragma unroll
-    for (int h = 0; h < NREP; ++h) {
-      const float2 a2 = make_float2(alpha[h], alpha[h]);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) oacc[h][k] = __fmul2_rn(oacc[h][k], a2);
-    }
-    const int nw = min(C::kTokPerWarp, max(0, nvalid - wt0));
-#pragma unroll 4
-    for (int t = tg; t < nw; t += C::kTG) {
-      const uint4 vw = vt[(wt0 + t) * C::kChunks + dc];
-      const float2 v0 = bf2_to_f2(vw.x), v1 = bf2_to_f2(vw.y), v2 = bf2_to_f2(vw.z), v3 = bf2_to_f2(vw.w);
-      const float4* pt = reinterpret_cast<const float4*>(pw + t * C::kNrep2);
-#pragma unroll
-      for (int h2 = 0; h2 < C::kNrep2 / 2; ++h2) {
-        const float4 pp = pt[h2];
-        const float2 pa = make_float2(pp.x, pp.y);
-        const float2 pb = make_float2(pp.z, pp.w);
-        const int ha = 2 * h2, hb = 2 * h2 + 1;
-        oacc[ha][0] = ffma2(pa, v0, oacc[ha][0]);
-        oacc[ha][1] = ffma2(pa, v1, oacc[ha][1]);
-        oacc[ha][2] = ffma2(pa, v2, oacc[ha][2]);
-        oacc[ha][3] = ffma2(pa, v3, oacc[ha][3]);
-        if (hb < NREP) {
-          oacc[hb][0] = ffma2(pb, v0, oacc[hb][0]);
-          oacc[hb][1] = ffma2(pb, v1, oacc[hb][1]);
-          oacc[hb][2] = ffma2(pb, v2, oacc[hb][2]);
-          oacc[hb][3] = ffma2(pb, v3, oacc[hb][3]);
-        }
-      }
-    }
-    __syncthreads();  // every warp is done with stage `st` and with its P slots
-    if (warp == 0 && i + STAGES < ntiles) issue_tile(i + STAGES);
-  }
-
-  // ---- reduce the PV token groups inside the warp, and l across lanes.
-#pragma unroll
-  for (int o = C::kChunks; o < 32; o <<= 1) {
+    tc::named_sync(1, 128);
+    float l_cta[NREP];
 #pragma unroll
     for (int h = 0; h < NREP; ++h)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        oacc[h][k].x += __shfl_xor_sync(0xffffffffu, oacc[h][k].x, o);
-        oacc[h][k].y += __shfl_xor_sync(0xffffffffu, oacc[h][k].y, o);
-      }
-  }
-#pragma unroll
-  for (int h = 0; h < NREP; ++h) l_run[h] = warp_sum(l_run[h]);
+      l_cta[h] = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] + red_sum[3 * kN + h];
 
-  // ---- cross-warp combine, in warp order (buffers alias the stage area).
-  float* comb_o = reinterpret_cast<float*>(smem);          // [NWARPS][NREP][D]
-  float* comb_ml = comb_o + NWARPS * NREP * D;              // [NWARPS][NREP][2]
-  if (tg == 0) {
+    const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
+    // Rows of O^T this thread holds: M=64 puts row d in lane (d % 16) + 32 (d / 16);
+    // M=128 puts row d in lane d; D = 256 uses two M=128 blocks 16 columns apart.
+    const bool holds = (C::kMO == 64) ? (lane < 16) : true;
+    const int d_base = (C::kMO == 64) ? warp * 16 + lane : warp * 32 + lane;
 #pragma unroll
-    for (int h = 0; h < NREP; ++h) {
-      float4* dst = reinterpret_cast<float4*>(comb_o + (warp * NREP + h) * D + dc * 8);
-      dst[0] = make_float4(oacc[h][0].x, oacc[h][0].y, oacc[h][1].x, oacc[h][1].y);
-      dst[1] = make_float4(oacc[h][2].x, oacc[h][2].y, oacc[h][3].x, oacc[h][3].y);
-    }
-  }
-  if (lane == 0) {
+    for (int mb = 0; mb < D / C::kMO; ++mb) {
+      float ov[16];
+      if (have_o) {
+        tmem_ld16(lane_addr + C::kTmemO + mb * kN, ov);
+      } else {
 #pragma unroll
-    for (int h = 0; h < NREP; ++h) {
-      comb_ml[(warp * NREP + h) * 2 + 0] = m_run[h];
-      comb_ml[(warp * NREP + h) * 2 + 1] = l_run[h];
+        for (int i = 0; i < 16; ++i) ov[i] = 0.0f;
+      }
+      const int d = d_base + mb * 128;
+      if (!holds) continue;
+#pragma unroll
+      for (int h = 0; h < NREP; ++h) {
+        if (n_splits == 1) {
+          const float r = finalize(ov[h], l_cta[h], m_run[h], p.phantom);
+          if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
+          else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
+        } else {
+          const int64_t slot = (head0 + h) * p.max_splits + split;
+          p.ws_o[slot * D + d] = ov[h];
+          if (d == 0) {
+            p.ws_ml[slot * 2 + 0] = m_run[h];
+            p.ws_ml[slot * 2 + 1] = l_cta[h];
+          }
+        }
+      }
     }
-  }
-  __syncthreads();
 
-  const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;  // first q head of this CTA
-  for (int e = threadIdx.x; e < NREP * D; e += C::kThreads) {
-    const int h = e / D, d = e - (e / D) * D;
-    float mc = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < NWARPS; ++w) mc = fmaxf(mc, comb_ml[(w * NREP + h) * 2]);
-    float o = 0.0f, l = 0.0f;
-    if (mc != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < NWARPS; ++w) {
-        const float mw = comb_ml[(w * NREP + h) * 2];
-        if (mw == -INFINITY) continue;
-        const float a = exp2f(mw - mc);
-        o += comb_o[(w * NREP + h) * D + d] * a;
-        l += comb_ml[(w * NREP + h) * 2 + 1] * a;
+    if (n_splits > 1) {
+      // ---- split combine: the last CTA of (sequence, kv head) merges in split order.
+      __threadfence();
+      tc::named_sync(1, 128);
+      if (t == 0) {
+        const unsigned int ticket = atomicAdd(&p.ws_cnt[s * p.hkv + g], 1u);
+        *last_flag = (ticket == static_cast<unsigned int>(n_splits - 1)) ? 1 : 0;
       }
-    }
-    if (n_splits == 1) {
-      const float r = finalize(o, l, mc, p.phantom);
-      if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
-      else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
-    } else {
-      const int64_t slot = (head0 + h) * p.max_splits + split;
-      p.ws_o[slot * D + d] = o;
-      if (d == 0) {
-        p.ws_ml[slot * 2 + 0] = mc;
-        p.ws_ml[slot * 2 + 1] = l;
+      tc::named_sync(1, 128);
+      if (*last_flag) {
+        __threadfence();
+        for (int e = t; e < NREP * D; e += 128) {
+          const int h = e / D, d = e - (e / D) * D;
+          const int64_t slot0 = (head0 + h) * p.max_splits;
+          float mall = -INFINITY;
+          for (int jj = 0; jj < n_splits; ++jj) mall = fmaxf(mall, ld_cg(p.ws_ml + (slot0 + jj) * 2));
+          float o = 0.0f, l = 0.0f;
+          if (mall != -INFINITY) {
+            for (int jj = 0; jj < n_splits; ++jj) {
+              const float mj = ld_cg(p.ws_ml + (slot0 + jj) * 2);
+              if (mj == -INFINITY) continue;
+              const float a = exp2f(mj - mall);
+              o += ld_cg(p.ws_o + (slot0 + jj) * D + d) * a;
+              l += ld_cg(p.ws_ml + (slot0 + jj) * 2 + 1) * a;
+            }
+          }
+          const float r = finalize(o, l, mall, p.phantom);
+          if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
+          else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
+        }
+        if (t == 0) p.ws_cnt[s * p.hkv + g] = 0u;  // ready for the next launch on this workspace
       }
     }
   }
-  if (n_splits == 1) return;
 
-  // ---- split combine: the last CTA of (sequence, kv head) merges in split order.
-  __threadfence();
+  tc::fence_before_sync();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int ticket = atomicAdd(&p.ws_cnt[s * p.hkv + g], 1u);
-    *flag = (ticket == static_cast<unsigned int>(n_splits - 1)) ? 1 : 0;
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::kTmemCols);
   }
-  __syncthreads();
-  if (*flag == 0) return;
-  __threadfence();
-  for (int e = threadIdx.x; e < NREP * D; e += C::kThreads) {
-    const int h = e / D, d = e - (e / D) * D;
-    const int64_t slot0 = (head0 + h) * p.max_splits;
-    float mall = -INFINITY;
-    for (int j = 0; j < n_splits; ++j) mall = fmaxf(mall, ld_cg(p.ws_ml + (slot0 + j) * 2));
-    float o = 0.0f, l = 0.0f;
-    if (mall != -INFINITY) {
-      for (int j = 0; j < n_splits; ++j) {
-        const float mj = ld_cg(p.ws_ml + (slot0 + j) * 2);
-        if (mj == -INFINITY) continue;
-        const float a = exp2f(mj - mall);
-        o += ld_cg(p.ws_o + (slot0 + j) * D + d) * a;
-        l += ld_cg(p.ws_ml + (slot0 + j) * 2 + 1) * a;
-      }
-    }
-    const float r = finalize(o, l, mall, p.phantom);
-    if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
-    else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
-  }
-  if (threadIdx.x == 0) p.ws_cnt[s * p.hkv + g] = 0u;  // ready for the next launch on this workspace
 }
 
-// Per-head-dim launch shapes: 64 KiB of K/V stages per CTA.
-template <int D> struct Shape;
-template <> struct Shape<64> { static constexpr int kWarps = 4, kTile = 128, kStages = 2; };
-template <> struct Shape<128> { static constexpr int kWarps = 2, kTile = 64, kStages = 2; };
-template <> struct Shape<256> { static constexpr int kWarps = 1, kTile = 32, kStages = 2; };
-
 template <int D, int NREP>
-int launch_decode(const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
-  using S = Shape<D>;
-  using C = DecodeCfg<D, NREP, S::kWarps, S::kTile, S::kStages>;
-  auto kern = paged_decode_kernel<D, NREP, S::kWarps, S::kTile, S::kStages>;
+int launch_decode(const CUtensorMap& tkv, const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
+  using C = DCfg<D>;
+  auto kern = paged_decode_kernel<D, NREP>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -425,36 +450,27 @@ int launch_decode(const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
     configured[dev] = true;
   }
   dim3 grid(prm.max_splits, prm.hkv, n_seqs);
-  kern<<<grid, C::kThreads, C::kSmem, stream>>>(prm);
+  kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
   return check_launch("paged_decode_kernel");
 }
 
 template <int D>
-int dispatch_nrep(int nrep, const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
+int dispatch_nrep(int nrep, const CUtensorMap& tkv, const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
   switch (nrep) {
-    case 1: return launch_decode<D, 1>(prm, n_seqs, stream);
-    case 2: return launch_decode<D, 2>(prm, n_seqs, stream);
-    case 3: return launch_decode<D, 3>(prm, n_seqs, stream);
-    case 4: return launch_decode<D, 4>(prm, n_seqs, stream);
-    case 5: return launch_decode<D, 5>(prm, n_seqs, stream);
-    case 6: return launch_decode<D, 6>(prm, n_seqs, stream);
-    case 7: return launch_decode<D, 7>(prm, n_seqs, stream);
-    case 8: return launch_decode<D, 8>(prm, n_seqs, stream);
+    case 1: return launch_decode<D, 1>(tkv, prm, n_seqs, stream);
+    case 2: return launch_decode<D, 2>(tkv, prm, n_seqs, stream);
+    case 3: return launch_decode<D, 3>(tkv, prm, n_seqs, stream);
+    case 4: return launch_decode<D, 4>(tkv, prm, n_seqs, stream);
+    case 5: return launch_decode<D, 5>(tkv, prm, n_seqs, stream);
+    case 6: return launch_decode<D, 6>(tkv, prm, n_seqs, stream);
+    case 7: return launch_decode<D, 7>(tkv, prm, n_seqs, stream);
+    case 8: return launch_decode<D, 8>(tkv, prm, n_seqs, stream);
     default: return set_error(MTN_EINVAL, "paged decode: query heads per kv head %d not in [1,8]", nrep);
   }
 }
 
-int tile_pages_for(int head_dim, int page_size) {
-  const int tile = head_dim == 64 ? Shape<64>::kTile : head_dim == 128 ? Shape<128>::kTile : Shape<256>::kTile;
-  return tile / page_size;
-}
-
-int tile_tokens_for(int head_dim) {
-  return head_dim == 64 ? Shape<64>::kTile : head_dim == 128 ? Shape<128>::kTile : Shape<256>::kTile;
-}
-
-int effective_split(int head_dim, int page_size, int pages_per_split) {
-  const int tp = tile_pages_for(head_dim, page_size);
+int effective_split(int page_size, int pages_per_split) {
+  const int tp = kTile / page_size;
   if (pages_per_split <= 0) pages_per_split = tp;
   return ((pages_per_split + tp - 1) / tp) * tp;
 }
@@ -469,32 +485,30 @@ extern "C" {
 size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                                         int32_t max_pages_per_seq, int32_t pages_per_split) {
   if (n_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_pages_per_seq < 0) return 0;
-  // Page size only changes the rounding of pages_per_split; size for the
-  // smallest legal tile (page_size 16 for every head dim) conservatively
-  // by using pages_per_split as given, at least 1.
+  // Splits are rounded up to whole 128-token tiles, which only lowers the
+  // split count, so sizing with the pages_per_split given (at least 1) is safe.
   const int64_t pps = pages_per_split > 0 ? pages_per_split : 1;
   const int64_t max_splits = std::max<int64_t>(1, (max_pages_per_seq + pps - 1) / pps);
   const int64_t slots = static_cast<int64_t>(n_seqs) * num_q_heads * max_splits;
-  size_t bytes = static_cast<size_t>(slots) * head_dim * 4;               // ws_o
-  bytes += static_cast<size_t>(slots) * 2 * 4;                              // ws_ml
-  bytes += static_cast<size_t>(n_seqs) * num_kv_heads * 4;                  // counters
+  size_t bytes = static_cast<size_t>(slots) * head_dim * 4;   // ws_o
+  bytes += static_cast<size_t>(slots) * 2 * 4;                  // ws_ml
+  bytes += static_cast<size_t>(n_seqs) * num_kv_heads * 4;      // arrival counters
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
 int32_t mtn_paged_decode_default_split(const mtn_kv_layout* pool, int32_t n_seqs, int64_t total_pages,
                                        int32_t max_pages_per_seq, int32_t num_q_heads) {
   (void)num_q_heads;
-  if (pool == nullptr || pool->page_size <= 0 || n_seqs <= 0) return 0;
-  if (pool->head_dim != 64 && pool->head_dim != 128 && pool->head_dim != 256) return 0;
-  if (mtn::tile_tokens_for(pool->head_dim) % pool->page_size != 0) return 0;
-  const int tp = mtn::tile_pages_for(pool->head_dim, pool->page_size);
-  // Aim for about four resident CTA slots' worth of work items per SM.
-  const int64_t target = static_cast<int64_t>(mtn::sm_count()) * 8;
+  if (pool == nullptr || pool->page_size <= 0 || n_seqs <= 0 || mtn::kTile % pool->page_size != 0) return 0;
+  const int tp = mtn::kTile / pool->page_size;
+  // About six CTAs per SM of (page, kv head) work: enough to cover the
+  // device twice with the ~3 resident CTAs per SM, few partials to merge.
+  const int64_t target = static_cast<int64_t>(mtn::sm_count()) * 6;
   const int64_t units = std::max<int64_t>(1, total_pages) * pool->num_kv_heads;
   int64_t pps = (units + target - 1) / target;
   pps = std::max<int64_t>(pps, tp);
   pps = std::min<int64_t>(pps, std::max(max_pages_per_seq, 1));
-  return mtn::effective_split(pool->head_dim, pool->page_size, static_cast<int>(pps));
+  return mtn::effective_split(pool->page_size, static_cast<int>(pps));
 }
 
 int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
@@ -511,16 +525,16 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_decode: bad o dtype");
   MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads % pool->num_kv_heads == 0,
                 "mtn_paged_decode: %d query heads not a multiple of %d kv heads", num_q_heads, pool->num_kv_heads);
+  MTN_CHECK_ARG(pool->num_kv_heads <= 65535, "mtn_paged_decode: too many kv heads");
   const int D = pool->head_dim;
-  MTN_CHECK_ARG(mtn::tile_tokens_for(D) % pool->page_size == 0,
-                "mtn_paged_decode: page_size %d must divide the %d-token tile", pool->page_size,
-                mtn::tile_tokens_for(D));
+  MTN_CHECK_ARG(pool->page_size % 8 == 0 && mtn::kTile % pool->page_size == 0,
+                "mtn_paged_decode: page_size %d must be a multiple of 8 dividing %d", pool->page_size, mtn::kTile);
   MTN_CHECK_ARG(max_pages_per_seq >= 0, "mtn_paged_decode: max_pages_per_seq < 0");
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
                 "mtn_paged_decode: q/o must be 16-byte aligned");
-  const int pps = mtn::effective_split(D, pool->page_size, pages_per_split);
+  const int pps = mtn::effective_split(pool->page_size, pages_per_split);
   const int max_splits = std::max(1, (max_pages_per_seq + pps - 1) / pps);
-  MTN_CHECK_ARG(max_splits <= 65535 * 32, "mtn_paged_decode: too many splits");
+  MTN_CHECK_ARG(max_splits <= (1 << 20), "mtn_paged_decode: too many splits");
   const size_t need = mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool->num_kv_heads, D,
                                                        max_pages_per_seq, pps);
   if (max_splits > 1) {
@@ -528,12 +542,14 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
                   "mtn_paged_decode: workspace of %zu bytes < %zu needed", workspace_bytes, need);
     MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "mtn_paged_decode: workspace alignment");
   }
+  CUtensorMap tkv;
+  st = mtn::pool_tensor_map(pool, &tkv);
+  if (st != MTN_OK) return st;
 
   mtn::DecodeParams prm{};
-  const int64_t page_elems = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * D;
-  auto* base = static_cast<const __nv_bfloat16*>(pool->base);
-  prm.kpool = base + (static_cast<int64_t>(layer) * 2 + 0) * pool->num_pages * page_elems;
-  prm.vpool = base + (static_cast<int64_t>(layer) * 2 + 1) * pool->num_pages * page_elems;
+  const int64_t rows_per_block = pool->num_pages * pool->num_kv_heads * pool->page_size;
+  prm.row_k = (static_cast<int64_t>(layer) * 2 + 0) * rows_per_block;
+  prm.row_v = (static_cast<int64_t>(layer) * 2 + 1) * rows_per_block;
   prm.num_pages = pool->num_pages;
   prm.hkv = pool->num_kv_heads;
   prm.ps = pool->page_size;
@@ -559,9 +575,9 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
   switch (D) {
-    case 64: return mtn::dispatch_nrep<64>(nrep, prm, n_seqs, s);
-    case 128: return mtn::dispatch_nrep<128>(nrep, prm, n_seqs, s);
-    default: return mtn::dispatch_nrep<256>(nrep, prm, n_seqs, s);
+    case 64: return mtn::dispatch_nrep<64>(nrep, tkv, prm, n_seqs, s);
+    case 128: return mtn::dispatch_nrep<128>(nrep, tkv, prm, n_seqs, s);
+    default: return mtn::dispatch_nrep<256>(nrep, tkv, prm, n_seqs, s);
   }
 }
 

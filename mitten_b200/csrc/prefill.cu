@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "tc.cuh"
+#include "tmaps.hpp"
 
 namespace mtn {
 namespace {
@@ -312,23 +313,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // --------------------------------------------------------------- host side
 
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled get_encoder() {
-  static EncodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(f);
-  });
-  return fn;
-}
-
 template <int D>
 int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
                    cudaStream_t stream) {
@@ -381,35 +365,11 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
                 "mtn_paged_prefill: page_size %d must be a multiple of 8 dividing %d", pool->page_size, bn);
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
                 "mtn_paged_prefill: q/o must be 16-byte aligned");
-  const int64_t rows = static_cast<int64_t>(pool->num_layers) * 2 * pool->num_pages * pool->num_kv_heads *
-                       pool->page_size;
-  MTN_CHECK_ARG(rows < (int64_t(1) << 31), "mtn_paged_prefill: pool has %lld rows; TMA coordinates need < 2^31",
-                (long long)rows);
-  auto enc = mtn::get_encoder();
-  if (enc == nullptr) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-
   CUtensorMap tq, tkv;
-  {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(num_q_heads),
-                                static_cast<cuuint64_t>(total_q)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(num_q_heads) * D * 2};
-    const cuuint32_t box[3] = {64, 1, mtn::kBM};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled(q) failed: %d", (int)r);
-  }
-  {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
-    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(pool->page_size)};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pool->base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled(kv) failed: %d", (int)r);
-  }
+  st = mtn::pool_tensor_map(pool, &tkv);
+  if (st != MTN_OK) return st;
+  st = mtn::q_tensor_map(q, total_q, num_q_heads, D, mtn::kBM, &tq);
+  if (st != MTN_OK) return st;
   mtn::PrefillParams prm{};
   prm.qo_indptr = qo_indptr;
   prm.kv_indptr = kv_indptr;

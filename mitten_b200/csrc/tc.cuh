@@ -140,12 +140,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
-// Instruction descriptor for kind::f16: bf16 A and B, f32 D, A K-major.
+// Instruction descriptor for kind::f16: bf16 A and B, f32 D.
 //   bits 4-5 D format (1 = f32)   bits 7-9 A format (1 = bf16)   bits 10-12 B format (1 = bf16)
-//   bit 15 A major (0 = K)        bit 16 B major (1 = MN)        bits 17-22 N >> 3   bits 24-28 M >> 4
-constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+//   bit 15 A major (1 = MN)       bit 16 B major (1 = MN)        bits 17-22 N >> 3   bits 24-28 M >> 4
+constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major, bool a_mn_major = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Named barrier over `count` threads (ids 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 }  // namespace tc
