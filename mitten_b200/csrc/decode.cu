@@ -71,22 +71,33 @@ struct DCfg {
   static constexpr int kQBytes = kN * D * 2;               // Q^T operand: 16 rows x D
   static constexpr int kKVBytes = kTile * D * 2;           // one of K or V per stage
   static constexpr int kPBytes = kN * kTile * 2;           // P^T operand: 16 rows x 128 tokens
-  static constexpr int kOffQ = 0;
+  static constexpr int kMaxSplitPages = 256;               // page ids staged per CTA
+  // Small state first, then the 1 KiB-aligned operand area.
+  static constexpr int kOffBar = 0;                        // 16 mbarriers
+  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort flag, last-CTA flag
+  static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums, [2] flags
+  static constexpr int kOffIdx = kOffRed + (2 * 4 * kN + 4 * kN + 16) * 4;
+  static constexpr int kSmallBytes = kOffIdx + kMaxSplitPages * 4;
+  static constexpr int kOffQ = 0;                          // relative to the aligned operand area
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKVBytes;
   static constexpr int kOffP = kOffV + kStages * kKVBytes;
-  static constexpr int kOffRed = kOffP + kPBytes;          // [2][4][16] maxima, [4][16] sums
-  static constexpr int kOffBar = kOffRed + (2 * 4 * kN + 4 * kN) * 4;
-  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort flag, last-CTA flag
-  static constexpr int kSmem = kOffMisc + 64 + 1024;       // + slack for 1024-byte alignment
+  static constexpr int kBigBytes = kOffP + kPBytes;
+  static constexpr int kSmem = kSmallBytes + 1023 + kBigBytes;
   static constexpr int kMO = D == 64 ? 64 : 128;           // MMA2 M
-  static constexpr int kTmemS = 0;                          // 16 columns
-  static constexpr int kTmemO = 16;                         // 16 (D <= 128) or 32 (D = 256) columns
+  static constexpr int kTmemS = 0;                          // 2 x 16 columns (double-buffered S^T)
+  static constexpr int kTmemO = 32;                         // 16 (D <= 128) or 32 (D = 256) columns
   static constexpr int kTmemCols = 64;
   static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KiB alignment");
 };
 
-enum Bar { kKVFull0 = 0, kKVFull1 = 1, kKVEmpty0 = 2, kKVEmpty1 = 3, kSFull = 4, kPFull = 5, kODone = 6 };
+// Lazy rescaling: P is exponentiated against a CTA-wide reference max that
+// only moves when a tile's max exceeds it by more than 2^kRescaleLog2, so
+// P <= 2^8 (exact in bf16 range) and O^T in TMEM is rarely touched.
+constexpr float kRescaleLog2 = 8.0f;
+
+enum Bar { kKVFull0 = 0, kKVFull1 = 1, kKVEmpty0 = 2, kKVEmpty1 = 3, kSFull0 = 4, kSFull1 = 5, kPFull = 6,
+           kODone = 7 };
 
 // Final normalisation of one output element: o/l with the phantom key folded in.
 __device__ __forceinline__ float finalize(float o, float l, float m, int phantom) {
@@ -125,17 +136,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 }
 
 template <int D, int NREP>
-__global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv,
-                                                                const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ DecodeParams p) {
   using C = DCfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  float* red_max = reinterpret_cast<float*>(smem + C::kOffRed);    // [2][4][16]
-  float* red_sum = red_max + 2 * 4 * kN;                           // [4][16]
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + C::kOffBar);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem_raw + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 8);
+  float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
+  float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
+  int* idx_s = reinterpret_cast<int*>(smem_raw + C::kOffIdx);        // this split's page ids
+  uint8_t* big = smem_raw + C::kSmallBytes;
+  big += (1024 - (smem_u32(big) & 1023)) & 1023;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -165,22 +178,64 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel
   const int ntiles = (ntok + kTile - 1) / kTile;
   const int tile_pages = kTile / p.ps;
 
-  // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], i == kPFull ? 128 : 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == kPFull ? 128 : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
-    tc::tmem_relinquish();
-  }
-  // Q^T operand (16 rows, rows >= NREP zero) in the 128B-swizzled K-major
-  // layout, and a zeroed P^T operand (its rows >= NREP stay zero).
-  {
-    uint8_t* q_s = smem + C::kOffQ;
+  __syncthreads();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    // Stage the split's page ids once (one coalesced round trip), then every
+    // tile's boxes are issued by tile_pages lanes in parallel.
+    for (int i = lane; i < pg1 - pg0; i += 32) {
+      int64_t page = p.kv_indices[pbeg + pg0 + i];
+      if (page < 0 || page >= p.num_pages) {
+        record_error(p.err, kDevErrBadPage, s);
+        page = 0;
+      }
+      idx_s[i] = static_cast<int>(page);
+    }
+    __syncwarp();
+    if (lane == 0) tc::prefetch_tmap(&tm_kv);
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % C::kStages;
+      if (j >= C::kStages) {
+        bool free_ok = true;
+        if (lane == 0) free_ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((j / C::kStages) - 1) & 1, abort_flag, p.err, 10);
+        if (!__shfl_sync(0xffffffffu, free_ok, 0)) break;  // warp-uniform
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
+      __syncwarp();
+      if (lane < tile_pages) {
+        // Past the split's last page: reload that page (finite data, masked).
+        const int pi = lane;
+        const int64_t page = idx_s[min(j * tile_pages + pi, pg1 - pg0 - 1)];
+        const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
+        const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
+        uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
+        uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
+#pragma unroll
+        for (int b = 0; b < C::kDB; ++b) {
+          const int off = b * kTile * 128 + pi * p.ps * 128;
+          tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
+          tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
+        }
+      }
+    }
+  } else {
+    // Everyone else: TMEM, the Q^T operand (16 rows, rows >= NREP zero, 128B
+    // swizzled K-major) and a zeroed P^T operand (rows >= NREP stay zero),
+    // overlapping the producer's first loads.
+    if (warp == 0) {
+      tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+      tc::tmem_relinquish();
+    }
+    const int tid = warp == 5 ? 128 + lane : threadIdx.x;  // 0..159
+    uint8_t* q_s = big + C::kOffQ;
     const int64_t qrow0 = static_cast<int64_t>(s) * p.hq + g * NREP;
-    for (int e = threadIdx.x; e < kN * (D / 8); e += kThreads) {
+    for (int e = tid; e < kN * (D / 8); e += 160) {
       const int r = e / (D / 8), c = e - r * (D / 8);
       const int b = c >> 3, cc = c & 7;
       uint4 w = make_uint4(0u, 0u, 0u, 0u);
@@ -196,70 +251,48 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel
       }
       *reinterpret_cast<uint4*>(q_s + b * (kN * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
     }
-    uint4* pz = reinterpret_cast<uint4*>(smem + C::kOffP);
-    for (int e = threadIdx.x; e < C::kPBytes / 16; e += kThreads) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+    uint4* pz = reinterpret_cast<uint4*>(big + C::kOffP);
+    for (int e = tid; e < C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_shared();
+    tc::fence_before_sync();
+    tc::named_sync(2, 160);
+    tc::fence_after_sync();
   }
-  fence_proxy_async_shared();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_base_s;
+  const uint32_t tmem = *tmem_base_s;  // valid for every role past named barrier 2
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tc::prefetch_tmap(&tm_kv);
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % C::kStages;
-        if (j >= C::kStages &&
-            !tc::wait_bounded(&bars[kKVEmpty0 + st], ((j / C::kStages) - 1) & 1, abort_flag, p.err, 10))
-          break;
-        mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
-        uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
-        uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
-        for (int pi = 0; pi < tile_pages; ++pi) {
-          // Past the split's last page: reload that page (finite data, masked).
-          const int pidx = min(pg0 + j * tile_pages + pi, pg1 - 1);
-          int64_t page = p.kv_indices[pbeg + pidx];
-          if (page < 0 || page >= p.num_pages) {
-            record_error(p.err, kDevErrBadPage, s);
-            page = 0;
-          }
-          const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
-          const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
-#pragma unroll
-          for (int b = 0; b < C::kDB; ++b) {
-            const int off = b * kTile * 128 + pi * p.ps * 128;
-            tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
-            tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
-          }
-        }
-      }
-    }
-  } else if (warp == 5) {
+  if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kTile, kN, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(C::kMO, kN, false, true);
-      const uint32_t q_s = smem_u32(smem + C::kOffQ);
-      const uint32_t p_s = smem_u32(smem + C::kOffP);
-      for (int j = 0; j < ntiles; ++j) {
+      const uint32_t q_s = smem_u32(big + C::kOffQ);
+      const uint32_t p_s = smem_u32(big + C::kOffP);
+      // S^T(j) = K_j Q^T into S buffer j&1: both operands K-major; 16-wide k
+      // steps walk 32 bytes inside a 128-byte swizzle row, then the next block.
+      auto issue_s = [&](int j) -> bool {
         const int st = j % C::kStages;
-        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j / C::kStages) & 1, abort_flag, p.err, 20)) break;
+        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j / C::kStages) & 1, abort_flag, p.err, 20)) return false;
         tc::fence_after_sync();
-        const uint32_t k_s = smem_u32(smem + C::kOffK + st * C::kKVBytes);
-        const uint32_t v_s = smem_u32(smem + C::kOffV + st * C::kKVBytes);
-        // S^T = K Q^T: both K-major; 16-wide k steps walk 32 bytes inside a
-        // 128-byte swizzle row, then jump to the next 64-wide head-dim block.
+        const uint32_t k_s = smem_u32(big + C::kOffK + st * C::kKVBytes);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint64_t a = tc::sdesc_sw128(k_s + (k >> 2) * kTile * 128 + (k & 3) * 32, 16, 1024);
           const uint64_t b = tc::sdesc_sw128(q_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
-          tc::mma_bf16(tmem + C::kTmemS, a, b, idS, k > 0 ? 1u : 0u);
+          tc::mma_bf16(tmem + C::kTmemS + (j & 1) * kN, a, b, idS, k > 0 ? 1u : 0u);
         }
-        tc::mma_commit(&bars[kSFull]);
+        tc::mma_commit(&bars[kSFull0 + (j & 1)]);
+        return true;
+      };
+      bool ok = ntiles == 0 || issue_s(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        // Overlap the next tile's S with this tile's softmax (its S buffer was
+        // released by the softmax of tile j-1, already waited on below).  With
+        // a single K/V stage the next tile only lands after this P V.
+        if (C::kStages > 1 && j + 1 < ntiles && !issue_s(j + 1)) break;
         if (!tc::wait_bounded(&bars[kPFull], j & 1, abort_flag, p.err, 21)) break;
         tc::fence_after_sync();
+        const int st = j % C::kStages;
+        const uint32_t v_s = smem_u32(big + C::kOffV + st * C::kKVBytes);
         // O^T += V^T P^T: A = V^T (MN-major: head dim contiguous; 64-wide
         // blocks kTile*128 bytes apart), B = P^T (K-major over tokens).
 #pragma unroll
@@ -267,32 +300,34 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel
           const uint64_t b = tc::sdesc_sw128(p_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
 #pragma unroll
           for (int mb = 0; mb < D / C::kMO; ++mb) {
-            const uint64_t a = tc::sdesc_sw128(v_s + mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128, kTile * 128, 1024);
+            const uint64_t a =
+                tc::sdesc_sw128(v_s + mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128, kTile * 128, 1024);
             tc::mma_bf16(tmem + C::kTmemO + mb * kN, a, b, idO, (j > 0 || k > 0) ? 1u : 0u);
           }
         }
         tc::mma_commit(&bars[kODone]);
         tc::mma_commit(&bars[kKVEmpty0 + st]);
+        if (C::kStages == 1 && j + 1 < ntiles && !issue_s(j + 1)) break;
       }
     }
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------ softmax
     const int t = threadIdx.x;  // token row of the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    float m_run[NREP], l_tok[NREP];
+    float m_ref[NREP], l_tok[NREP];
 #pragma unroll
     for (int h = 0; h < NREP; ++h) {
-      m_run[h] = -INFINITY;
+      m_ref[h] = -INFINITY;
       l_tok[h] = 0.0f;
     }
-    uint8_t* p_s = smem + C::kOffP;
+    uint8_t* p_s = big + C::kOffP;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      ok = tc::wait_bounded(&bars[kSFull], j & 1, abort_flag, p.err, 30);
+      ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
       if (!ok) break;
       tc::fence_after_sync();
       float sv[16];
-      tmem_ld16(lane_addr + C::kTmemS, sv);
+      tmem_ld16(lane_addr + C::kTmemS + (j & 1) * kN, sv);
       const bool valid = j * kTile + t < ntok;
       float* rm = red_max + (j & 1) * 4 * kN;
 #pragma unroll
@@ -307,19 +342,22 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
         const float mt = fmaxf(fmaxf(rm[h], rm[kN + h]), fmaxf(rm[2 * kN + h], rm[3 * kN + h]));
-        const float mn = fmaxf(m_run[h], mt);  // finite: every tile holds a valid token
-        alpha[h] = (m_run[h] == -INFINITY) ? 0.0f : exp2f(m_run[h] - mn);
-        rescale |= alpha[h] != 1.0f;
-        sv[h] = exp2f(sv[h] - mn);  // masked tokens: exp2(-inf) = 0
+        alpha[h] = 1.0f;
+        if (mt > m_ref[h] + kRescaleLog2 || m_ref[h] == -INFINITY) {  // CTA-uniform decision
+          alpha[h] = (m_ref[h] == -INFINITY) ? 0.0f : exp2f(m_ref[h] - mt);
+          m_ref[h] = mt;  // finite: every tile holds a valid token
+          rescale |= j > 0;
+        }
+        sv[h] = exp2f(sv[h] - m_ref[h]);  // masked tokens: exp2(-inf) = 0
         l_tok[h] = l_tok[h] * alpha[h] + sv[h];
-        m_run[h] = mn;
       }
       if (j > 0) {
-        // O^T and the P^T buffer are busy until the previous P V finishes.
+        // The P^T buffer (and O^T, when rescaling) is busy until the
+        // previous P V finishes.
         ok = tc::wait_bounded(&bars[kODone], (j - 1) & 1, abort_flag, p.err, 31);
         if (!ok) break;
         tc::fence_after_sync();
-        if (rescale) {  // alpha is uniform over the CTA, so is this branch
+        if (rescale) {
 #pragma unroll
           for (int mb = 0; mb < D / C::kMO; ++mb) {
             float ov[16];
@@ -380,14 +418,14 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1) paged_decode_kernel
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
         if (n_splits == 1) {
-          const float r = finalize(ov[h], l_cta[h], m_run[h], p.phantom);
+          const float r = finalize(ov[h], l_cta[h], m_ref[h], p.phantom);
           if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
           else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
         } else {
           const int64_t slot = (head0 + h) * p.max_splits + split;
           p.ws_o[slot * D + d] = ov[h];
           if (d == 0) {
-            p.ws_ml[slot * 2 + 0] = m_run[h];
+            p.ws_ml[slot * 2 + 0] = m_ref[h];
             p.ws_ml[slot * 2 + 1] = l_cta[h];
           }
         }
@@ -472,6 +510,7 @@ int dispatch_nrep(int nrep, const CUtensorMap& tkv, const DecodeParams& prm, int
 int effective_split(int page_size, int pages_per_split) {
   const int tp = kTile / page_size;
   if (pages_per_split <= 0) pages_per_split = tp;
+  pages_per_split = std::min(pages_per_split, DCfg<64>::kMaxSplitPages);
   return ((pages_per_split + tp - 1) / tp) * tp;
 }
 
