@@ -66,13 +66,14 @@ def make_lens(n=N_SEQS):
 
 
 def decode_bytes(seq_lens: np.ndarray) -> int:
-    """Algorithmic bytes of one decode launch (K+V read once, Q in, O out, page ids, lens/indptr)."""
+    """Algorithmic bytes of one decode (K+V read once, Q in, O out, page ids, lens/indptr)."""
     pages = np.ceil(seq_lens / PS).astype(np.int64)
     return int(seq_lens.sum() * B_TOK + N_SEQS * HQ * D * 2 * 2 + 4 * pages.sum() + 8 * N_SEQS)
 
 
 def append_bytes(n_tok: int) -> int:
-    return int(2 * n_tok * HKV * D * 2 + 8 * n_tok)
+    """Algorithmic bytes of appending n_tok tokens (read new K/V, write them into pages)."""
+    return int(2 * n_tok * HKV * D * 2)
 
 
 # ----------------------------------------------------------------- clocks
@@ -227,84 +228,86 @@ def step_inputs(st, step: int, device):
 def run_ours(args, rank, world, local, pg):
     import torch
 
-    from mitten_b200 import _lib, paged
+    from mitten_b200 import paged
 
     device = torch.device("cuda", local)
     total_steps = args.warmup + args.steps
     st = build_state(total_steps + 1, device)
     pool = st["pool"]
-    split = paged.default_split(pool, N_SEQS, int(st["indptr_np"][-1]), st["max_pages"], HQ)
-    ws = paged.DecodeWorkspace.for_shape(pool, N_SEQS, HQ, st["max_pages"], split)
+    ws = paged.DecodeWorkspace.for_shape(pool, N_SEQS, HQ)
     gen = st["gen"]
     q_all = torch.randn((total_steps, N_SEQS, HQ, D), generator=gen, device=device).to(torch.bfloat16)
     k_all = torch.randn((total_steps, N_SEQS, HKV, D), generator=gen, device=device).to(torch.bfloat16)
     v_all = torch.randn((total_steps, N_SEQS, HKV, D), generator=gen, device=device).to(torch.bfloat16)
-    slots_np, lens_np = zip(*[step_inputs(st, i, device) for i in range(total_steps)])
-    slots_all = torch.from_numpy(np.stack(slots_np)).to(device)
+    lens_np = [step_inputs(st, i, device)[1] for i in range(total_steps)]
     lens_all = torch.from_numpy(np.stack(lens_np)).to(device)
     out = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    stream = torch.cuda.current_stream()
     scale = D ** -0.5
 
-    def step(i, ev=None):
-        if ev is not None:
-            ev[0].record(stream)
-        pool.append(0, k_all[i], v_all[i], slots_all[i])
-        if ev is not None:
-            ev[1].record(stream)
-        paged.paged_decode(pool, 0, q_all[i], st["indptr"], st["indices"], lens_all[i], st["max_pages"],
-                           scale=scale, phantom=False, pages_per_split=split, out=out, workspace=ws)
-        if ev is not None:
-            ev[2].record(stream)
+    def step(i):
+        # One launch: append this step's K/V at position len-1, then decode.
+        paged.paged_decode(pool, 0, q_all[i], st["indptr"], st["indices"], lens_all[i], scale=scale,
+                           phantom=False, k_new=k_all[i], v_new=v_all[i], out=out, workspace=ws)
 
-    # correctness spot-check of the last warm-up step happens in tests; here: run warm-up
-    for i in range(args.warmup):
+    for i in range(args.warmup):  # also configures the kernel before capture
         flush.zero_()
         step(i)
+    torch.cuda.synchronize()
+    graphs = []
+    for j in range(args.steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(args.warmup + j)
+        graphs.append(g)
+    torch.cuda.synchronize()
     barrier(pg)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    stream = torch.cuda.current_stream()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         barrier(pg)
         for j in range(args.steps):
             flush.zero_()
-            step(args.warmup + j, evs[j])
+            evs[j][0].record(stream)
+            graphs[j].replay()
+            evs[j][1].record(stream)
         torch.cuda.synchronize()
     barrier(pg)
-    t_append = [evs[j][0].elapsed_time(evs[j][1]) * 1e-3 for j in range(args.steps)]
-    t_decode = [evs[j][1].elapsed_time(evs[j][2]) * 1e-3 for j in range(args.steps)]
-    t_step = sum(t_append) + sum(t_decode)
+    t_decode = [evs[j][0].elapsed_time(evs[j][1]) * 1e-3 for j in range(args.steps)]
+    t_step = sum(t_decode)
     code, detail = paged.device_error(local)
     if code:
         raise SystemExit(f"device error {code} (detail {detail}) during the bench")
-    dec_bytes = [decode_bytes(lens_np[args.warmup + j].astype(np.int64)) for j in range(args.steps)]
+    dec_bytes = [decode_bytes(lens_np[args.warmup + j].astype(np.int64)) + append_bytes(N_SEQS)
+                 for j in range(args.steps)]
     kv_bytes = sum(int(lens_np[args.warmup + j].sum()) * B_TOK for j in range(args.steps))
+    del graphs
 
     # ---- e2e through the C ABI with pinned host buffers
-    e2e = run_e2e(args, st, pool, split, ws, device, stream, total_steps)
+    e2e = run_e2e(args, st, pool, ws, device, stream, total_steps)
 
     t_max = max_over_ranks(pg, t_step)
-    dec_max = max_over_ranks(pg, sum(t_decode))
     tokens = sum_over_ranks(pg, float(N_SEQS * args.steps))
     e2e_t = max_over_ranks(pg, e2e["t"])
     e2e_tokens = sum_over_ranks(pg, float(N_SEQS * e2e["steps"]))
     peaks = load_peaks()
-    achieved = (sum(dec_bytes) / len(dec_bytes)) / (sum(t_decode) / len(t_decode)) / 1e9
+    achieved = (sum(dec_bytes) / len(dec_bytes)) / (t_step / len(t_decode)) / 1e9
     res = {
         "metric": METRIC, "value": tokens / t_max, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q/K/V)",
-        "config": workload_config({"parallelism": f"replicas{world}", "pages_per_split": split}),
+        "config": workload_config({"parallelism": f"replicas{world}",
+                                   "step": "one fused append+decode launch, replayed from a CUDA graph"}),
         "kv_read_gbs": sum_over_ranks(pg, kv_bytes) / t_max / 1e9,
-        "decode_us_per_step": 1e6 * dec_max / args.steps,
-        "append_us_per_step": 1e6 * sum(t_append) / args.steps,
-        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<64,7>", "achieved": achieved,
+        "decode_us_per_step": 1e6 * t_step / args.steps,
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<64,7> (append fused)", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_source": peaks["source"], "traffic": traffic_from_profile(),
                      "algorithmic_bytes_per_launch": sum(dec_bytes) / len(dec_bytes)},
         "e2e": {"value": e2e_tokens / e2e_t, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
-                "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"]},
-        "gpu_launches": 2 * args.steps,
+                "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
+                "path": "pinned host Q/K/V/seq_lens -> H2D -> mtn_paged_decode (C ABI) -> D2H output, per step"},
+        "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -312,7 +315,7 @@ def run_ours(args, rank, world, local, pg):
     return res
 
 
-def run_e2e(args, st, pool, split, ws, device, stream, total_steps):
+def run_e2e(args, st, pool, ws, device, stream, total_steps):
     """Append + decode through the C ABI with host inputs/outputs copied inside the timed region."""
     import ctypes as C
 
@@ -328,45 +331,48 @@ def run_e2e(args, st, pool, split, ws, device, stream, total_steps):
     k_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
     v_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
     o_h = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory()
-    slot_h = [torch.from_numpy(step_inputs(st, i, device)[0]).pin_memory() for i in range(total_steps)]
     len_h = [torch.from_numpy(step_inputs(st, i, device)[1]).pin_memory() for i in range(total_steps)]
     q_d, k_d, v_d = (torch.empty_like(x, device=device) for x in (q_h, k_h, v_h))
     o_d = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
-    s_d = torch.empty(N_SEQS, dtype=torch.int64, device=device)
     l_d = torch.empty(N_SEQS, dtype=torch.int32, device=device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    sp = int(stream.cuda_stream)
     scale = D ** -0.5
 
     def one(i):
+        sp = int(torch.cuda.current_stream().cuda_stream)
         q_d.copy_(q_h, non_blocking=True)
         k_d.copy_(k_h, non_blocking=True)
         v_d.copy_(v_h, non_blocking=True)
-        s_d.copy_(slot_h[i], non_blocking=True)
         l_d.copy_(len_h[i], non_blocking=True)
-        _lib.check(lib.mtn_kv_append(C.byref(pool.layout), 0, k_d.data_ptr(), v_d.data_ptr(), _lib.MTN_DTYPE_BF16,
-                                     HKV * D, s_d.data_ptr(), N_SEQS, sp))
         _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_d.data_ptr(), _lib.MTN_DTYPE_BF16,
-                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
-                                        st["indices"].data_ptr(), l_d.data_ptr(), st["max_pages"], split, scale, 0,
-                                        ws.buf.data_ptr(), ws.nbytes, sp))
+                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, k_d.data_ptr(), v_d.data_ptr(),
+                                        _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
+                                        st["indices"].data_ptr(), l_d.data_ptr(), scale, 0, ws.buf.data_ptr(),
+                                        ws.nbytes, sp))
         o_h.copy_(o_d, non_blocking=True)
 
-    # the pool already holds warm-up + timed appends of the device arm: rewrite the same slots
+    # the pool already holds the device arm's appends: these steps rewrite the same positions
     for i in range(min(3, total_steps)):
         one(i)
     torch.cuda.synchronize()
+    graphs = []
+    for j in range(steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            one(j % total_steps)
+        graphs.append(g)
+    torch.cuda.synchronize()
     t = 0.0
     for j in range(steps):
-        i = j % total_steps
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        one(i)
+        graphs[j].replay()
         b.record(stream)
         b.synchronize()
         t += a.elapsed_time(b) * 1e-3
-    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, slot_h[0], len_h[0]))
+    del graphs
+    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, len_h[0]))
     d2h = o_h.numel() * o_h.element_size()
     return {"t": t, "steps": steps, "h2d": h2d, "d2h": d2h}
 

@@ -148,27 +148,28 @@ MTN_API int mtn_kv_gather(const mtn_kv_layout* pool, int32_t layer,
                   const int32_t* seq_lens, const int64_t* out_offsets, int32_t n_seqs,
                   void* out_k, void* out_v, int64_t total_tokens, void* stream);
 
-/* Paged decode attention (one query token per sequence), split-KV.
+/* Paged decode attention (one query token per sequence) with the step's KV
+ * append fused in (tcgen05 tensor cores, persistent split-KV).
  *   q: [n_seqs][num_q_heads][head_dim] (q_dtype), o: same shape (o_dtype).
  *   Sequence r reads pages kv_indices[kv_indptr[r] .. kv_indptr[r+1]) and its
- *   first seq_lens[r] tokens (the query's own K/V already appended).
- *   q head h uses kv head h / (num_q_heads / num_kv_heads) (model.rs:398-408).
- *   scale multiplies q.k (model.rs:298, 413).
- *   pages_per_split: KV pages per CTA (0 = choose from max_pages_per_seq);
- *   the workspace must hold mtn_paged_decode_workspace_bytes(...) bytes and
- *   must be zeroed once before its first use (the kernels leave it reusable).
- *   Concurrent calls must not share a workspace. */
+ *   first seq_lens[r] tokens.
+ *   k_new / v_new (both or neither; new_dtype): [n_seqs][num_kv_heads][head_dim]
+ *   rows of the token each sequence appends this step.  When given, the
+ *   kernel first stores them at position seq_lens[r]-1 (the paged form of
+ *   the Tensor::cat at qwen model.rs:390-392), then attends over them; when
+ *   NULL the cache must already hold seq_lens[r] tokens.
+ *   q head h uses kv head h / (num_q_heads / num_kv_heads) (model.rs:398-408),
+ *   at most 8 query heads per kv head.  scale multiplies q.k (model.rs:298, 413).
+ *   workspace: mtn_paged_decode_workspace_bytes(...) bytes, zeroed once before
+ *   first use (calls leave it reusable); concurrent calls must not share one.
+ *   The pool memory must have been zero-initialised (mtn_kv_pool_alloc does). */
 MTN_API size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads,
-                                        int32_t head_dim, int32_t max_pages_per_seq,
-                                        int32_t pages_per_split);
-MTN_API int32_t mtn_paged_decode_default_split(const mtn_kv_layout* pool, int32_t n_seqs,
-                                       int64_t total_pages, int32_t max_pages_per_seq,
-                                       int32_t num_q_heads);
+                                        int32_t head_dim);
 MTN_API int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer,
                      const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
+                     const void* k_new, const void* v_new, int32_t new_dtype,
                      int32_t n_seqs, int32_t num_q_heads,
                      const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
-                     int32_t max_pages_per_seq, int32_t pages_per_split,
                      float scale, uint32_t flags,
                      void* workspace, size_t workspace_bytes, void* stream);
 

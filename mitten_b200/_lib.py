@@ -86,12 +86,11 @@ SIGNATURES: dict[str, tuple] = {
     "mtn_page_copy": (C.c_int, [C.POINTER(KvLayout), C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
     "mtn_kv_gather": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
-    "mtn_paged_decode_workspace_bytes": (C.c_size_t, [C.c_int32] * 6),
-    "mtn_paged_decode_default_split": (C.c_int32, [C.POINTER(KvLayout), C.c_int32, C.c_int64, C.c_int32,
-                                                   C.c_int32]),
+    "mtn_paged_decode_workspace_bytes": (C.c_size_t, [C.c_int32] * 4),
     "mtn_paged_decode": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
-                                   C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
-                                   C.c_float, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p]),
+                                   C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p, C.c_size_t,
+                                   C.c_void_p]),
     "mtn_paged_prefill_workspace_bytes": (C.c_size_t, [C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int32]),
     "mtn_paged_prefill": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
                                     C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -1,32 +1,44 @@
-// Paged GQA/MQA decode attention for sm_100a (one query token per sequence).
+// Paged GQA/MQA decode attention for sm_100a (one query token per sequence),
+// with the step's KV append fused in.
 //
-// Replaces the decode-step attention of qwen model.rs:394-416: GQA head
-// mapping h -> h / n_rep (model.rs:398-408), scores q.k * scale
-// (model.rs:298, 413), softmax over every key including the reference's
-// all-zero first row (model.rs:207-220, flag MTN_ATTN_PHANTOM_ZERO_SLOT),
-// output P.V (model.rs:416).  One query token sees every key, so
-// generate_causal_mask (model.rs:542-555) masks nothing here.
+// Replaces the decode step of qwen model.rs:390-416: the new K/V row is
+// stored at position seq_len-1 (the paged form of the Tensor::cat at
+// model.rs:390-392), then q head h attends over every key of KV head
+// h / n_rep (model.rs:398-408) with scores q.k * scale (model.rs:298, 413),
+// softmax over all keys including the reference's all-zero first row
+// (model.rs:207-220, flag MTN_ATTN_PHANTOM_ZERO_SLOT) and output P.V
+// (model.rs:416).  One query token sees every key, so generate_causal_mask
+// (model.rs:542-555) masks nothing here.
 //
-// Design.  The step is HBM-bound (every K/V byte is read once) but at GQA
-// n_rep = 7 the arithmetic is 3.5 FMA per byte, more than the CUDA cores can
+// Design.  The step is HBM-bound (each K/V byte is read once) but at
+// n_rep = 7 the arithmetic is 3.5 FMA per byte, more than the CUDA cores
 // issue at HBM speed, so both contractions run on the tensor cores with the
-// n_rep query heads of one KV head as the narrow N dimension:
-//   S^T[128 tokens][16] = K_tile[128][D] . Q^T            (tcgen05, M=128, N=16)
-//   O^T[D][16]         += V_tile^T[D][128] . P^T[128][16] (tcgen05, M=D (64|128), N=16)
-// grid = (split, kv head, sequence); a CTA owns `pages_per_split` pages of
-// one sequence for one KV head.  6 warps:
+// query heads of one KV head as the narrow N dimension:
+//   S^T[128 tokens][16] = K_tile[128][D] . Q^T            (tcgen05, M = 128, N = 16)
+//   O^T[D][16]         += V_tile^T[D][128] . P^T[128][16] (tcgen05, M = 64 | 128, N = 16)
+// Persistent grid: SMs x CTAs-per-SM CTAs.  The (sequence, kv head)
+// segments are cut into 128-token tiles, laid end to end, and every CTA
+// takes an equal contiguous range of tiles (computed on the device from
+// seq_lens), so the producer streams TMA loads across segment boundaries
+// without bubbles.  6 warps per CTA:
 //   warps 0-3  softmax: TMEM lane = token; online softmax in the exp2 domain
-//              with a CTA-wide running max per query head, P^T (bf16) written
-//              to shared memory, O^T rescaled in TMEM, epilogue.
-//   warp 4     TMA producer: each page of each 128-token tile is one 2-D box
-//              (page_size rows x 64 columns, 128B swizzle) straight from the
-//              block table into a STAGES-deep ring.
-//   warp 5     MMA issuer (one thread), completion through tcgen05.commit.
-// Splits of one sequence write (m, l, O) partials to the workspace; the last
-// CTA to arrive (atomic ticket, no spinning) merges them in split order, so
-// the result does not depend on CTA scheduling.  Every wait is bounded.
+//              against a CTA-wide reference max that moves only when a tile
+//              exceeds it by 2^8 (lazy rescale), P^T (bf16) to shared memory,
+//              segment epilogues.
+//   warp 4     producer: per segment the Q^T operand, per tile one TMA box
+//              per page per 64-wide head-dim block straight from the block
+//              table into a STAGES-deep ring, and the fused KV append.
+//   warp 5     MMA issuer (one thread); S^T double-buffered in TMEM so the
+//              next tile's QK^T overlaps this tile's softmax; O^T
+//              double-buffered per segment so an epilogue overlaps the next
+//              segment.
+// A segment cut by a CTA boundary leaves (m, l, O) partials in per-CTA
+// workspace slots; the last CTA to finish one (atomic ticket, no spinning)
+// merges them in CTA order, so results do not depend on scheduling.  Every
+// wait is bounded.
 #include <algorithm>
 #include <cfloat>
+#include <cstring>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -39,27 +51,33 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kTile = 128;    // tokens per tile = MMA1 M = TMEM lanes
 constexpr int kThreads = 192;
 constexpr int kN = 16;        // query heads per KV head, padded (MMA N)
+// P is exponentiated against a reference max that moves only when a tile's
+// max exceeds it by more than 2^8, so P <= 256 and O^T is rarely rescaled.
+constexpr float kRescaleLog2 = 8.0f;
 
 struct DecodeParams {
   int64_t num_pages;
   int64_t row_k;  // pool-view row of (layer K, page 0, head 0, token 0)
   int64_t row_v;
+  __nv_bfloat16* pool;  // for the fused append (generic stores)
   int hkv;
   int ps;
   int hq;
+  int n_seqs;
   const void* q;
   void* o;
   int q_f32;
   int o_f32;
+  const void* k_new;  // optional [n_seqs][hkv][D]
+  const void* v_new;
+  int new_f32;
   const int32_t* kv_indptr;
   const int32_t* kv_indices;
   const int32_t* seq_lens;
-  int pages_per_split;
-  int max_splits;
   float qscale;  // scale * log2(e)
   int phantom;
-  float* ws_o;           // [n_seqs][hq][max_splits][D]
-  float* ws_ml;          // [n_seqs][hq][max_splits][2]
+  float* ws_o;           // [ctas][2][16][D]
+  float* ws_ml;          // [ctas][2][16][2]
   unsigned int* ws_cnt;  // [n_seqs][hkv]
   int* err;
 };
@@ -67,37 +85,41 @@ struct DecodeParams {
 template <int D>
 struct DCfg {
   static constexpr int kDB = D / 64;                       // 64-wide head-dim blocks
-  static constexpr int kStages = D == 256 ? 1 : 2;
+  static constexpr int kStages = D == 256 ? 1 : 3;
+  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
   static constexpr int kQBytes = kN * D * 2;               // Q^T operand: 16 rows x D
   static constexpr int kKVBytes = kTile * D * 2;           // one of K or V per stage
   static constexpr int kPBytes = kN * kTile * 2;           // P^T operand: 16 rows x 128 tokens
-  static constexpr int kMaxSplitPages = 256;               // page ids staged per CTA
   // Small state first, then the 1 KiB-aligned operand area.
   static constexpr int kOffBar = 0;                        // 16 mbarriers
-  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort flag, last-CTA flag
-  static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums, [2] flags
-  static constexpr int kOffIdx = kOffRed + (2 * 4 * kN + 4 * kN + 16) * 4;
-  static constexpr int kSmallBytes = kOffIdx + kMaxSplitPages * 4;
-  static constexpr int kOffQ = 0;                          // relative to the aligned operand area
-  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort, last flag, start info
+  static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums
+  static constexpr int kOffScan = kOffRed + (2 * 4 * kN + 4 * kN) * 4;  // [6] warp totals
+  static constexpr int kSmallBytes = kOffScan + 64;
+  static constexpr int kOffQ = 0;                          // [2] relative to the aligned operand area
+  static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKVBytes;
   static constexpr int kOffP = kOffV + kStages * kKVBytes;
   static constexpr int kBigBytes = kOffP + kPBytes;
   static constexpr int kSmem = kSmallBytes + 1023 + kBigBytes;
   static constexpr int kMO = D == 64 ? 64 : 128;           // MMA2 M
-  static constexpr int kTmemS = 0;                          // 2 x 16 columns (double-buffered S^T)
-  static constexpr int kTmemO = 32;                         // 16 (D <= 128) or 32 (D = 256) columns
-  static constexpr int kTmemCols = 64;
+  static constexpr int kTmemS = 0;                          // [2] x 16 columns
+  static constexpr int kTmemO = 32;                         // [2] x 32 columns
+  static constexpr int kTmemCols = 128;
   static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KiB alignment");
 };
 
-// Lazy rescaling: P is exponentiated against a CTA-wide reference max that
-// only moves when a tile's max exceeds it by more than 2^kRescaleLog2, so
-// P <= 2^8 (exact in bf16 range) and O^T in TMEM is rarely touched.
-constexpr float kRescaleLog2 = 8.0f;
-
-enum Bar { kKVFull0 = 0, kKVFull1 = 1, kKVEmpty0 = 2, kKVEmpty1 = 3, kSFull0 = 4, kSFull1 = 5, kPFull = 6,
-           kODone = 7 };
+enum Bar {
+  kKVFull0 = 0,   // [3]
+  kKVEmpty0 = 3,  // [3]
+  kSFull0 = 6,    // [2]
+  kPFull = 8,
+  kODone = 9,
+  kQFull0 = 10,   // [2]
+  kQEmpty0 = 12,  // [2]
+  kOFree0 = 14,   // [2]
+  kNumBars = 16
+};
 
 // Final normalisation of one output element: o/l with the phantom key folded in.
 __device__ __forceinline__ float finalize(float o, float l, float m, int phantom) {
@@ -108,6 +130,11 @@ __device__ __forceinline__ float finalize(float o, float l, float m, int phantom
     o = o * a;
   }
   return l > 0.0f ? o / l : 0.0f;
+}
+
+__device__ __forceinline__ void store_out(const DecodeParams& p, int64_t idx, float v) {
+  if (p.o_f32) static_cast<float*>(p.o)[idx] = v;
+  else static_cast<__nv_bfloat16*>(p.o)[idx] = __float2bfloat16_rn(v);
 }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -135,201 +162,369 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+// Valid length of sequence s, clamped to its block table (an out-of-range
+// value records kDevErrBadSeqLen, from CTA 0 only).
+__device__ __forceinline__ int seq_len_of(const DecodeParams& p, int s) {
+  const int ntab = p.kv_indptr[s + 1] - p.kv_indptr[s];
+  const int len = p.seq_lens[s];
+  if (len < 0 || len > ntab * p.ps) {
+    if (blockIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
+    return min(max(len, 0), ntab * p.ps);
+  }
+  return len;
+}
+
+// Walks a CTA's tiles in order: (sequence s, kv head g, tile j of T).
+struct Walker {
+  int s, g, j, T, len, pbeg;
+  int64_t pre;  // tiles (in units of one kv head) of the sequences before s
+
+  __device__ void load(const DecodeParams& p) {
+    len = seq_len_of(p, s);
+    T = (len + kTile - 1) / kTile;
+    pbeg = p.kv_indptr[s];
+  }
+  __device__ void start(const DecodeParams& p, int s0, int64_t pre0, int64_t t0) {
+    s = s0;
+    pre = pre0;
+    load(p);
+    const int64_t off = t0 - pre * p.hkv;
+    g = static_cast<int>(off / T);
+    j = static_cast<int>(off - static_cast<int64_t>(g) * T);
+  }
+  // Only called while tiles remain, so a non-empty sequence follows.
+  __device__ void next(const DecodeParams& p) {
+    if (++j < T) return;
+    j = 0;
+    if (++g < p.hkv) return;
+    g = 0;
+    do {
+      pre += T;
+      ++s;
+      load(p);
+    } while (T == 0 && s + 1 < p.n_seqs);
+  }
+  __device__ int64_t seg_start(const DecodeParams& p) const { return pre * p.hkv + static_cast<int64_t>(g) * T; }
+};
+
+__device__ __forceinline__ int64_t tile_begin(int64_t c, int64_t U, int64_t C) { return c * U / C; }
+// The CTA whose tile range holds global tile x.
+__device__ __forceinline__ int64_t cta_of(int64_t x, int64_t U, int64_t C) {
+  return min(C - 1, ((x + 1) * C - 1) / U);
+}
+
 template <int D, int NREP>
-__global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ DecodeParams p) {
   using C = DCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + C::kOffBar);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem_raw + C::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 8);
+  int* start_s = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 12);
+  int64_t* start_pre = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 16);
+  int64_t* total_u = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 24);
   float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
   float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
-  int* idx_s = reinterpret_cast<int*>(smem_raw + C::kOffIdx);        // this split's page ids
+  int64_t* scan = reinterpret_cast<int64_t*>(smem_raw + C::kOffScan);  // [6]
   uint8_t* big = smem_raw + C::kSmallBytes;
   big += (1024 - (smem_u32(big) & 1023)) & 1023;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int split = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int64_t ctas = gridDim.x;
+  const int64_t cta = blockIdx.x;
 
-  const int pbeg = p.kv_indptr[s];
-  const int ntab = p.kv_indptr[s + 1] - pbeg;
-  int seq_len = p.seq_lens[s];
-  if (seq_len < 0 || seq_len > ntab * p.ps) {
-    if (split == 0 && g == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
-    seq_len = min(max(seq_len, 0), ntab * p.ps);
+  // ------------------------------------------------------------ work split
+  // Tiles per sequence (for one kv head), prefix-summed over the CTA; each
+  // thread owns a contiguous chunk of sequences.
+  const int chunk = (p.n_seqs + kThreads - 1) / kThreads;
+  const int sb = min(p.n_seqs, tid * chunk), se = min(p.n_seqs, sb + chunk);
+  int64_t mine = 0;
+  for (int s = sb; s < se; ++s) {
+    const int len = seq_len_of(p, s);
+    const int T = (len + kTile - 1) / kTile;
+    mine += T;
+    if (T == 0 && s % ctas == cta) {
+      // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
+      const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
+      for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
+    }
   }
-  int npages = (seq_len + p.ps - 1) / p.ps;
-  if (npages > p.max_splits * p.pages_per_split) {
-    // More pages than max_pages_per_seq promised: the grid and the workspace
-    // only cover max_splits splits, so attend to the covered prefix only.
-    if (split == 0 && g == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
-    npages = p.max_splits * p.pages_per_split;
-    seq_len = npages * p.ps;
+  int64_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
   }
-  const int n_splits = max(1, (npages + p.pages_per_split - 1) / p.pages_per_split);
-  if (split >= n_splits) return;
-  const int pg0 = split * p.pages_per_split;
-  const int pg1 = min(npages, pg0 + p.pages_per_split);
-  const int tok_begin = pg0 * p.ps;
-  const int ntok = max(0, min(seq_len, pg1 * p.ps) - tok_begin);
-  const int ntiles = (ntok + kTile - 1) / kTile;
-  const int tile_pages = kTile / p.ps;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == kPFull ? 128 : 1);
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(&bars[i], (i == kPFull || i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
     *abort_flag = 0;
+    *start_s = -1;
     fence_barrier_init();
   }
+  if (lane == 31) scan[warp] = incl;
   __syncthreads();
+  int64_t before = incl - mine;
+  for (int w = 0; w < warp; ++w) before += scan[w];
+  int64_t total_seq_tiles = 0;
+  for (int w = 0; w < kThreads / 32; ++w) total_seq_tiles += scan[w];
+  const int64_t U = total_seq_tiles * p.hkv;
+  const int64_t t0 = U > 0 ? tile_begin(cta, U, ctas) : 0;
+  const int64_t t1 = U > 0 ? tile_begin(cta + 1, U, ctas) : 0;
+  const int n_local = static_cast<int>(t1 - t0);
+  if (n_local > 0 && t0 >= before * p.hkv && t0 < (before + mine) * p.hkv) {
+    int64_t pre = before;
+    for (int s = sb; s < se; ++s) {
+      const int T = (seq_len_of(p, s) + kTile - 1) / kTile;
+      if (t0 < (pre + T) * p.hkv) {
+        *start_s = s;
+        *start_pre = pre;
+        break;
+      }
+      pre += T;
+    }
+  }
+  if (tid == 0) *total_u = U;
+  __syncthreads();
+  if (n_local == 0) return;  // uniform over the CTA; nothing allocated yet
+  if (*start_s < 0 || *start_s >= p.n_seqs) {  // cannot happen for consistent metadata
+    if (tid == 0) record_error(p.err, kDevErrBadSeqLen, -1);
+    return;
+  }
+
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  uint8_t* p_s = big + C::kOffP;
+  {
+    uint4* pz = reinterpret_cast<uint4*>(p_s);  // rows >= NREP of P^T stay zero
+    for (int e = tid; e < C::kPBytes / 16; e += kThreads) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_shared();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+  const int s0 = *start_s;
+  const int64_t pre0 = *start_pre;
+  const int tile_pages = kTile / p.ps;
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
-    // Stage the split's page ids once (one coalesced round trip), then every
-    // tile's boxes are issued by tile_pages lanes in parallel.
-    for (int i = lane; i < pg1 - pg0; i += 32) {
-      int64_t page = p.kv_indices[pbeg + pg0 + i];
-      if (page < 0 || page >= p.num_pages) {
-        record_error(p.err, kDevErrBadPage, s);
-        page = 0;
-      }
-      idx_s[i] = static_cast<int>(page);
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_kv);
+      if (!p.q_f32) tc::prefetch_tmap(&tm_q);
     }
-    __syncwarp();
-    if (lane == 0) tc::prefetch_tmap(&tm_kv);
-    for (int j = 0; j < ntiles; ++j) {
-      const int st = j % C::kStages;
-      if (j >= C::kStages) {
-        bool free_ok = true;
-        if (lane == 0) free_ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((j / C::kStages) - 1) & 1, abort_flag, p.err, 10);
-        if (!__shfl_sync(0xffffffffu, free_ok, 0)) break;  // warp-uniform
+    Walker w;
+    w.start(p, s0, pre0, t0);
+    int qcnt = 0;
+    for (int i = 0; i < n_local; ++i) {
+      const bool first = (i == 0) || w.j == 0;
+      if (first) {
+        const int qb = qcnt & 1;
+        if (qcnt >= 2) {
+          bool ok = true;
+          if (lane == 0) ok = tc::wait_bounded(&bars[kQEmpty0 + qb], ((qcnt >> 1) - 1) & 1, abort_flag, p.err, 11);
+          if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        uint8_t* q_s = big + C::kOffQ + qb * C::kQBytes;
+        const int qrow = w.s * p.hq + w.g * NREP;
+        if (!p.q_f32) {
+          // Rows past NREP belong to other heads (or lie past the end and
+          // read as zero): their S^T columns are never used.
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bars[kQFull0 + qb], C::kQBytes);
+#pragma unroll
+            for (int b = 0; b < C::kDB; ++b)
+              tc::tma_load_3d(q_s + b * (kN * 128), &tm_q, b * 64, 0, qrow, &bars[kQFull0 + qb]);
+          }
+        } else {
+          for (int e = lane; e < NREP * (D / 8); e += 32) {
+            const int r = e / (D / 8), c = e - r * (D / 8);
+            const float* src = static_cast<const float*>(p.q) + (static_cast<int64_t>(qrow) + r) * D + c * 8;
+            const float4 a = *reinterpret_cast<const float4*>(src);
+            const float4 b2 = *reinterpret_cast<const float4*>(src + 4);
+            *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+                make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(b2.x, b2.y), f2_to_bf2(b2.z, b2.w));
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bars[kQFull0 + qb]);
+        }
+        ++qcnt;
+      }
+      const int st = i % C::kStages;
+      if (i >= C::kStages) {
+        bool ok = true;
+        if (lane == 0)
+          ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((i / C::kStages) - 1) & 1, abort_flag, p.err, 10);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      const int npg = (w.len + p.ps - 1) / p.ps;
+      if (p.k_new != nullptr && w.j == w.T - 1) {
+        // Fused KV append: store this step's row at position len-1, then
+        // order it before the async-proxy (TMA) read of the same page.
+        const int pos = w.len - 1;
+        int64_t page = p.kv_indices[w.pbeg + pos / p.ps];
+        if (page < 0 || page >= p.num_pages) {
+          record_error(p.err, kDevErrBadPage, w.s);
+          page = -1;
+        }
+        if (page >= 0 && lane < D / 8) {
+          const int64_t src = (static_cast<int64_t>(w.s) * p.hkv + w.g) * D + lane * 8;
+          uint4 kk, vv;
+          if (p.new_f32) {
+            const float* kf = static_cast<const float*>(p.k_new) + src;
+            const float* vf = static_cast<const float*>(p.v_new) + src;
+            const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
+            const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
+            kk = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
+                            f2_to_bf2(k1.z, k1.w));
+            vv = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
+                            f2_to_bf2(v1.z, v1.w));
+          } else {
+            kk = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
+            vv = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
+          }
+          const int64_t rowoff = (page * p.hkv + w.g) * p.ps + pos % p.ps;
+          *reinterpret_cast<uint4*>(p.pool + (p.row_k + rowoff) * D + lane * 8) = kk;
+          *reinterpret_cast<uint4*>(p.pool + (p.row_v + rowoff) * D + lane * 8) = vv;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        __syncwarp();
       }
       if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
       __syncwarp();
       if (lane < tile_pages) {
-        // Past the split's last page: reload that page (finite data, masked).
-        const int pi = lane;
-        const int64_t page = idx_s[min(j * tile_pages + pi, pg1 - pg0 - 1)];
-        const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
-        const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
+        // Past the sequence's last page: reload that page (finite data, masked).
+        int64_t page = p.kv_indices[w.pbeg + min(w.j * tile_pages + lane, npg - 1)];
+        if (page < 0 || page >= p.num_pages) {
+          record_error(p.err, kDevErrBadPage, w.s);
+          page = 0;
+        }
+        const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
+        const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
         uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
         uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
 #pragma unroll
         for (int b = 0; b < C::kDB; ++b) {
-          const int off = b * kTile * 128 + pi * p.ps * 128;
+          const int off = b * kTile * 128 + lane * p.ps * 128;
           tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
           tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
         }
       }
+      if (i + 1 < n_local) w.next(p);
     }
-  } else {
-    // Everyone else: TMEM, the Q^T operand (16 rows, rows >= NREP zero, 128B
-    // swizzled K-major) and a zeroed P^T operand (rows >= NREP stay zero),
-    // overlapping the producer's first loads.
-    if (warp == 0) {
-      tc::tmem_alloc(tmem_base_s, C::kTmemCols);
-      tc::tmem_relinquish();
-    }
-    const int tid = warp == 5 ? 128 + lane : threadIdx.x;  // 0..159
-    uint8_t* q_s = big + C::kOffQ;
-    const int64_t qrow0 = static_cast<int64_t>(s) * p.hq + g * NREP;
-    for (int e = tid; e < kN * (D / 8); e += 160) {
-      const int r = e / (D / 8), c = e - r * (D / 8);
-      const int b = c >> 3, cc = c & 7;
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (r < NREP) {
-        const int64_t off = (qrow0 + r) * D + c * 8;
-        if (p.q_f32) {
-          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off);
-          const float4 bb = *(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off) + 1);
-          w = make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(bb.x, bb.y), f2_to_bf2(bb.z, bb.w));
-        } else {
-          w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + off);
-        }
-      }
-      *reinterpret_cast<uint4*>(q_s + b * (kN * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
-    }
-    uint4* pz = reinterpret_cast<uint4*>(big + C::kOffP);
-    for (int e = tid; e < C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
-    fence_proxy_async_shared();
-    tc::fence_before_sync();
-    tc::named_sync(2, 160);
-    tc::fence_after_sync();
-  }
-  const uint32_t tmem = *tmem_base_s;  // valid for every role past named barrier 2
-
-  if (warp == 5) {
+  } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kTile, kN, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(C::kMO, kN, false, true);
-      const uint32_t q_s = smem_u32(big + C::kOffQ);
-      const uint32_t p_s = smem_u32(big + C::kOffP);
-      // S^T(j) = K_j Q^T into S buffer j&1: both operands K-major; 16-wide k
-      // steps walk 32 bytes inside a 128-byte swizzle row, then the next block.
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % C::kStages;
-        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j / C::kStages) & 1, abort_flag, p.err, 20)) return false;
+      const uint32_t p_addr = smem_u32(p_s);
+      Walker wsw, wo;  // wsw: tiles whose S^T is issued; wo: tiles whose O^T is issued
+      wsw.start(p, s0, pre0, t0);
+      wo.start(p, s0, pre0, t0);
+      int q_seg = -1;  // segment counter of the S^T issue
+      int o_seg = -1;  // segment counter of the O^T issue
+      // S^T(i) = K_i Q^T into S buffer i&1: both operands K-major; 16-wide
+      // k steps walk 32 bytes inside a 128-byte swizzle row, then the next block.
+      auto issue_s = [&](int i) -> bool {
+        const bool first = (i == 0) || wsw.j == 0;
+        const bool last = (i == n_local - 1) || wsw.j == wsw.T - 1;
+        if (first) {
+          ++q_seg;
+          if (!tc::wait_bounded(&bars[kQFull0 + (q_seg & 1)], (q_seg >> 1) & 1, abort_flag, p.err, 22)) return false;
+        }
+        const int st = i % C::kStages;
+        if (!tc::wait_bounded(&bars[kKVFull0 + st], (i / C::kStages) & 1, abort_flag, p.err, 20)) return false;
         tc::fence_after_sync();
         const uint32_t k_s = smem_u32(big + C::kOffK + st * C::kKVBytes);
+        const uint32_t q_s = smem_u32(big + C::kOffQ + (q_seg & 1) * C::kQBytes);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint64_t a = tc::sdesc_sw128(k_s + (k >> 2) * kTile * 128 + (k & 3) * 32, 16, 1024);
           const uint64_t b = tc::sdesc_sw128(q_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
-          tc::mma_bf16(tmem + C::kTmemS + (j & 1) * kN, a, b, idS, k > 0 ? 1u : 0u);
+          tc::mma_bf16(tmem + C::kTmemS + (i & 1) * kN, a, b, idS, k > 0 ? 1u : 0u);
         }
-        tc::mma_commit(&bars[kSFull0 + (j & 1)]);
+        tc::mma_commit(&bars[kSFull0 + (i & 1)]);
+        if (last) tc::mma_commit(&bars[kQEmpty0 + (q_seg & 1)]);
+        if (i + 1 < n_local) wsw.next(p);
         return true;
       };
-      bool ok = ntiles == 0 || issue_s(0);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        // Overlap the next tile's S with this tile's softmax (its S buffer was
-        // released by the softmax of tile j-1, already waited on below).  With
-        // a single K/V stage the next tile only lands after this P V.
-        if (C::kStages > 1 && j + 1 < ntiles && !issue_s(j + 1)) break;
-        if (!tc::wait_bounded(&bars[kPFull], j & 1, abort_flag, p.err, 21)) break;
+      bool ok = issue_s(0);
+      for (int i = 0; ok && i < n_local; ++i) {
+        // Overlap the next tile's S^T with this tile's softmax (its S buffer
+        // was released by the softmax of tile i-1, waited on below).  With a
+        // single K/V stage the next tile only lands after this P V.
+        if (C::kStages > 1 && i + 1 < n_local && !issue_s(i + 1)) break;
+        const bool first = (i == 0) || wo.j == 0;
+        if (first) {
+          ++o_seg;
+          if (o_seg >= 2 &&
+              !tc::wait_bounded(&bars[kOFree0 + (o_seg & 1)], ((o_seg >> 1) - 1) & 1, abort_flag, p.err, 23))
+            break;
+        }
+        if (!tc::wait_bounded(&bars[kPFull], i & 1, abort_flag, p.err, 21)) break;
         tc::fence_after_sync();
-        const int st = j % C::kStages;
+        const int st = i % C::kStages;
         const uint32_t v_s = smem_u32(big + C::kOffV + st * C::kKVBytes);
+        const uint32_t o_col = C::kTmemO + (o_seg & 1) * 32;
         // O^T += V^T P^T: A = V^T (MN-major: head dim contiguous; 64-wide
         // blocks kTile*128 bytes apart), B = P^T (K-major over tokens).
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
-          const uint64_t b = tc::sdesc_sw128(p_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(p_addr + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
 #pragma unroll
           for (int mb = 0; mb < D / C::kMO; ++mb) {
             const uint64_t a =
                 tc::sdesc_sw128(v_s + mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128, kTile * 128, 1024);
-            tc::mma_bf16(tmem + C::kTmemO + mb * kN, a, b, idO, (j > 0 || k > 0) ? 1u : 0u);
+            tc::mma_bf16(tmem + o_col + mb * kN, a, b, idO, (!first || k > 0) ? 1u : 0u);
           }
         }
         tc::mma_commit(&bars[kODone]);
         tc::mma_commit(&bars[kKVEmpty0 + st]);
-        if (C::kStages == 1 && j + 1 < ntiles && !issue_s(j + 1)) break;
+        if (i + 1 < n_local) wo.next(p);
+        if (C::kStages == 1 && i + 1 < n_local && !issue_s(i + 1)) break;
       }
     }
-  } else if (warp < 4) {
+  } else {
     // ------------------------------------------------------------ softmax
-    const int t = threadIdx.x;  // token row of the tile == TMEM lane
+    const int t = tid;  // token row of the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // Rows of O^T this thread holds: M=64 puts row d in lane (d % 16) + 32 (d / 16);
+    // M=128 puts row d in lane d; D = 256 uses two M=128 blocks 16 columns apart.
+    const bool holds = (C::kMO == 64) ? (lane < 16) : true;
+    const int d_base = (C::kMO == 64) ? warp * 16 + lane : warp * 32 + lane;
+    Walker w;
+    w.start(p, s0, pre0, t0);
     float m_ref[NREP], l_tok[NREP];
-#pragma unroll
-    for (int h = 0; h < NREP; ++h) {
-      m_ref[h] = -INFINITY;
-      l_tok[h] = 0.0f;
-    }
-    uint8_t* p_s = big + C::kOffP;
+    int seg = -1;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
+    for (int i = 0; i < n_local; ++i) {
+      const bool first = (i == 0) || w.j == 0;
+      const bool last = (i == n_local - 1) || w.j == w.T - 1;
+      if (first) {
+        ++seg;
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+          m_ref[h] = -INFINITY;
+          l_tok[h] = 0.0f;
+        }
+      }
+      const uint32_t o_col = C::kTmemO + (seg & 1) * 32;
+      ok = tc::wait_bounded(&bars[kSFull0 + (i & 1)], (i >> 1) & 1, abort_flag, p.err, 30);
       if (!ok) break;
       tc::fence_after_sync();
       float sv[16];
-      tmem_ld16(lane_addr + C::kTmemS + (j & 1) * kN, sv);
-      const bool valid = j * kTile + t < ntok;
-      float* rm = red_max + (j & 1) * 4 * kN;
+      tmem_ld16(lane_addr + C::kTmemS + (i & 1) * kN, sv);
+      const bool valid = w.j * kTile + t < w.len;
+      float* rm = red_max + (i & 1) * 4 * kN;
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
         sv[h] = valid ? sv[h] * p.qscale : -INFINITY;
@@ -346,25 +541,24 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
         if (mt > m_ref[h] + kRescaleLog2 || m_ref[h] == -INFINITY) {  // CTA-uniform decision
           alpha[h] = (m_ref[h] == -INFINITY) ? 0.0f : exp2f(m_ref[h] - mt);
           m_ref[h] = mt;  // finite: every tile holds a valid token
-          rescale |= j > 0;
+          rescale |= !first;
         }
         sv[h] = exp2f(sv[h] - m_ref[h]);  // masked tokens: exp2(-inf) = 0
         l_tok[h] = l_tok[h] * alpha[h] + sv[h];
       }
-      if (j > 0) {
-        // The P^T buffer (and O^T, when rescaling) is busy until the
-        // previous P V finishes.
-        ok = tc::wait_bounded(&bars[kODone], (j - 1) & 1, abort_flag, p.err, 31);
+      if (i > 0) {
+        // P^T (and O^T, when rescaling) is busy until the previous P V finishes.
+        ok = tc::wait_bounded(&bars[kODone], (i - 1) & 1, abort_flag, p.err, 31);
         if (!ok) break;
         tc::fence_after_sync();
         if (rescale) {
 #pragma unroll
           for (int mb = 0; mb < D / C::kMO; ++mb) {
             float ov[16];
-            tmem_ld16(lane_addr + C::kTmemO + mb * kN, ov);
+            tmem_ld16(lane_addr + o_col + mb * kN, ov);
 #pragma unroll
             for (int h = 0; h < NREP; ++h) ov[h] *= alpha[h];
-            tmem_st16(lane_addr + C::kTmemO + mb * kN, ov);
+            tmem_st16(lane_addr + o_col + mb * kN, ov);
           }
           tc::tmem_st_wait();
         }
@@ -382,88 +576,96 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
       fence_proxy_async_shared();
       tc::fence_before_sync();
       tc::mbar_arrive(&bars[kPFull]);
-    }
 
-    // ---- epilogue: l per head over the CTA; O^T rows of this thread's lane.
-    if (ok && ntiles > 0) ok = tc::wait_bounded(&bars[kODone], (ntiles - 1) & 1, abort_flag, p.err, 32);
-    tc::fence_after_sync();
-    const bool have_o = __all_sync(0xffffffffu, ok) && ntiles > 0;  // warp-uniform for tcgen05.ld
+      if (last) {
+        // ---- segment epilogue: O^T of (s, g) over this CTA's tiles.
+        ok = tc::wait_bounded(&bars[kODone], i & 1, abort_flag, p.err, 32);
+        tc::fence_after_sync();
+        if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform for tcgen05.ld
+        float ov[D / C::kMO][16];
 #pragma unroll
-    for (int h = 0; h < NREP; ++h) {
-      const float ws = warp_sum(l_tok[h]);
-      if (lane == 0) red_sum[warp * kN + h] = ws;
-    }
-    tc::named_sync(1, 128);
-    float l_cta[NREP];
+        for (int mb = 0; mb < D / C::kMO; ++mb) tmem_ld16(lane_addr + o_col + mb * kN, ov[mb]);
+        tc::fence_before_sync();
+        tc::mbar_arrive(&bars[kOFree0 + (seg & 1)]);  // O^T buffer reusable two segments on
 #pragma unroll
-    for (int h = 0; h < NREP; ++h)
-      l_cta[h] = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] + red_sum[3 * kN + h];
-
-    const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
-    // Rows of O^T this thread holds: M=64 puts row d in lane (d % 16) + 32 (d / 16);
-    // M=128 puts row d in lane d; D = 256 uses two M=128 blocks 16 columns apart.
-    const bool holds = (C::kMO == 64) ? (lane < 16) : true;
-    const int d_base = (C::kMO == 64) ? warp * 16 + lane : warp * 32 + lane;
-#pragma unroll
-    for (int mb = 0; mb < D / C::kMO; ++mb) {
-      float ov[16];
-      if (have_o) {
-        tmem_ld16(lane_addr + C::kTmemO + mb * kN, ov);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) ov[i] = 0.0f;
-      }
-      const int d = d_base + mb * 128;
-      if (!holds) continue;
-#pragma unroll
-      for (int h = 0; h < NREP; ++h) {
-        if (n_splits == 1) {
-          const float r = finalize(ov[h], l_cta[h], m_ref[h], p.phantom);
-          if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
-          else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
-        } else {
-          const int64_t slot = (head0 + h) * p.max_splits + split;
-          p.ws_o[slot * D + d] = ov[h];
-          if (d == 0) {
-            p.ws_ml[slot * 2 + 0] = m_ref[h];
-            p.ws_ml[slot * 2 + 1] = l_cta[h];
-          }
+        for (int h = 0; h < NREP; ++h) {
+          const float wsum = warp_sum(l_tok[h]);
+          if (lane == 0) red_sum[warp * kN + h] = wsum;
         }
-      }
-    }
-
-    if (n_splits > 1) {
-      // ---- split combine: the last CTA of (sequence, kv head) merges in split order.
-      __threadfence();
-      tc::named_sync(1, 128);
-      if (t == 0) {
-        const unsigned int ticket = atomicAdd(&p.ws_cnt[s * p.hkv + g], 1u);
-        *last_flag = (ticket == static_cast<unsigned int>(n_splits - 1)) ? 1 : 0;
-      }
-      tc::named_sync(1, 128);
-      if (*last_flag) {
-        __threadfence();
-        for (int e = t; e < NREP * D; e += 128) {
-          const int h = e / D, d = e - (e / D) * D;
-          const int64_t slot0 = (head0 + h) * p.max_splits;
-          float mall = -INFINITY;
-          for (int jj = 0; jj < n_splits; ++jj) mall = fmaxf(mall, ld_cg(p.ws_ml + (slot0 + jj) * 2));
-          float o = 0.0f, l = 0.0f;
-          if (mall != -INFINITY) {
-            for (int jj = 0; jj < n_splits; ++jj) {
-              const float mj = ld_cg(p.ws_ml + (slot0 + jj) * 2);
-              if (mj == -INFINITY) continue;
-              const float a = exp2f(mj - mall);
-              o += ld_cg(p.ws_o + (slot0 + jj) * D + d) * a;
-              l += ld_cg(p.ws_ml + (slot0 + jj) * 2 + 1) * a;
+        tc::named_sync(1, 128);
+        float l_cta[NREP];
+#pragma unroll
+        for (int h = 0; h < NREP; ++h)
+          l_cta[h] = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] + red_sum[3 * kN + h];
+        tc::named_sync(1, 128);  // red_sum is reused by the next segment
+        const int64_t head0 = static_cast<int64_t>(w.s) * p.hq + w.g * NREP;
+        const int64_t U = *total_u;
+        const int64_t s_start = w.seg_start(p);
+        const int64_t ca = cta_of(s_start, U, ctas), cb = cta_of(s_start + w.T - 1, U, ctas);
+        if (ca == cb) {
+          if (holds) {
+#pragma unroll
+            for (int mb = 0; mb < D / C::kMO; ++mb)
+#pragma unroll
+              for (int h = 0; h < NREP; ++h)
+                store_out(p, (head0 + h) * D + d_base + mb * 128,
+                          finalize(ov[mb][h], l_cta[h], m_ref[h], p.phantom));
+          }
+        } else {
+          // Partial: slot (cta, 0) if the segment is this CTA's first, else (cta, 1).
+          const int which = (cta == ca && t0 != s_start) ? 1 : 0;
+          const int64_t slot = (cta * 2 + which) * kN;
+          if (holds) {
+#pragma unroll
+            for (int mb = 0; mb < D / C::kMO; ++mb)
+#pragma unroll
+              for (int h = 0; h < NREP; ++h) p.ws_o[(slot + h) * D + d_base + mb * 128] = ov[mb][h];
+          }
+#pragma unroll
+          for (int h = 0; h < NREP; ++h) {
+            if (t == h) {  // static register indexing: one thread per head
+              p.ws_ml[(slot + h) * 2 + 0] = m_ref[h];
+              p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
-          const float r = finalize(o, l, mall, p.phantom);
-          if (p.o_f32) static_cast<float*>(p.o)[(head0 + h) * D + d] = r;
-          else static_cast<__nv_bfloat16*>(p.o)[(head0 + h) * D + d] = __float2bfloat16_rn(r);
+          __threadfence();
+          tc::named_sync(1, 128);
+          const int64_t seg_id = static_cast<int64_t>(w.s) * p.hkv + w.g;
+          if (t == 0) {
+            const unsigned int ticket = atomicAdd(&p.ws_cnt[seg_id], 1u);
+            *last_flag = (ticket == static_cast<unsigned int>(cb - ca)) ? 1 : 0;
+          }
+          tc::named_sync(1, 128);
+          if (*last_flag) {
+            // Merge the pieces in CTA order.
+            __threadfence();
+            const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
+            for (int e = t; e < NREP * D; e += 128) {
+              const int h = e / D, d = e - (e / D) * D;
+              float mall = -INFINITY;
+              for (int64_t cc = ca; cc <= cb; ++cc) {
+                const int64_t sl = (cc * 2 + (cc == ca ? wa : 0)) * kN + h;
+                mall = fmaxf(mall, ld_cg(p.ws_ml + sl * 2));
+              }
+              float o = 0.0f, l = 0.0f;
+              if (mall != -INFINITY) {
+                for (int64_t cc = ca; cc <= cb; ++cc) {
+                  const int64_t sl = (cc * 2 + (cc == ca ? wa : 0)) * kN + h;
+                  const float mj = ld_cg(p.ws_ml + sl * 2);
+                  if (mj == -INFINITY) continue;
+                  const float a = exp2f(mj - mall);
+                  o += ld_cg(p.ws_o + sl * D + d) * a;
+                  l += ld_cg(p.ws_ml + sl * 2 + 1) * a;
+                }
+              }
+              store_out(p, (head0 + h) * D + d, finalize(o, l, mall, p.phantom));
+            }
+            if (t == 0) p.ws_cnt[seg_id] = 0u;  // ready for the next launch on this workspace
+          }
+          tc::named_sync(1, 128);  // last_flag is reused by the next segment
         }
-        if (t == 0) p.ws_cnt[s * p.hkv + g] = 0u;  // ready for the next launch on this workspace
       }
+      if (i + 1 < n_local) w.next(p);
     }
   }
 
@@ -476,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
 }
 
 template <int D, int NREP>
-int launch_decode(const CUtensorMap& tkv, const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
+int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm, cudaStream_t stream) {
   using C = DCfg<D>;
   auto kern = paged_decode_kernel<D, NREP>;
   static bool configured[64] = {};
@@ -487,31 +689,31 @@ int launch_decode(const CUtensorMap& tkv, const DecodeParams& prm, int n_seqs, c
                  "cudaFuncSetAttribute(decode)");
     configured[dev] = true;
   }
-  dim3 grid(prm.max_splits, prm.hkv, n_seqs);
-  kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
+  const int grid = sm_count() * C::kCtasPerSm;
+  kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, tq, prm);
   return check_launch("paged_decode_kernel");
 }
 
 template <int D>
-int dispatch_nrep(int nrep, const CUtensorMap& tkv, const DecodeParams& prm, int n_seqs, cudaStream_t stream) {
+int dispatch_nrep(int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm,
+                  cudaStream_t stream) {
   switch (nrep) {
-    case 1: return launch_decode<D, 1>(tkv, prm, n_seqs, stream);
-    case 2: return launch_decode<D, 2>(tkv, prm, n_seqs, stream);
-    case 3: return launch_decode<D, 3>(tkv, prm, n_seqs, stream);
-    case 4: return launch_decode<D, 4>(tkv, prm, n_seqs, stream);
-    case 5: return launch_decode<D, 5>(tkv, prm, n_seqs, stream);
-    case 6: return launch_decode<D, 6>(tkv, prm, n_seqs, stream);
-    case 7: return launch_decode<D, 7>(tkv, prm, n_seqs, stream);
-    case 8: return launch_decode<D, 8>(tkv, prm, n_seqs, stream);
+    case 1: return launch_decode<D, 1>(tkv, tq, prm, stream);
+    case 2: return launch_decode<D, 2>(tkv, tq, prm, stream);
+    case 3: return launch_decode<D, 3>(tkv, tq, prm, stream);
+    case 4: return launch_decode<D, 4>(tkv, tq, prm, stream);
+    case 5: return launch_decode<D, 5>(tkv, tq, prm, stream);
+    case 6: return launch_decode<D, 6>(tkv, tq, prm, stream);
+    case 7: return launch_decode<D, 7>(tkv, tq, prm, stream);
+    case 8: return launch_decode<D, 8>(tkv, tq, prm, stream);
     default: return set_error(MTN_EINVAL, "paged decode: query heads per kv head %d not in [1,8]", nrep);
   }
 }
 
-int effective_split(int page_size, int pages_per_split) {
-  const int tp = kTile / page_size;
-  if (pages_per_split <= 0) pages_per_split = tp;
-  pages_per_split = std::min(pages_per_split, DCfg<64>::kMaxSplitPages);
-  return ((pages_per_split + tp - 1) / tp) * tp;
+int decode_ctas(int head_dim) {
+  const int per = head_dim == 64 ? DCfg<64>::kCtasPerSm : head_dim == 128 ? DCfg<128>::kCtasPerSm
+                                                                          : DCfg<256>::kCtasPerSm;
+  return sm_count() * per;
 }
 
 }  // namespace
@@ -521,102 +723,89 @@ using mtn::set_error;
 
 extern "C" {
 
-size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                                        int32_t max_pages_per_seq, int32_t pages_per_split) {
-  if (n_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_pages_per_seq < 0) return 0;
-  // Splits are rounded up to whole 128-token tiles, which only lowers the
-  // split count, so sizing with the pages_per_split given (at least 1) is safe.
-  const int64_t pps = pages_per_split > 0 ? pages_per_split : 1;
-  const int64_t max_splits = std::max<int64_t>(1, (max_pages_per_seq + pps - 1) / pps);
-  const int64_t slots = static_cast<int64_t>(n_seqs) * num_q_heads * max_splits;
+size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                                        int32_t head_dim) {
+  (void)num_q_heads;
+  if (n_seqs <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256)) return 0;
+  const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(head_dim)) * 2 * mtn::kN;
   size_t bytes = static_cast<size_t>(slots) * head_dim * 4;   // ws_o
   bytes += static_cast<size_t>(slots) * 2 * 4;                  // ws_ml
   bytes += static_cast<size_t>(n_seqs) * num_kv_heads * 4;      // arrival counters
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
-int32_t mtn_paged_decode_default_split(const mtn_kv_layout* pool, int32_t n_seqs, int64_t total_pages,
-                                       int32_t max_pages_per_seq, int32_t num_q_heads) {
-  (void)num_q_heads;
-  if (pool == nullptr || pool->page_size <= 0 || n_seqs <= 0 || mtn::kTile % pool->page_size != 0) return 0;
-  const int tp = mtn::kTile / pool->page_size;
-  // About six CTAs per SM of (page, kv head) work: enough to cover the
-  // device twice with the ~3 resident CTAs per SM, few partials to merge.
-  const int64_t target = static_cast<int64_t>(mtn::sm_count()) * 6;
-  const int64_t units = std::max<int64_t>(1, total_pages) * pool->num_kv_heads;
-  int64_t pps = (units + target - 1) / target;
-  pps = std::max<int64_t>(pps, tp);
-  pps = std::min<int64_t>(pps, std::max(max_pages_per_seq, 1));
-  return mtn::effective_split(pool->page_size, static_cast<int>(pps));
-}
-
 int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
-                     int32_t o_dtype, int32_t n_seqs, int32_t num_q_heads, const int32_t* kv_indptr,
-                     const int32_t* kv_indices, const int32_t* seq_lens, int32_t max_pages_per_seq,
-                     int32_t pages_per_split, float scale, uint32_t flags, void* workspace, size_t workspace_bytes,
+                     int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
+                     int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,
+                     const int32_t* seq_lens, float scale, uint32_t flags, void* workspace, size_t workspace_bytes,
                      void* stream) {
   int st = mtn::validate_layout(pool, layer, "mtn_paged_decode");
   if (st != MTN_OK) return st;
-  MTN_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65535, "mtn_paged_decode: n_seqs %d outside [0, 65535]", n_seqs);
+  MTN_CHECK_ARG(n_seqs >= 0, "mtn_paged_decode: n_seqs < 0");
   if (n_seqs == 0) return MTN_OK;
   MTN_CHECK_ARG(q && o && kv_indptr && kv_indices && seq_lens, "mtn_paged_decode: null pointer");
   MTN_CHECK_ARG(q_dtype == MTN_DTYPE_BF16 || q_dtype == MTN_DTYPE_F32, "mtn_paged_decode: bad q dtype");
   MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_decode: bad o dtype");
+  MTN_CHECK_ARG((k_new == nullptr) == (v_new == nullptr), "mtn_paged_decode: give both k_new and v_new or neither");
+  MTN_CHECK_ARG(k_new == nullptr || new_dtype == MTN_DTYPE_BF16 || new_dtype == MTN_DTYPE_F32,
+                "mtn_paged_decode: bad k_new/v_new dtype");
   MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads % pool->num_kv_heads == 0,
                 "mtn_paged_decode: %d query heads not a multiple of %d kv heads", num_q_heads, pool->num_kv_heads);
-  MTN_CHECK_ARG(pool->num_kv_heads <= 65535, "mtn_paged_decode: too many kv heads");
   const int D = pool->head_dim;
   MTN_CHECK_ARG(pool->page_size % 8 == 0 && mtn::kTile % pool->page_size == 0,
                 "mtn_paged_decode: page_size %d must be a multiple of 8 dividing %d", pool->page_size, mtn::kTile);
-  MTN_CHECK_ARG(max_pages_per_seq >= 0, "mtn_paged_decode: max_pages_per_seq < 0");
-  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
-                "mtn_paged_decode: q/o must be 16-byte aligned");
-  const int pps = mtn::effective_split(pool->page_size, pages_per_split);
-  const int max_splits = std::max(1, (max_pages_per_seq + pps - 1) / pps);
-  MTN_CHECK_ARG(max_splits <= (1 << 20), "mtn_paged_decode: too many splits");
-  const size_t need = mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool->num_kv_heads, D,
-                                                       max_pages_per_seq, pps);
-  if (max_splits > 1) {
-    MTN_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
-                  "mtn_paged_decode: workspace of %zu bytes < %zu needed", workspace_bytes, need);
-    MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "mtn_paged_decode: workspace alignment");
-  }
-  CUtensorMap tkv;
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(k_new) & 15) == 0 && (reinterpret_cast<uintptr_t>(v_new) & 15) == 0,
+                "mtn_paged_decode: q/o/k_new/v_new must be 16-byte aligned");
+  MTN_CHECK_ARG(static_cast<int64_t>(n_seqs) * num_q_heads < (int64_t(1) << 31), "mtn_paged_decode: q too large");
+  const size_t need = mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool->num_kv_heads, D);
+  MTN_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
+                "mtn_paged_decode: workspace of %zu bytes < %zu needed", workspace_bytes, need);
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "mtn_paged_decode: workspace alignment");
+  CUtensorMap tkv, tq;
   st = mtn::pool_tensor_map(pool, &tkv);
   if (st != MTN_OK) return st;
+  if (q_dtype == MTN_DTYPE_BF16) {
+    // 16-row boxes over the [n_seqs * heads, head_dim] view of q.
+    st = mtn::q_tensor_map(q, static_cast<int64_t>(n_seqs) * num_q_heads, 1, D, mtn::kN, &tq);
+    if (st != MTN_OK) return st;
+  } else {
+    std::memset(&tq, 0, sizeof(tq));
+  }
 
   mtn::DecodeParams prm{};
   const int64_t rows_per_block = pool->num_pages * pool->num_kv_heads * pool->page_size;
   prm.row_k = (static_cast<int64_t>(layer) * 2 + 0) * rows_per_block;
   prm.row_v = (static_cast<int64_t>(layer) * 2 + 1) * rows_per_block;
+  prm.pool = static_cast<__nv_bfloat16*>(pool->base);
   prm.num_pages = pool->num_pages;
   prm.hkv = pool->num_kv_heads;
   prm.ps = pool->page_size;
   prm.hq = num_q_heads;
+  prm.n_seqs = n_seqs;
   prm.q = q;
   prm.o = o;
   prm.q_f32 = q_dtype == MTN_DTYPE_F32;
   prm.o_f32 = o_dtype == MTN_DTYPE_F32;
+  prm.k_new = k_new;
+  prm.v_new = v_new;
+  prm.new_f32 = new_dtype == MTN_DTYPE_F32;
   prm.kv_indptr = kv_indptr;
   prm.kv_indices = kv_indices;
   prm.seq_lens = seq_lens;
-  prm.pages_per_split = pps;
-  prm.max_splits = max_splits;
   prm.qscale = scale * mtn::kLog2e;
   prm.phantom = (flags & MTN_ATTN_PHANTOM_ZERO_SLOT) ? 1 : 0;
-  if (max_splits > 1) {
-    const int64_t slots = static_cast<int64_t>(n_seqs) * num_q_heads * max_splits;
-    prm.ws_o = static_cast<float*>(workspace);
-    prm.ws_ml = prm.ws_o + slots * D;
-    prm.ws_cnt = reinterpret_cast<unsigned int*>(prm.ws_ml + slots * 2);
-  }
+  const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(D)) * 2 * mtn::kN;
+  prm.ws_o = static_cast<float*>(workspace);
+  prm.ws_ml = prm.ws_o + slots * D;
+  prm.ws_cnt = reinterpret_cast<unsigned int*>(prm.ws_ml + slots * 2);
   prm.err = mtn::device_error_ptr();
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
   switch (D) {
-    case 64: return mtn::dispatch_nrep<64>(nrep, tkv, prm, n_seqs, s);
-    case 128: return mtn::dispatch_nrep<128>(nrep, tkv, prm, n_seqs, s);
-    default: return mtn::dispatch_nrep<256>(nrep, tkv, prm, n_seqs, s);
+    case 64: return mtn::dispatch_nrep<64>(nrep, tkv, tq, prm, s);
+    case 128: return mtn::dispatch_nrep<128>(nrep, tkv, tq, prm, s);
+    default: return mtn::dispatch_nrep<256>(nrep, tkv, tq, prm, s);
   }
 }
 

@@ -124,32 +124,28 @@ def build_slot_mapping(qo_indptr, positions, kv_indptr, kv_indices, page_size: i
 
 
 class DecodeWorkspace:
-    """Split-KV partials + arrival counters for mtn_paged_decode (zeroed once)."""
+    """Partials + arrival counters for mtn_paged_decode (zeroed once, reusable)."""
 
     def __init__(self, nbytes: int, device):
         self.nbytes = max(int(nbytes), 256)
         self.buf = torch.zeros(self.nbytes, dtype=torch.uint8, device=device)
 
     @classmethod
-    def for_shape(cls, pool: PagedKVPool, n_seqs: int, num_q_heads: int, max_pages_per_seq: int,
-                  pages_per_split: int = 0):
-        nb = L.lib().mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool.num_kv_heads, pool.head_dim,
-                                                      max_pages_per_seq, pages_per_split)
+    def for_shape(cls, pool: PagedKVPool, n_seqs: int, num_q_heads: int):
+        nb = L.lib().mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool.num_kv_heads, pool.head_dim)
         return cls(nb, pool.device)
 
 
-def default_split(pool: PagedKVPool, n_seqs: int, total_pages: int, max_pages_per_seq: int,
-                  num_q_heads: int) -> int:
-    return int(L.lib().mtn_paged_decode_default_split(C.byref(pool.layout), n_seqs, total_pages,
-                                                      max_pages_per_seq, num_q_heads))
-
-
 def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torch.Tensor,
-                 kv_indices: torch.Tensor, seq_lens: torch.Tensor, max_pages_per_seq: int,
-                 scale: float | None = None, phantom: bool = False, pages_per_split: int = 0,
+                 kv_indices: torch.Tensor, seq_lens: torch.Tensor, scale: float | None = None,
+                 phantom: bool = False, k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
                  workspace: DecodeWorkspace | None = None, stream=None) -> torch.Tensor:
-    """Decode attention for q [n_seqs, num_q_heads, head_dim] over the paged cache."""
+    """Decode attention for q [n_seqs, num_q_heads, head_dim] over the paged cache.
+
+    With k_new/v_new [n_seqs, kv_heads, head_dim] the step's token is first
+    stored at position seq_lens[r]-1 of each sequence (fused KV append).
+    """
     if q.dim() != 3 or not q.is_contiguous():
         raise ValueError("q must be a contiguous [n_seqs, heads, head_dim] tensor")
     n, hq, d = q.shape
@@ -160,12 +156,19 @@ def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torc
     if out is None:
         out = torch.empty((n, hq, d), dtype=out_dtype, device=q.device)
     if workspace is None:
-        workspace = DecodeWorkspace.for_shape(pool, n, hq, max_pages_per_seq, pages_per_split)
+        workspace = DecodeWorkspace.for_shape(pool, n, hq)
+    new_code = 0
+    if k_new is not None or v_new is not None:
+        if k_new is None or v_new is None or not k_new.is_contiguous() or not v_new.is_contiguous():
+            raise ValueError("k_new and v_new must both be contiguous [n_seqs, kv_heads, head_dim] tensors")
+        if k_new.dtype != v_new.dtype or k_new.numel() != n * pool.num_kv_heads * d:
+            raise ValueError("k_new/v_new shape or dtype mismatch")
+        new_code = _dtype_code(k_new.dtype)
     flags = L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0
     L.check(L.lib().mtn_paged_decode(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype), _ptr(out),
-                                     _dtype_code(out.dtype), n, hq, _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)),
-                                     _ptr(_i32(seq_lens)), max_pages_per_seq, pages_per_split, float(scale), flags,
-                                     _ptr(workspace.buf), workspace.nbytes, _stream(stream)))
+                                     _dtype_code(out.dtype), _ptr(k_new), _ptr(v_new), new_code, n, hq,
+                                     _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)), _ptr(_i32(seq_lens)),
+                                     float(scale), flags, _ptr(workspace.buf), workspace.nbytes, _stream(stream)))
     return out
 
 
