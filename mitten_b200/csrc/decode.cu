@@ -235,7 +235,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  const int64_t ctas = gridDim.x;
   const int64_t cta = blockIdx.x;
 
   // ------------------------------------------------------------ work split
@@ -248,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     const int len = seq_len_of(p, s);
     const int T = (len + kTile - 1) / kTile;
     mine += T;
-    if (T == 0 && s % ctas == cta) {
+    if (T == 0 && s % static_cast<int64_t>(gridDim.x) == cta) {
       // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
       const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
       for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
@@ -274,8 +273,12 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   int64_t total_seq_tiles = 0;
   for (int w = 0; w < kThreads / 32; ++w) total_seq_tiles += scan[w];
   const int64_t U = total_seq_tiles * p.hkv;
-  const int64_t t0 = U > 0 ? tile_begin(cta, U, ctas) : 0;
-  const int64_t t1 = U > 0 ? tile_begin(cta + 1, U, ctas) : 0;
+  // With fewer tiles than CTAs only the first U CTAs take part, so every
+  // participating CTA owns at least one tile and a segment's pieces are
+  // exactly the CTAs cta_of(first tile) .. cta_of(last tile).
+  const int64_t ctas = min(static_cast<int64_t>(gridDim.x), U);
+  const int64_t t0 = cta < ctas ? tile_begin(cta, U, ctas) : 0;
+  const int64_t t1 = cta < ctas ? tile_begin(cta + 1, U, ctas) : 0;
   const int n_local = static_cast<int>(t1 - t0);
   if (n_local > 0 && t0 >= before * p.hkv && t0 < (before + mine) * p.hkv) {
     int64_t pre = before;
