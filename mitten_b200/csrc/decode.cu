@@ -184,10 +184,13 @@ struct Walker {
     T = (len + kTile - 1) / kTile;
     pbeg = p.kv_indptr[s];
   }
-  __device__ void start(const DecodeParams& p, int s0, int64_t pre0, int64_t t0) {
+  // Start at global tile t0 of sequence s0 whose metadata is already known.
+  __device__ void start(const DecodeParams& p, int s0, int64_t pre0, int64_t t0, int len0, int pbeg0) {
     s = s0;
     pre = pre0;
-    load(p);
+    len = len0;
+    T = (len + kTile - 1) / kTile;
+    pbeg = pbeg0;
     const int64_t off = t0 - pre * p.hkv;
     g = static_cast<int>(off / T);
     j = static_cast<int>(off - static_cast<int64_t>(g) * T);
@@ -226,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   int* start_s = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 12);
   int64_t* start_pre = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 16);
   int64_t* total_u = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 24);
+  int* start_len = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 32);
+  int* start_pbeg = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 36);
   float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
   float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
   int64_t* scan = reinterpret_cast<int64_t*>(smem_raw + C::kOffScan);  // [6]
@@ -243,9 +248,11 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int chunk = (p.n_seqs + kThreads - 1) / kThreads;
   const int sb = min(p.n_seqs, tid * chunk), se = min(p.n_seqs, sb + chunk);
   int64_t mine = 0;
+  int len_first = 0;  // metadata of this thread's first sequence, kept for the start search
   for (int s = sb; s < se; ++s) {
     const int len = seq_len_of(p, s);
     const int T = (len + kTile - 1) / kTile;
+    if (s == sb) len_first = len;
     mine += T;
     if (T == 0 && s % static_cast<int64_t>(gridDim.x) == cta) {
       // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
@@ -283,10 +290,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   if (n_local > 0 && t0 >= before * p.hkv && t0 < (before + mine) * p.hkv) {
     int64_t pre = before;
     for (int s = sb; s < se; ++s) {
-      const int T = (seq_len_of(p, s) + kTile - 1) / kTile;
+      const int len = (s == sb) ? len_first : seq_len_of(p, s);
+      const int T = (len + kTile - 1) / kTile;
       if (t0 < (pre + T) * p.hkv) {
         *start_s = s;
         *start_pre = pre;
+        *start_len = len;
+        *start_pbeg = p.kv_indptr[s];
         break;
       }
       pre += T;
@@ -316,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const uint32_t tmem = *tmem_base_s;
   const int s0 = *start_s;
   const int64_t pre0 = *start_pre;
+  const int len0 = *start_len, pbeg0 = *start_pbeg;
   const int tile_pages = kTile / p.ps;
 
   if (warp == 4) {
@@ -325,8 +336,51 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (!p.q_f32) tc::prefetch_tmap(&tm_q);
     }
     Walker w;
-    w.start(p, s0, pre0, t0);
+    w.start(p, s0, pre0, t0, len0, pbeg0);
     int qcnt = 0;
+    // Page id of this lane's page of the next tile, and (when that tile ends
+    // its segment) this step's K/V row for the fused append: loaded one tile
+    // ahead so they overlap the wait for a free stage.
+    int64_t pg_next = 0, app_row = -1;
+    uint4 app_k = make_uint4(0u, 0u, 0u, 0u), app_v = app_k;
+    auto prefetch = [&]() {
+      const int npg = (w.len + p.ps - 1) / p.ps;
+      if (lane < tile_pages) {
+        int64_t page = p.kv_indices[w.pbeg + min(w.j * tile_pages + lane, npg - 1)];
+        if (page < 0 || page >= p.num_pages) {
+          record_error(p.err, kDevErrBadPage, w.s);
+          page = 0;  // past the sequence's last page: reload a valid page (masked)
+        }
+        pg_next = page;
+      }
+      app_row = -1;
+      if (p.k_new != nullptr && w.j == w.T - 1) {
+        const int pos = w.len - 1;
+        const int64_t page = p.kv_indices[w.pbeg + pos / p.ps];
+        if (page < 0 || page >= p.num_pages) {
+          record_error(p.err, kDevErrBadPage, w.s);
+        } else {
+          app_row = (page * p.hkv + w.g) * p.ps + pos % p.ps;
+          if (lane < D / 8) {
+            const int64_t src = (static_cast<int64_t>(w.s) * p.hkv + w.g) * D + lane * 8;
+            if (p.new_f32) {
+              const float* kf = static_cast<const float*>(p.k_new) + src;
+              const float* vf = static_cast<const float*>(p.v_new) + src;
+              const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
+              const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
+              app_k = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
+                                 f2_to_bf2(k1.z, k1.w));
+              app_v = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
+                                 f2_to_bf2(v1.z, v1.w));
+            } else {
+              app_k = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
+              app_v = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
+            }
+          }
+        }
+      }
+    };
+    prefetch();
     for (int i = 0; i < n_local; ++i) {
       const bool first = (i == 0) || w.j == 0;
       if (first) {
@@ -369,35 +423,12 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((i / C::kStages) - 1) & 1, abort_flag, p.err, 10);
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       }
-      const int npg = (w.len + p.ps - 1) / p.ps;
-      if (p.k_new != nullptr && w.j == w.T - 1) {
+      if (app_row >= 0) {
         // Fused KV append: store this step's row at position len-1, then
         // order it before the async-proxy (TMA) read of the same page.
-        const int pos = w.len - 1;
-        int64_t page = p.kv_indices[w.pbeg + pos / p.ps];
-        if (page < 0 || page >= p.num_pages) {
-          record_error(p.err, kDevErrBadPage, w.s);
-          page = -1;
-        }
-        if (page >= 0 && lane < D / 8) {
-          const int64_t src = (static_cast<int64_t>(w.s) * p.hkv + w.g) * D + lane * 8;
-          uint4 kk, vv;
-          if (p.new_f32) {
-            const float* kf = static_cast<const float*>(p.k_new) + src;
-            const float* vf = static_cast<const float*>(p.v_new) + src;
-            const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
-            const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
-            kk = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
-                            f2_to_bf2(k1.z, k1.w));
-            vv = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
-                            f2_to_bf2(v1.z, v1.w));
-          } else {
-            kk = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
-            vv = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
-          }
-          const int64_t rowoff = (page * p.hkv + w.g) * p.ps + pos % p.ps;
-          *reinterpret_cast<uint4*>(p.pool + (p.row_k + rowoff) * D + lane * 8) = kk;
-          *reinterpret_cast<uint4*>(p.pool + (p.row_v + rowoff) * D + lane * 8) = vv;
+        if (lane < D / 8) {
+          *reinterpret_cast<uint4*>(p.pool + (p.row_k + app_row) * D + lane * 8) = app_k;
+          *reinterpret_cast<uint4*>(p.pool + (p.row_v + app_row) * D + lane * 8) = app_v;
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
         __syncwarp();
@@ -405,14 +436,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
       __syncwarp();
       if (lane < tile_pages) {
-        // Past the sequence's last page: reload that page (finite data, masked).
-        int64_t page = p.kv_indices[w.pbeg + min(w.j * tile_pages + lane, npg - 1)];
-        if (page < 0 || page >= p.num_pages) {
-          record_error(p.err, kDevErrBadPage, w.s);
-          page = 0;
-        }
-        const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
-        const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
+        const int64_t rk = p.row_k + (pg_next * p.hkv + w.g) * p.ps;
+        const int64_t rv = p.row_v + (pg_next * p.hkv + w.g) * p.ps;
         uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
         uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
 #pragma unroll
@@ -422,7 +447,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
         }
       }
-      if (i + 1 < n_local) w.next(p);
+      if (i + 1 < n_local) {
+        w.next(p);
+        prefetch();
+      }
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
@@ -431,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       constexpr uint32_t idO = tc::idesc_bf16(C::kMO, kN, false, true);
       const uint32_t p_addr = smem_u32(p_s);
       Walker wsw, wo;  // wsw: tiles whose S^T is issued; wo: tiles whose O^T is issued
-      wsw.start(p, s0, pre0, t0);
-      wo.start(p, s0, pre0, t0);
+      wsw.start(p, s0, pre0, t0, len0, pbeg0);
+      wo.start(p, s0, pre0, t0, len0, pbeg0);
       int q_seg = -1;  // segment counter of the S^T issue
       int o_seg = -1;  // segment counter of the O^T issue
       // S^T(i) = K_i Q^T into S buffer i&1: both operands K-major; 16-wide
@@ -505,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     const bool holds = (C::kMO == 64) ? (lane < 16) : true;
     const int d_base = (C::kMO == 64) ? warp * 16 + lane : warp * 32 + lane;
     Walker w;
-    w.start(p, s0, pre0, t0);
+    w.start(p, s0, pre0, t0, len0, pbeg0);
     float m_ref[NREP], l_tok[NREP];
     int seg = -1;
     bool ok = true;
@@ -631,39 +659,98 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
-          __threadfence();
+          // One cumulative fence after the barrier publishes every thread's
+          // partials before the ticket (and orders the merge's reads after it).
           tc::named_sync(1, 128);
           const int64_t seg_id = static_cast<int64_t>(w.s) * p.hkv + w.g;
           if (t == 0) {
+            __threadfence();
             const unsigned int ticket = atomicAdd(&p.ws_cnt[seg_id], 1u);
             *last_flag = (ticket == static_cast<unsigned int>(cb - ca)) ? 1 : 0;
+            __threadfence();
           }
           tc::named_sync(1, 128);
           if (*last_flag) {
-            // Merge the pieces in CTA order.
-            __threadfence();
+            // Merge the pieces in CTA order.  The pieces' (m, l) are staged
+            // in the idle P^T buffer with one round trip; each thread then
+            // loads its O partials for up to four pieces at a time.
             const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
-            for (int e = t; e < NREP * D; e += 128) {
-              const int h = e / D, d = e - (e / D) * D;
-              float mall = -INFINITY;
-              for (int64_t cc = ca; cc <= cb; ++cc) {
-                const int64_t sl = (cc * 2 + (cc == ca ? wa : 0)) * kN + h;
-                mall = fmaxf(mall, ld_cg(p.ws_ml + sl * 2));
+            const int np = static_cast<int>(cb - ca + 1);
+            constexpr int kElems = (NREP * D + 127) / 128;
+            float* stage = reinterpret_cast<float*>(p_s);  // [32 pieces][16 heads][2]
+            const bool staged = np <= 32;
+            if (staged) {
+              for (int e = t; e < np * NREP; e += 128) {
+                const int k = e / NREP, h = e - k * NREP;
+                const int64_t cc = ca + k;
+                const int64_t sl = (cc * 2 + (k == 0 ? wa : 0)) * kN + h;
+                stage[(k * kN + h) * 2 + 0] = ld_cg(p.ws_ml + sl * 2);
+                stage[(k * kN + h) * 2 + 1] = ld_cg(p.ws_ml + sl * 2 + 1);
               }
-              float o = 0.0f, l = 0.0f;
-              if (mall != -INFINITY) {
-                for (int64_t cc = ca; cc <= cb; ++cc) {
-                  const int64_t sl = (cc * 2 + (cc == ca ? wa : 0)) * kN + h;
-                  const float mj = ld_cg(p.ws_ml + sl * 2);
-                  if (mj == -INFINITY) continue;
-                  const float a = exp2f(mj - mall);
-                  o += ld_cg(p.ws_o + sl * D + d) * a;
-                  l += ld_cg(p.ws_ml + sl * 2 + 1) * a;
+            }
+            tc::named_sync(1, 128);
+            float acc_o[kElems], acc_l[kElems], mall[kElems];
+#pragma unroll
+            for (int q = 0; q < kElems; ++q) {
+              const int e = t + q * 128;
+              const int h = e / D;
+              mall[q] = -INFINITY;
+              acc_o[q] = 0.0f;
+              acc_l[q] = 0.0f;
+              if (e < NREP * D) {
+                for (int k = 0; k < np; ++k) {
+                  const float mk = staged ? stage[(k * kN + h) * 2]
+                                          : ld_cg(p.ws_ml + ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN * 2 + h * 2);
+                  mall[q] = fmaxf(mall[q], mk);
                 }
               }
-              store_out(p, (head0 + h) * D + d, finalize(o, l, mall, p.phantom));
+            }
+            for (int k0 = 0; k0 < np; k0 += 4) {
+              float ov4[kElems][4];
+#pragma unroll
+              for (int q = 0; q < kElems; ++q) {
+                const int e = t + q * 128;
+                const int h = e / D, d = e - (e / D) * D;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int k = k0 + u;
+                  ov4[q][u] = 0.0f;
+                  if (e < NREP * D && k < np) {
+                    const int64_t sl = ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN + h;
+                    ov4[q][u] = ld_cg(p.ws_o + sl * D + d);
+                  }
+                }
+              }
+#pragma unroll
+              for (int q = 0; q < kElems; ++q) {
+                const int e = t + q * 128;
+                const int h = e / D;
+                if (e >= NREP * D || mall[q] == -INFINITY) continue;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int k = k0 + u;
+                  if (k >= np) break;
+                  const int64_t sl = ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN + h;
+                  const float mk = staged ? stage[(k * kN + h) * 2] : ld_cg(p.ws_ml + sl * 2);
+                  if (mk == -INFINITY) continue;
+                  const float lk = staged ? stage[(k * kN + h) * 2 + 1] : ld_cg(p.ws_ml + sl * 2 + 1);
+                  const float a = exp2f(mk - mall[q]);
+                  acc_o[q] += ov4[q][u] * a;
+                  acc_l[q] += lk * a;
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < kElems; ++q) {
+              const int e = t + q * 128;
+              if (e < NREP * D) store_out(p, head0 * D + e, finalize(acc_o[q], acc_l[q], mall[q], p.phantom));
             }
             if (t == 0) p.ws_cnt[seg_id] = 0u;  // ready for the next launch on this workspace
+            // Restore the zero rows of P^T used as scratch.
+            tc::named_sync(1, 128);
+            uint4* pz = reinterpret_cast<uint4*>(p_s);
+            for (int e = t; e < C::kPBytes / 16; e += 128) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+            fence_proxy_async_shared();
           }
           tc::named_sync(1, 128);  // last_flag is reused by the next segment
         }
