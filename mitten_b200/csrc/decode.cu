@@ -32,10 +32,11 @@
 //              next tile's QK^T overlaps this tile's softmax; O^T
 //              double-buffered per segment so an epilogue overlaps the next
 //              segment.
-// A segment cut by a CTA boundary leaves (m, l, O) partials in per-CTA
-// workspace slots; the last CTA to finish one (atomic ticket, no spinning)
-// merges them in CTA order, so results do not depend on scheduling.  Every
-// wait is bounded.
+// A segment cut by CTA boundaries leaves (m, l, O) partials in per-CTA
+// workspace slots and a descriptor from the CTA holding its last tile; a
+// second small kernel on the same stream merges each such segment's pieces
+// in CTA order, so results do not depend on scheduling.  Every wait is
+// bounded.
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
@@ -76,9 +77,9 @@ struct DecodeParams {
   const int32_t* seq_lens;
   float qscale;  // scale * log2(e)
   int phantom;
-  float* ws_o;           // [ctas][2][16][D]
-  float* ws_ml;          // [ctas][2][16][2]
-  unsigned int* ws_cnt;  // [n_seqs][hkv]
+  float* ws_o;    // [ctas][2][16][D]   partial O of split segments
+  float* ws_ml;   // [ctas][2][16][2]   partial (m, l)
+  int4* ws_desc;  // [ctas] split segment ending in this CTA: (segment + 1, ca, cb, wa); x = 0: none
   int* err;
 };
 
@@ -225,7 +226,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + C::kOffBar);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem_raw + C::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 4);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 8);
   int* start_s = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 12);
   int64_t* start_pre = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 16);
   int64_t* total_u = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 24);
@@ -310,20 +310,24 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     return;
   }
 
-  if (warp == 0) {
-    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
-    tc::tmem_relinquish();
-  }
   uint8_t* p_s = big + C::kOffP;
-  {
-    uint4* pz = reinterpret_cast<uint4*>(p_s);  // rows >= NREP of P^T stay zero
-    for (int e = tid; e < C::kPBytes / 16; e += kThreads) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t tmem = 0;
+  if (warp != 4) {
+    // TMEM and the zeroed P^T operand (rows >= NREP stay zero) for the MMA
+    // and softmax roles; the producer starts loading meanwhile.
+    if (warp == 0) {
+      tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+      tc::tmem_relinquish();
+    }
+    const int tid160 = warp == 5 ? 128 + lane : tid;
+    uint4* pz = reinterpret_cast<uint4*>(p_s);
+    for (int e = tid160; e < C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_shared();
+    tc::fence_before_sync();
+    tc::named_sync(2, 160);
+    tc::fence_after_sync();
+    tmem = *tmem_base_s;
   }
-  fence_proxy_async_shared();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_base_s;
   const int s0 = *start_s;
   const int64_t pre0 = *start_pre;
   const int len0 = *start_len, pbeg0 = *start_pbeg;
@@ -488,12 +492,22 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (i + 1 < n_local) wsw.next(p);
         return true;
       };
+      // Can S^T(j) be issued without waiting?  (wsw is positioned at tile j.)
+      auto s_ready = [&](int j) -> bool {
+        const bool first = (j == 0) || wsw.j == 0;
+        if (first && !mbar_test_wait(&bars[kQFull0 + ((q_seg + 1) & 1)], ((q_seg + 1) >> 1) & 1)) return false;
+        return mbar_test_wait(&bars[kKVFull0 + j % C::kStages], (j / C::kStages) & 1);
+      };
       bool ok = issue_s(0);
+      int next_s = 1;  // next tile whose S^T is not issued yet
       for (int i = 0; ok && i < n_local; ++i) {
-        // Overlap the next tile's S^T with this tile's softmax (its S buffer
-        // was released by the softmax of tile i-1, waited on below).  With a
-        // single K/V stage the next tile only lands after this P V.
-        if (C::kStages > 1 && i + 1 < n_local && !issue_s(i + 1)) break;
+        // Overlap the next tile's S^T with this tile's softmax when its K/V
+        // already landed (its S buffer was released by the softmax of tile
+        // i-1, waited on below), but never let that wait hold up this P V.
+        if (C::kStages > 1 && next_s == i + 1 && next_s < n_local && s_ready(next_s)) {
+          if (!issue_s(next_s)) break;
+          ++next_s;
+        }
         const bool first = (i == 0) || wo.j == 0;
         if (first) {
           ++o_seg;
@@ -521,7 +535,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         tc::mma_commit(&bars[kODone]);
         tc::mma_commit(&bars[kKVEmpty0 + st]);
         if (i + 1 < n_local) wo.next(p);
-        if (C::kStages == 1 && i + 1 < n_local && !issue_s(i + 1)) break;
+        if (next_s == i + 1 && next_s < n_local) {
+          if (!issue_s(next_s)) break;
+          ++next_s;
+        }
       }
     }
   } else {
@@ -659,100 +676,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
-          // One cumulative fence after the barrier publishes every thread's
-          // partials before the ticket (and orders the merge's reads after it).
-          tc::named_sync(1, 128);
-          const int64_t seg_id = static_cast<int64_t>(w.s) * p.hkv + w.g;
-          if (t == 0) {
-            __threadfence();
-            const unsigned int ticket = atomicAdd(&p.ws_cnt[seg_id], 1u);
-            *last_flag = (ticket == static_cast<unsigned int>(cb - ca)) ? 1 : 0;
-            __threadfence();
-          }
-          tc::named_sync(1, 128);
-          if (*last_flag) {
-            // Merge the pieces in CTA order.  The pieces' (m, l) are staged
-            // in the idle P^T buffer with one round trip; each thread then
-            // loads its O partials for up to four pieces at a time.
+          if (cta == cb && t == 0) {
+            // The segment's last piece records it for the merge kernel
+            // (the kernel boundary orders every piece's partials before it).
             const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
-            const int np = static_cast<int>(cb - ca + 1);
-            constexpr int kElems = (NREP * D + 127) / 128;
-            float* stage = reinterpret_cast<float*>(p_s);  // [32 pieces][16 heads][2]
-            const bool staged = np <= 32;
-            if (staged) {
-              for (int e = t; e < np * NREP; e += 128) {
-                const int k = e / NREP, h = e - k * NREP;
-                const int64_t cc = ca + k;
-                const int64_t sl = (cc * 2 + (k == 0 ? wa : 0)) * kN + h;
-                stage[(k * kN + h) * 2 + 0] = ld_cg(p.ws_ml + sl * 2);
-                stage[(k * kN + h) * 2 + 1] = ld_cg(p.ws_ml + sl * 2 + 1);
-              }
-            }
-            tc::named_sync(1, 128);
-            float acc_o[kElems], acc_l[kElems], mall[kElems];
-#pragma unroll
-            for (int q = 0; q < kElems; ++q) {
-              const int e = t + q * 128;
-              const int h = e / D;
-              mall[q] = -INFINITY;
-              acc_o[q] = 0.0f;
-              acc_l[q] = 0.0f;
-              if (e < NREP * D) {
-                for (int k = 0; k < np; ++k) {
-                  const float mk = staged ? stage[(k * kN + h) * 2]
-                                          : ld_cg(p.ws_ml + ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN * 2 + h * 2);
-                  mall[q] = fmaxf(mall[q], mk);
-                }
-              }
-            }
-            for (int k0 = 0; k0 < np; k0 += 4) {
-              float ov4[kElems][4];
-#pragma unroll
-              for (int q = 0; q < kElems; ++q) {
-                const int e = t + q * 128;
-                const int h = e / D, d = e - (e / D) * D;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int k = k0 + u;
-                  ov4[q][u] = 0.0f;
-                  if (e < NREP * D && k < np) {
-                    const int64_t sl = ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN + h;
-                    ov4[q][u] = ld_cg(p.ws_o + sl * D + d);
-                  }
-                }
-              }
-#pragma unroll
-              for (int q = 0; q < kElems; ++q) {
-                const int e = t + q * 128;
-                const int h = e / D;
-                if (e >= NREP * D || mall[q] == -INFINITY) continue;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int k = k0 + u;
-                  if (k >= np) break;
-                  const int64_t sl = ((ca + k) * 2 + (k == 0 ? wa : 0)) * kN + h;
-                  const float mk = staged ? stage[(k * kN + h) * 2] : ld_cg(p.ws_ml + sl * 2);
-                  if (mk == -INFINITY) continue;
-                  const float lk = staged ? stage[(k * kN + h) * 2 + 1] : ld_cg(p.ws_ml + sl * 2 + 1);
-                  const float a = exp2f(mk - mall[q]);
-                  acc_o[q] += ov4[q][u] * a;
-                  acc_l[q] += lk * a;
-                }
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < kElems; ++q) {
-              const int e = t + q * 128;
-              if (e < NREP * D) store_out(p, head0 * D + e, finalize(acc_o[q], acc_l[q], mall[q], p.phantom));
-            }
-            if (t == 0) p.ws_cnt[seg_id] = 0u;  // ready for the next launch on this workspace
-            // Restore the zero rows of P^T used as scratch.
-            tc::named_sync(1, 128);
-            uint4* pz = reinterpret_cast<uint4*>(p_s);
-            for (int e = t; e < C::kPBytes / 16; e += 128) pz[e] = make_uint4(0u, 0u, 0u, 0u);
-            fence_proxy_async_shared();
+            p.ws_desc[cta] = make_int4(static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g) + 1,
+                                       static_cast<int>(ca), static_cast<int>(cb), wa);
           }
-          tc::named_sync(1, 128);  // last_flag is reused by the next segment
         }
       }
       if (i + 1 < n_local) w.next(p);
@@ -764,6 +694,88 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// Merge of the pieces of segments split across CTAs, in CTA order.  One
+// block per descriptor slot; most slots are empty and exit at once.
+template <int D, int NREP>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const __grid_constant__ DecodeParams p, int grid) {
+  constexpr int kElems = (NREP * D + 127) / 128;
+  constexpr int kChunk = 32;  // pieces staged per round
+  __shared__ float stage[kChunk * NREP * 2];
+  __shared__ int4 desc_s;
+  const int t = threadIdx.x;
+  for (int c = blockIdx.x; c < grid; c += gridDim.x) {
+    if (t == 0) desc_s = p.ws_desc[c];
+    __syncthreads();
+    const int4 dsc = desc_s;
+    __syncthreads();
+    if (dsc.x == 0) continue;
+    const int seg = dsc.x - 1, ca = dsc.y, cb = dsc.z, wa = dsc.w;
+    const int s = seg / p.hkv, g = seg - (seg / p.hkv) * p.hkv;
+    const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
+    const int np = cb - ca + 1;
+    float mrun[kElems], orun[kElems], lrun[kElems];
+#pragma unroll
+    for (int q = 0; q < kElems; ++q) {
+      mrun[q] = -INFINITY;
+      orun[q] = 0.0f;
+      lrun[q] = 0.0f;
+    }
+    for (int kb = 0; kb < np; kb += kChunk) {
+      const int nk = min(kChunk, np - kb);
+      for (int e = t; e < nk * NREP; e += 128) {
+        const int k = e / NREP, h = e - (e / NREP) * NREP;
+        const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
+        stage[(k * NREP + h) * 2 + 0] = p.ws_ml[sl * 2 + 0];
+        stage[(k * NREP + h) * 2 + 1] = p.ws_ml[sl * 2 + 1];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < kElems; ++q) {
+        const int e = t + q * 128;
+        if (e >= NREP * D) continue;
+        const int h = e / D, d = e - (e / D) * D;
+        float mc = -INFINITY;
+        for (int k = 0; k < nk; ++k) mc = fmaxf(mc, stage[(k * NREP + h) * 2]);
+        if (mc == -INFINITY) continue;
+        const float mnew = fmaxf(mrun[q], mc);
+        const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
+        orun[q] *= a_old;
+        lrun[q] *= a_old;
+        mrun[q] = mnew;
+        for (int k0 = 0; k0 < nk; k0 += 4) {
+          float ov[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {  // four independent loads in flight
+            const int k = k0 + u;
+            ov[u] = 0.0f;
+            if (k < nk) {
+              const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
+              ov[u] = p.ws_o[sl * D + d];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u;
+            if (k >= nk) break;
+            const float mk = stage[(k * NREP + h) * 2];
+            if (mk == -INFINITY) continue;
+            const float a = exp2f(mk - mnew);
+            orun[q] += ov[u] * a;
+            lrun[q] += stage[(k * NREP + h) * 2 + 1] * a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < kElems; ++q) {
+      const int e = t + q * 128;
+      if (e < NREP * D) store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
+    }
+    if (t == 0) p.ws_desc[c] = make_int4(0, 0, 0, 0);  // ready for the next call on this workspace
   }
 }
 
@@ -781,7 +793,10 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
   }
   const int grid = sm_count() * C::kCtasPerSm;
   kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, tq, prm);
-  return check_launch("paged_decode_kernel");
+  int st = check_launch("paged_decode_kernel");
+  if (st != MTN_OK) return st;
+  decode_merge_kernel<D, NREP><<<grid, 128, 0, stream>>>(prm, grid);
+  return check_launch("decode_merge_kernel");
 }
 
 template <int D>
@@ -818,9 +833,9 @@ size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int
   (void)num_q_heads;
   if (n_seqs <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256)) return 0;
   const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(head_dim)) * 2 * mtn::kN;
-  size_t bytes = static_cast<size_t>(slots) * head_dim * 4;   // ws_o
-  bytes += static_cast<size_t>(slots) * 2 * 4;                  // ws_ml
-  bytes += static_cast<size_t>(n_seqs) * num_kv_heads * 4;      // arrival counters
+  size_t bytes = static_cast<size_t>(slots) * head_dim * 4;    // ws_o
+  bytes += static_cast<size_t>(slots) * 2 * 4;                   // ws_ml
+  bytes += static_cast<size_t>(mtn::decode_ctas(head_dim)) * 16;  // ws_desc
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -888,7 +903,7 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(D)) * 2 * mtn::kN;
   prm.ws_o = static_cast<float*>(workspace);
   prm.ws_ml = prm.ws_o + slots * D;
-  prm.ws_cnt = reinterpret_cast<unsigned int*>(prm.ws_ml + slots * 2);
+  prm.ws_desc = reinterpret_cast<int4*>(prm.ws_ml + slots * 2);
   prm.err = mtn::device_error_ptr();
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);

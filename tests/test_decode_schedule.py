@@ -2,8 +2,8 @@
 only, mirrored from mitten_b200/csrc/decode.cu): every tile of every
 (sequence, kv head) segment is owned by exactly one CTA, each CTA's range is
 contiguous and non-empty, partial segments use distinct workspace slots, and
-the number of pieces the merge waits for equals the number of CTAs that
-write one."""
+the pieces the merge kernel reads (CTAs ca..cb with slot wa for ca) are
+exactly the pieces the CTAs wrote."""
 from __future__ import annotations
 
 import numpy as np
@@ -59,7 +59,7 @@ def simulate(lens, hkv, grid):
             assert (s, g) not in writes
             continue
         w = writes[(s, g)]
-        assert len(w) == cb - ca + 1, "ticket count matches the pieces written"
+        assert len(w) == cb - ca + 1, "every CTA in ca..cb wrote a piece"
         wa = 1 if tile_begin(ca, U, C) != start else 0
         assert [x for x in w] == [(cc, wa if cc == ca else 0) for cc in range(ca, cb + 1)]
         for slot in w:
