@@ -33,10 +33,10 @@
 //              double-buffered per segment so an epilogue overlaps the next
 //              segment.
 // A segment cut by CTA boundaries leaves (m, l, O) partials in per-CTA
-// workspace slots and a descriptor from the CTA holding its last tile; a
-// second small kernel on the same stream merges each such segment's pieces
-// in CTA order, so results do not depend on scheduling.  Every wait is
-// bounded.
+// workspace slots.  After its last tile each CTA takes a ticket for the (at
+// most two) segments it only holds part of; the last CTA to arrive merges
+// that segment's pieces in CTA order (no spinning, nothing stalls the tile
+// pipeline), so results do not depend on scheduling.  Every wait is bounded.
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
@@ -77,9 +77,9 @@ struct DecodeParams {
   const int32_t* seq_lens;
   float qscale;  // scale * log2(e)
   int phantom;
-  float* ws_o;    // [ctas][2][16][D]   partial O of split segments
-  float* ws_ml;   // [ctas][2][16][2]   partial (m, l)
-  int4* ws_desc;  // [ctas] split segment ending in this CTA: (segment + 1, ca, cb, wa); x = 0: none
+  float* ws_o;           // [ctas][2][16][D]   partial O of split segments
+  float* ws_ml;          // [ctas][2][16][2]   partial (m, l)
+  unsigned int* ws_cnt;  // [n_seqs][hkv]      arrival tickets (left at zero)
   int* err;
 };
 
@@ -96,7 +96,8 @@ struct DCfg {
   static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort, last flag, start info
   static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums
   static constexpr int kOffScan = kOffRed + (2 * 4 * kN + 4 * kN) * 4;  // [6] warp totals
-  static constexpr int kSmallBytes = kOffScan + 64;
+  static constexpr int kOffPend = kOffScan + 64;                         // [2] int4 deferred merges
+  static constexpr int kSmallBytes = kOffPend + 32 + 16;
   static constexpr int kOffQ = 0;                          // [2] relative to the aligned operand area
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKVBytes;
@@ -234,6 +235,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
   float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
   int64_t* scan = reinterpret_cast<int64_t*>(smem_raw + C::kOffScan);  // [6]
+  int4* pend = reinterpret_cast<int4*>(smem_raw + C::kOffPend);        // [2] (segment, ca, cb, wa)
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffPend + 32);
   uint8_t* big = smem_raw + C::kSmallBytes;
   big += (1024 - (smem_u32(big) & 1023)) & 1023;
 
@@ -553,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     w.start(p, s0, pre0, t0, len0, pbeg0);
     float m_ref[NREP], l_tok[NREP];
     int seg = -1;
+    int n_pend = 0;  // partial segments written (at most the first and the last)
     bool ok = true;
     for (int i = 0; i < n_local; ++i) {
       const bool first = (i == 0) || w.j == 0;
@@ -676,17 +680,101 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
-          if (cta == cb && t == 0) {
-            // The segment's last piece records it for the merge kernel
-            // (the kernel boundary orders every piece's partials before it).
+          if (t == 0) {
+            // Ticket and merge come after this CTA's last tile.
             const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
-            p.ws_desc[cta] = make_int4(static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g) + 1,
-                                       static_cast<int>(ca), static_cast<int>(cb), wa);
+            pend[n_pend] = make_int4(static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g),
+                                     static_cast<int>(ca), static_cast<int>(cb), wa);
           }
+          ++n_pend;
         }
       }
       if (i + 1 < n_local) w.next(p);
     }
+
+    // ---- deferred merges: one ticket per partial segment; the last CTA to
+    // arrive merges the pieces in CTA order.
+    const int64_t U = *total_u;
+    for (int pi = 0; ok && pi < n_pend; ++pi) {
+      tc::named_sync(1, 128);  // pend[] and this CTA's partials are complete
+      const int4 pd = pend[pi];
+      if (t == 0) {
+        // One cumulative fence after the barrier publishes every thread's partials.
+        __threadfence();
+        const unsigned int ticket = atomicAdd(&p.ws_cnt[pd.x], 1u);
+        *last_flag = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
+        __threadfence();
+      }
+      tc::named_sync(1, 128);
+      if (!*last_flag) continue;
+      const int s = pd.x / p.hkv, g = pd.x - (pd.x / p.hkv) * p.hkv;
+      const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
+      const int ca = pd.y, np = pd.z - pd.y + 1, wa = pd.w;
+      constexpr int kElems = (NREP * D + 127) / 128;
+      constexpr int kChunk = C::kPBytes / (kN * 2 * 4);  // pieces staged per round in the idle P^T buffer
+      float* stage = reinterpret_cast<float*>(p_s);        // [kChunk][16][2]
+      float mrun[kElems], orun[kElems], lrun[kElems];
+#pragma unroll
+      for (int q = 0; q < kElems; ++q) {
+        mrun[q] = -INFINITY;
+        orun[q] = 0.0f;
+        lrun[q] = 0.0f;
+      }
+      for (int kb = 0; kb < np; kb += kChunk) {
+        const int nk = min(kChunk, np - kb);
+        for (int e = t; e < nk * NREP; e += 128) {
+          const int k = e / NREP, h = e - (e / NREP) * NREP;
+          const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
+          stage[(k * kN + h) * 2 + 0] = ld_cg(p.ws_ml + sl * 2 + 0);
+          stage[(k * kN + h) * 2 + 1] = ld_cg(p.ws_ml + sl * 2 + 1);
+        }
+        tc::named_sync(1, 128);
+#pragma unroll
+        for (int q = 0; q < kElems; ++q) {
+          const int e = t + q * 128;
+          if (e >= NREP * D) continue;
+          const int h = e / D, d = e - (e / D) * D;
+          float mc = -INFINITY;
+          for (int k = 0; k < nk; ++k) mc = fmaxf(mc, stage[(k * kN + h) * 2]);
+          if (mc == -INFINITY) continue;
+          const float mnew = fmaxf(mrun[q], mc);
+          const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
+          orun[q] *= a_old;
+          lrun[q] *= a_old;
+          mrun[q] = mnew;
+          for (int k0 = 0; k0 < nk; k0 += 4) {
+            float ov4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // four independent loads in flight
+              const int k = k0 + u;
+              ov4[u] = 0.0f;
+              if (k < nk) {
+                const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
+                ov4[u] = ld_cg(p.ws_o + sl * D + d);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int k = k0 + u;
+              if (k >= nk) break;
+              const float mk = stage[(k * kN + h) * 2];
+              if (mk == -INFINITY) continue;
+              const float a = exp2f(mk - mnew);
+              orun[q] += ov4[u] * a;
+              lrun[q] += stage[(k * kN + h) * 2 + 1] * a;
+            }
+          }
+        }
+        tc::named_sync(1, 128);  // the stage is rewritten by the next round
+      }
+#pragma unroll
+      for (int q = 0; q < kElems; ++q) {
+        const int e = t + q * 128;
+        if (e < NREP * D) store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
+      }
+      if (t == 0) p.ws_cnt[pd.x] = 0u;  // ready for the next call on this workspace
+    }
+    (void)U;
   }
 
   tc::fence_before_sync();
@@ -694,88 +782,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, C::kTmemCols);
-  }
-}
-
-// Merge of the pieces of segments split across CTAs, in CTA order.  One
-// block per descriptor slot; most slots are empty and exit at once.
-template <int D, int NREP>
-__global__ void __launch_bounds__(128) decode_merge_kernel(const __grid_constant__ DecodeParams p, int grid) {
-  constexpr int kElems = (NREP * D + 127) / 128;
-  constexpr int kChunk = 32;  // pieces staged per round
-  __shared__ float stage[kChunk * NREP * 2];
-  __shared__ int4 desc_s;
-  const int t = threadIdx.x;
-  for (int c = blockIdx.x; c < grid; c += gridDim.x) {
-    if (t == 0) desc_s = p.ws_desc[c];
-    __syncthreads();
-    const int4 dsc = desc_s;
-    __syncthreads();
-    if (dsc.x == 0) continue;
-    const int seg = dsc.x - 1, ca = dsc.y, cb = dsc.z, wa = dsc.w;
-    const int s = seg / p.hkv, g = seg - (seg / p.hkv) * p.hkv;
-    const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
-    const int np = cb - ca + 1;
-    float mrun[kElems], orun[kElems], lrun[kElems];
-#pragma unroll
-    for (int q = 0; q < kElems; ++q) {
-      mrun[q] = -INFINITY;
-      orun[q] = 0.0f;
-      lrun[q] = 0.0f;
-    }
-    for (int kb = 0; kb < np; kb += kChunk) {
-      const int nk = min(kChunk, np - kb);
-      for (int e = t; e < nk * NREP; e += 128) {
-        const int k = e / NREP, h = e - (e / NREP) * NREP;
-        const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
-        stage[(k * NREP + h) * 2 + 0] = p.ws_ml[sl * 2 + 0];
-        stage[(k * NREP + h) * 2 + 1] = p.ws_ml[sl * 2 + 1];
-      }
-      __syncthreads();
-#pragma unroll
-      for (int q = 0; q < kElems; ++q) {
-        const int e = t + q * 128;
-        if (e >= NREP * D) continue;
-        const int h = e / D, d = e - (e / D) * D;
-        float mc = -INFINITY;
-        for (int k = 0; k < nk; ++k) mc = fmaxf(mc, stage[(k * NREP + h) * 2]);
-        if (mc == -INFINITY) continue;
-        const float mnew = fmaxf(mrun[q], mc);
-        const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
-        orun[q] *= a_old;
-        lrun[q] *= a_old;
-        mrun[q] = mnew;
-        for (int k0 = 0; k0 < nk; k0 += 4) {
-          float ov[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {  // four independent loads in flight
-            const int k = k0 + u;
-            ov[u] = 0.0f;
-            if (k < nk) {
-              const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
-              ov[u] = p.ws_o[sl * D + d];
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int k = k0 + u;
-            if (k >= nk) break;
-            const float mk = stage[(k * NREP + h) * 2];
-            if (mk == -INFINITY) continue;
-            const float a = exp2f(mk - mnew);
-            orun[q] += ov[u] * a;
-            lrun[q] += stage[(k * NREP + h) * 2 + 1] * a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int q = 0; q < kElems; ++q) {
-      const int e = t + q * 128;
-      if (e < NREP * D) store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
-    }
-    if (t == 0) p.ws_desc[c] = make_int4(0, 0, 0, 0);  // ready for the next call on this workspace
   }
 }
 
@@ -793,10 +799,7 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
   }
   const int grid = sm_count() * C::kCtasPerSm;
   kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, tq, prm);
-  int st = check_launch("paged_decode_kernel");
-  if (st != MTN_OK) return st;
-  decode_merge_kernel<D, NREP><<<grid, 128, 0, stream>>>(prm, grid);
-  return check_launch("decode_merge_kernel");
+  return check_launch("paged_decode_kernel");
 }
 
 template <int D>
@@ -835,7 +838,7 @@ size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int
   const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(head_dim)) * 2 * mtn::kN;
   size_t bytes = static_cast<size_t>(slots) * head_dim * 4;    // ws_o
   bytes += static_cast<size_t>(slots) * 2 * 4;                   // ws_ml
-  bytes += static_cast<size_t>(mtn::decode_ctas(head_dim)) * 16;  // ws_desc
+  bytes += static_cast<size_t>(n_seqs) * num_kv_heads * 4;       // ws_cnt
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -903,7 +906,7 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(D)) * 2 * mtn::kN;
   prm.ws_o = static_cast<float*>(workspace);
   prm.ws_ml = prm.ws_o + slots * D;
-  prm.ws_desc = reinterpret_cast<int4*>(prm.ws_ml + slots * 2);
+  prm.ws_cnt = reinterpret_cast<unsigned int*>(prm.ws_ml + slots * 2);
   prm.err = mtn::device_error_ptr();
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
