@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
   int64_t* scan = reinterpret_cast<int64_t*>(smem_raw + C::kOffScan);  // [6]
   int4* pend = reinterpret_cast<int4*>(smem_raw + C::kOffPend);        // [2] (segment, ca, cb, wa)
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffPend + 32);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffPend + 32);  // [2]
   uint8_t* big = smem_raw + C::kSmallBytes;
   big += (1024 - (smem_u32(big) & 1023)) & 1023;
 
@@ -692,21 +692,24 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (i + 1 < n_local) w.next(p);
     }
 
-    // ---- deferred merges: one ticket per partial segment; the last CTA to
-    // arrive merges the pieces in CTA order.
-    const int64_t U = *total_u;
-    for (int pi = 0; ok && pi < n_pend; ++pi) {
+    // ---- deferred merges: one ticket per partial segment (both in one
+    // round trip); the last CTA to arrive merges the pieces in CTA order.
+    if (ok && n_pend > 0) {
       tc::named_sync(1, 128);  // pend[] and this CTA's partials are complete
-      const int4 pd = pend[pi];
-      if (t == 0) {
-        // One cumulative fence after the barrier publishes every thread's partials.
+      if (t < n_pend) {
+        const int4 pd = pend[t];
+        // One cumulative fence per ticket after the barrier publishes every
+        // thread's partials.
         __threadfence();
         const unsigned int ticket = atomicAdd(&p.ws_cnt[pd.x], 1u);
-        *last_flag = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
+        last_flag[t] = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
         __threadfence();
       }
       tc::named_sync(1, 128);
-      if (!*last_flag) continue;
+    }
+    for (int pi = 0; ok && pi < n_pend; ++pi) {
+      if (!last_flag[pi]) continue;
+      const int4 pd = pend[pi];
       const int s = pd.x / p.hkv, g = pd.x - (pd.x / p.hkv) * p.hkv;
       const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
       const int ca = pd.y, np = pd.z - pd.y + 1, wa = pd.w;
@@ -729,30 +732,38 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           stage[(k * kN + h) * 2 + 1] = ld_cg(p.ws_ml + sl * 2 + 1);
         }
         tc::named_sync(1, 128);
+        for (int k0 = 0; k0 < nk; k0 += 4) {
+          // Every O load of this round first (kElems x 4 in flight), then the math.
+          float ov4[kElems][4];
 #pragma unroll
-        for (int q = 0; q < kElems; ++q) {
-          const int e = t + q * 128;
-          if (e >= NREP * D) continue;
-          const int h = e / D, d = e - (e / D) * D;
-          float mc = -INFINITY;
-          for (int k = 0; k < nk; ++k) mc = fmaxf(mc, stage[(k * kN + h) * 2]);
-          if (mc == -INFINITY) continue;
-          const float mnew = fmaxf(mrun[q], mc);
-          const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
-          orun[q] *= a_old;
-          lrun[q] *= a_old;
-          mrun[q] = mnew;
-          for (int k0 = 0; k0 < nk; k0 += 4) {
-            float ov4[4];
+          for (int q = 0; q < kElems; ++q) {
+            const int e = t + q * 128;
+            const int h = e / D, d = e - (e / D) * D;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {  // four independent loads in flight
+            for (int u = 0; u < 4; ++u) {
               const int k = k0 + u;
-              ov4[u] = 0.0f;
-              if (k < nk) {
+              ov4[q][u] = 0.0f;
+              if (e < NREP * D && k < nk) {
                 const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
-                ov4[u] = ld_cg(p.ws_o + sl * D + d);
+                ov4[q][u] = ld_cg(p.ws_o + sl * D + d);
               }
             }
+          }
+#pragma unroll
+          for (int q = 0; q < kElems; ++q) {
+            const int e = t + q * 128;
+            if (e >= NREP * D) continue;
+            const int h = e / D;
+            float mc = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (k0 + u < nk) mc = fmaxf(mc, stage[((k0 + u) * kN + h) * 2]);
+            if (mc == -INFINITY) continue;
+            const float mnew = fmaxf(mrun[q], mc);
+            const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
+            orun[q] *= a_old;
+            lrun[q] *= a_old;
+            mrun[q] = mnew;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int k = k0 + u;
@@ -760,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               const float mk = stage[(k * kN + h) * 2];
               if (mk == -INFINITY) continue;
               const float a = exp2f(mk - mnew);
-              orun[q] += ov4[u] * a;
+              orun[q] += ov4[q][u] * a;
               lrun[q] += stage[(k * kN + h) * 2 + 1] * a;
             }
           }
@@ -774,7 +785,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       }
       if (t == 0) p.ws_cnt[pd.x] = 0u;  // ready for the next call on this workspace
     }
-    (void)U;
   }
 
   tc::fence_before_sync();
