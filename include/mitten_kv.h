@@ -173,6 +173,31 @@ MTN_API int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer,
                      float scale, uint32_t flags,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of mtn_paged_decode (no counterpart in the
+ * reference).  For callers that cannot call cudaMalloc: a host engine whose
+ * device memory is all handed out up front by its own arena (the KV pool
+ * typically takes nearly all of HBM), or a serving loop that must not
+ * allocate mid-step because cudaMalloc can synchronise the device and stall
+ * the streams in flight.  Same arguments and results as mtn_paged_decode,
+ * without the workspace: the scratch is a static 8 MiB device array inside
+ * this library, present on every GPU that loads it until the process exits.
+ * Batches needing more scratch than that (mtn_paged_decode_workspace_bytes
+ * > 8 MiB: on a 148-SM B200, more than about 1.4 million sequence x kv-head
+ * pairs at head_dim 64, or 0.7 million at head_dim 256) are rejected with
+ * MTN_EINVAL.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress with that device current), so make that
+ * first call before any stream capture.  Every call on a device shares the
+ * one array and it keeps the previous call's contents; the part that must
+ * start at zero is cleared on the call's stream.  Calls that can overlap on
+ * the GPU (different streams without ordering between them) race on the
+ * array: serialise them. */
+MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
+                     const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
+                     const void* k_new, const void* v_new, int32_t new_dtype,
+                     int32_t n_seqs, int32_t num_q_heads,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
+                     float scale, uint32_t flags, void* stream);
+
 /* Chunked-prefill attention over paged KV (tcgen05 / TMEM tensor cores).
  *   q: [total_q][num_q_heads][head_dim] bf16; o: same shape (o_dtype).
  *   Sequence r owns query rows qo_indptr[r] .. qo_indptr[r+1]; those are its

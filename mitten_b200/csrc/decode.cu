@@ -40,10 +40,15 @@
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "tc.cuh"
 #include "tmaps.hpp"
+
+// Scratch of mtn_paged_decode_noalloc: a file-scope device array, so the
+// library image itself reserves it on every device that loads it.
+static __device__ __align__(256) unsigned char mtn_noalloc_decode_scratch[8u << 20];
 
 namespace mtn {
 namespace {
@@ -928,3 +933,62 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point: the workspace is mtn_noalloc_decode_scratch.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = sizeof(mtn_noalloc_decode_scratch);
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  MTN_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return mtn::set_error(MTN_EINVAL, "mtn_paged_decode_noalloc: device %d unsupported", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, mtn_noalloc_decode_scratch);
+    if (e != cudaSuccess) return mtn::cuda_status(e, "cudaGetSymbolAddress(mtn_noalloc_decode_scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return MTN_OK;
+}
+
+}  // namespace
+
+extern "C" int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype,
+                                        void* o, int32_t o_dtype, const void* k_new, const void* v_new,
+                                        int32_t new_dtype, int32_t n_seqs, int32_t num_q_heads,
+                                        const int32_t* kv_indptr, const int32_t* kv_indices,
+                                        const int32_t* seq_lens, float scale, uint32_t flags, void* stream) {
+  MTN_CHECK_ARG(pool != nullptr, "mtn_paged_decode_noalloc: null pool");
+  MTN_CHECK_ARG(n_seqs >= 0, "mtn_paged_decode_noalloc: n_seqs < 0");
+  if (n_seqs == 0) return MTN_OK;
+  const int D = pool->head_dim;
+  MTN_CHECK_ARG(D == 64 || D == 128 || D == 256, "mtn_paged_decode_noalloc: head_dim %d not in {64,128,256}", D);
+  MTN_CHECK_ARG(pool->num_kv_heads > 0, "mtn_paged_decode_noalloc: bad pool");
+  const size_t need = mtn_paged_decode_workspace_bytes(n_seqs, num_q_heads, pool->num_kv_heads, D);
+  MTN_CHECK_ARG(need > 0 && need <= kNoAllocScratchBytes,
+                "mtn_paged_decode_noalloc: %d sequences x %d kv heads need %zu bytes of scratch; the static scratch "
+                "holds %zu (use mtn_paged_decode with a caller workspace)",
+                n_seqs, pool->num_kv_heads, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st != MTN_OK) return st;
+  // The arrival counters must start at zero.  Calls leave them zero, but a
+  // call that failed part-way may not have: clear them on this stream.
+  const int64_t slots = static_cast<int64_t>(mtn::decode_ctas(D)) * 2 * mtn::kN;
+  const size_t cnt_off = static_cast<size_t>(slots) * (D + 2) * 4;
+  const size_t cnt_bytes = static_cast<size_t>(n_seqs) * pool->num_kv_heads * 4;
+  MTN_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(scratch) + cnt_off, 0, cnt_bytes,
+                               static_cast<cudaStream_t>(stream)),
+               "cudaMemsetAsync(decode scratch counters)");
+  return mtn_paged_decode(pool, layer, q, q_dtype, o, o_dtype, k_new, v_new, new_dtype, n_seqs, num_q_heads,
+                          kv_indptr, kv_indices, seq_lens, scale, flags, scratch, kNoAllocScratchBytes, stream);
+}
