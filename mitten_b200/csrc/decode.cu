@@ -250,6 +250,16 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int tid = threadIdx.x;
   const int64_t cta = blockIdx.x;
 
+  // TMEM first.  Measured with %globaltimer on B200: the second CTA of an SM
+  // started only once the first had allocated TMEM and given up its
+  // allocation permit (2.5 us late when that came after the metadata scan,
+  // 0.7 us when it comes first).
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+  }
+
   // ------------------------------------------------------------ work split
   // Tiles per sequence (for one kv head), prefix-summed over the CTA; each
   // thread owns a contiguous chunk of sequences.
@@ -312,29 +322,25 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
   if (tid == 0) *total_u = U;
   __syncthreads();
-  if (n_local == 0) return;  // uniform over the CTA; nothing allocated yet
-  if (*start_s < 0 || *start_s >= p.n_seqs) {  // cannot happen for consistent metadata
-    if (tid == 0) record_error(p.err, kDevErrBadSeqLen, -1);
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+  // Uniform over the CTA.  The bad start cannot happen for consistent metadata.
+  const bool bad_start = n_local > 0 && (*start_s < 0 || *start_s >= p.n_seqs);
+  if (n_local == 0 || bad_start) {
+    if (bad_start && tid == 0) record_error(p.err, kDevErrBadSeqLen, -1);
+    if (warp == 0) tc::tmem_dealloc(tmem, C::kTmemCols);
     return;
   }
 
   uint8_t* p_s = big + C::kOffP;
-  uint32_t tmem = 0;
   if (warp != 4) {
-    // TMEM and the zeroed P^T operand (rows >= NREP stay zero) for the MMA
-    // and softmax roles; the producer starts loading meanwhile.
-    if (warp == 0) {
-      tc::tmem_alloc(tmem_base_s, C::kTmemCols);
-      tc::tmem_relinquish();
-    }
+    // The zeroed P^T operand (rows >= NREP stay zero) for the MMA and
+    // softmax roles; the producer starts loading meanwhile.
     const int tid160 = warp == 5 ? 128 + lane : tid;
     uint4* pz = reinterpret_cast<uint4*>(p_s);
     for (int e = tid160; e < C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_shared();
-    tc::fence_before_sync();
     tc::named_sync(2, 160);
-    tc::fence_after_sync();
-    tmem = *tmem_base_s;
   }
   const int s0 = *start_s;
   const int64_t pre0 = *start_pre;
@@ -347,121 +353,144 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       tc::prefetch_tmap(&tm_kv);
       if (!p.q_f32) tc::prefetch_tmap(&tm_q);
     }
-    Walker w;
+    Walker w;   // the tile whose loads are issued
     w.start(p, s0, pre0, t0, len0, pbeg0);
+    Walker wp = w;  // the tile whose page ids are fetched, kStages tiles ahead
     int qcnt = 0;
-    // Page id of this lane's page of the next tile, and (when that tile ends
-    // its segment) this step's K/V row for the fused append: loaded one tile
-    // ahead so they overlap the wait for a free stage.
-    int64_t pg_next = 0, app_row = -1;
-    uint4 app_k = make_uint4(0u, 0u, 0u, 0u), app_v = app_k;
-    auto prefetch = [&]() {
-      const int npg = (w.len + p.ps - 1) / p.ps;
-      if (lane < tile_pages) {
-        int64_t page = p.kv_indices[w.pbeg + min(w.j * tile_pages + lane, npg - 1)];
-        if (page < 0 || page >= p.num_pages) {
-          record_error(p.err, kDevErrBadPage, w.s);
-          page = 0;  // past the sequence's last page: reload a valid page (masked)
-        }
-        pg_next = page;
-      }
-      app_row = -1;
-      if (p.k_new != nullptr && w.j == w.T - 1) {
-        const int pos = w.len - 1;
-        const int64_t page = p.kv_indices[w.pbeg + pos / p.ps];
-        if (page < 0 || page >= p.num_pages) {
-          record_error(p.err, kDevErrBadPage, w.s);
-        } else {
-          app_row = (page * p.hkv + w.g) * p.ps + pos % p.ps;
-          if (lane < D / 8) {
-            const int64_t src = (static_cast<int64_t>(w.s) * p.hkv + w.g) * D + lane * 8;
-            if (p.new_f32) {
-              const float* kf = static_cast<const float*>(p.k_new) + src;
-              const float* vf = static_cast<const float*>(p.v_new) + src;
-              const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
-              const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
-              app_k = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
-                                 f2_to_bf2(k1.z, k1.w));
-              app_v = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
-                                 f2_to_bf2(v1.z, v1.w));
-            } else {
-              app_k = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
-              app_v = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
-            }
+    // Per stage slot: this lane's page id of the slot's tile and, when that
+    // tile ends its segment, the page and offset of this step's K/V row for
+    // the fused append plus the row itself.  Fetched kStages tiles ahead, so
+    // the first kStages tiles are issued back to back and later fetches
+    // overlap the wait for a free stage; the ids are checked only when used,
+    // so no fetch waits for its own load.
+    int pg[C::kStages], apg[C::kStages], apos[C::kStages];
+    uint4 ak[C::kStages], av[C::kStages];
+    auto fetch = [&](int& pg_o, int& apg_o, int& apos_o, uint4& ak_o, uint4& av_o) {
+      const int npg = (wp.len + p.ps - 1) / p.ps;
+      pg_o = 0;
+      if (lane < tile_pages) pg_o = p.kv_indices[wp.pbeg + min(wp.j * tile_pages + lane, npg - 1)];
+      apos_o = -1;  // no append
+      apg_o = 0;
+      ak_o = make_uint4(0u, 0u, 0u, 0u);
+      av_o = ak_o;
+      if (p.k_new != nullptr && wp.j == wp.T - 1) {
+        const int pos = wp.len - 1;
+        apos_o = pos % p.ps;
+        apg_o = p.kv_indices[wp.pbeg + pos / p.ps];
+        if (lane < D / 8) {
+          const int64_t src = (static_cast<int64_t>(wp.s) * p.hkv + wp.g) * D + lane * 8;
+          if (p.new_f32) {
+            const float* kf = static_cast<const float*>(p.k_new) + src;
+            const float* vf = static_cast<const float*>(p.v_new) + src;
+            const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
+            const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
+            ak_o = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
+                              f2_to_bf2(k1.z, k1.w));
+            av_o = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
+                              f2_to_bf2(v1.z, v1.w));
+          } else {
+            ak_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
+            av_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
           }
         }
       }
     };
-    prefetch();
-    for (int i = 0; i < n_local; ++i) {
-      const bool first = (i == 0) || w.j == 0;
-      if (first) {
-        const int qb = qcnt & 1;
-        if (qcnt >= 2) {
+#pragma unroll
+    for (int k = 0; k < C::kStages; ++k) {
+      if (k < n_local) fetch(pg[k], apg[k], apos[k], ak[k], av[k]);
+      if (k + 1 < n_local) wp.next(p);
+    }
+    bool run = true;
+    // Stage slot st of round i0 is tile i0 + st: unrolled so the ring
+    // registers are indexed with constants.
+    for (int i0 = 0; run && i0 < n_local; i0 += C::kStages) {
+#pragma unroll
+      for (int st = 0; st < C::kStages; ++st) {
+        const int i = i0 + st;
+        if (!run || i >= n_local) break;
+        const bool first = (i == 0) || w.j == 0;
+        if (first) {
+          const int qb = qcnt & 1;
+          if (qcnt >= 2) {
+            bool ok = true;
+            if (lane == 0) ok = tc::wait_bounded(&bars[kQEmpty0 + qb], ((qcnt >> 1) - 1) & 1, abort_flag, p.err, 11);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+              run = false;
+              break;
+            }
+          }
+          uint8_t* q_s = big + C::kOffQ + qb * C::kQBytes;
+          const int qrow = w.s * p.hq + w.g * NREP;
+          if (!p.q_f32) {
+            // Rows past NREP belong to other heads (or lie past the end and
+            // read as zero): their S^T columns are never used.
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&bars[kQFull0 + qb], C::kQBytes);
+#pragma unroll
+              for (int b = 0; b < C::kDB; ++b)
+                tc::tma_load_3d(q_s + b * (kN * 128), &tm_q, b * 64, 0, qrow, &bars[kQFull0 + qb]);
+            }
+          } else {
+            for (int e = lane; e < NREP * (D / 8); e += 32) {
+              const int r = e / (D / 8), c = e - r * (D / 8);
+              const float* src = static_cast<const float*>(p.q) + (static_cast<int64_t>(qrow) + r) * D + c * 8;
+              const float4 a = *reinterpret_cast<const float4*>(src);
+              const float4 b2 = *reinterpret_cast<const float4*>(src + 4);
+              *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+                  make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(b2.x, b2.y), f2_to_bf2(b2.z, b2.w));
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars[kQFull0 + qb]);
+          }
+          ++qcnt;
+        }
+        if (i >= C::kStages) {
           bool ok = true;
-          if (lane == 0) ok = tc::wait_bounded(&bars[kQEmpty0 + qb], ((qcnt >> 1) - 1) & 1, abort_flag, p.err, 11);
-          if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+          if (lane == 0)
+            ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((i / C::kStages) - 1) & 1, abort_flag, p.err, 10);
+          if (!__shfl_sync(0xffffffffu, ok, 0)) {
+            run = false;
+            break;
+          }
         }
-        uint8_t* q_s = big + C::kOffQ + qb * C::kQBytes;
-        const int qrow = w.s * p.hq + w.g * NREP;
-        if (!p.q_f32) {
-          // Rows past NREP belong to other heads (or lie past the end and
-          // read as zero): their S^T columns are never used.
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&bars[kQFull0 + qb], C::kQBytes);
-#pragma unroll
-            for (int b = 0; b < C::kDB; ++b)
-              tc::tma_load_3d(q_s + b * (kN * 128), &tm_q, b * 64, 0, qrow, &bars[kQFull0 + qb]);
+        if (apos[st] >= 0) {
+          // Fused KV append: store this step's row at position len-1, then
+          // order it before the async-proxy (TMA) read of the same page.
+          if (apg[st] < 0 || apg[st] >= p.num_pages) {
+            if (lane == 0) record_error(p.err, kDevErrBadPage, w.s);
+          } else if (lane < D / 8) {
+            const int64_t arow = (static_cast<int64_t>(apg[st]) * p.hkv + w.g) * p.ps + apos[st];
+            *reinterpret_cast<uint4*>(p.pool + (p.row_k + arow) * D + lane * 8) = ak[st];
+            *reinterpret_cast<uint4*>(p.pool + (p.row_v + arow) * D + lane * 8) = av[st];
+            asm volatile("fence.proxy.async.global;" ::: "memory");
           }
-        } else {
-          for (int e = lane; e < NREP * (D / 8); e += 32) {
-            const int r = e / (D / 8), c = e - r * (D / 8);
-            const float* src = static_cast<const float*>(p.q) + (static_cast<int64_t>(qrow) + r) * D + c * 8;
-            const float4 a = *reinterpret_cast<const float4*>(src);
-            const float4 b2 = *reinterpret_cast<const float4*>(src + 4);
-            *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
-                make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(b2.x, b2.y), f2_to_bf2(b2.z, b2.w));
-          }
-          fence_proxy_async_shared();
           __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&bars[kQFull0 + qb]);
         }
-        ++qcnt;
-      }
-      const int st = i % C::kStages;
-      if (i >= C::kStages) {
-        bool ok = true;
-        if (lane == 0)
-          ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((i / C::kStages) - 1) & 1, abort_flag, p.err, 10);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      }
-      if (app_row >= 0) {
-        // Fused KV append: store this step's row at position len-1, then
-        // order it before the async-proxy (TMA) read of the same page.
-        if (lane < D / 8) {
-          *reinterpret_cast<uint4*>(p.pool + (p.row_k + app_row) * D + lane * 8) = app_k;
-          *reinterpret_cast<uint4*>(p.pool + (p.row_v + app_row) * D + lane * 8) = app_v;
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-        }
+        if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
         __syncwarp();
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
-      __syncwarp();
-      if (lane < tile_pages) {
-        const int64_t rk = p.row_k + (pg_next * p.hkv + w.g) * p.ps;
-        const int64_t rv = p.row_v + (pg_next * p.hkv + w.g) * p.ps;
-        uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
-        uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
+        if (lane < tile_pages) {
+          int64_t page = pg[st];
+          if (page < 0 || page >= p.num_pages) {
+            record_error(p.err, kDevErrBadPage, w.s);
+            page = 0;  // past the sequence's last page: reload a valid page (masked)
+          }
+          const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
+          const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
+          uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
+          uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
 #pragma unroll
-        for (int b = 0; b < C::kDB; ++b) {
-          const int off = b * kTile * 128 + lane * p.ps * 128;
-          tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
-          tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
+          for (int b = 0; b < C::kDB; ++b) {
+            const int off = b * kTile * 128 + lane * p.ps * 128;
+            tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
+            tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
+          }
         }
-      }
-      if (i + 1 < n_local) {
-        w.next(p);
-        prefetch();
+        if (i + C::kStages < n_local) {
+          fetch(pg[st], apg[st], apos[st], ak[st], av[st]);  // wp is at tile i + kStages
+          if (i + C::kStages + 1 < n_local) wp.next(p);
+        }
+        if (i + 1 < n_local) w.next(p);
       }
     }
   } else if (warp == 5) {
@@ -562,6 +591,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     float m_ref[NREP], l_tok[NREP];
     int seg = -1;
     int n_pend = 0;  // partial segments written (at most the first and the last)
+    bool early = false;             // pend[0] already holds its ticket (thread 0)
+    unsigned int early_ticket = 0;  // that ticket
     bool ok = true;
     for (int i = 0; i < n_local; ++i) {
       const bool first = (i == 0) || w.j == 0;
@@ -685,11 +716,22 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
+          const int seg_id = static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g);
           if (t == 0) {
-            // Ticket and merge come after this CTA's last tile.
             const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
-            pend[n_pend] = make_int4(static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g),
-                                     static_cast<int>(ca), static_cast<int>(cb), wa);
+            pend[n_pend] = make_int4(seg_id, static_cast<int>(ca), static_cast<int>(cb), wa);
+          }
+          if (cta == cb && i + 1 < n_local) {
+            // The tail of a segment whose other pieces end their CTAs' ranges:
+            // take the ticket now (those CTAs arrive later), so that at most
+            // one merge is left for the end.  Only thread 0 waits on the fence;
+            // the ticket value is first needed after the last tile.
+            tc::named_sync(1, 128);  // every thread's partial is written
+            if (t == 0) {
+              __threadfence();
+              early_ticket = atomicAdd(&p.ws_cnt[seg_id], 1u);
+            }
+            early = true;
           }
           ++n_pend;
         }
@@ -697,16 +739,22 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (i + 1 < n_local) w.next(p);
     }
 
-    // ---- deferred merges: one ticket per partial segment (both in one
-    // round trip); the last CTA to arrive merges the pieces in CTA order.
+    // ---- deferred merges: one ticket per partial segment not yet ticketed
+    // (both in one round trip); the last CTA to arrive merges the pieces in
+    // CTA order.
     if (ok && n_pend > 0) {
       tc::named_sync(1, 128);  // pend[] and this CTA's partials are complete
       if (t < n_pend) {
         const int4 pd = pend[t];
-        // One cumulative fence per ticket after the barrier publishes every
-        // thread's partials.
-        __threadfence();
-        const unsigned int ticket = atomicAdd(&p.ws_cnt[pd.x], 1u);
+        unsigned int ticket;
+        if (t == 0 && early) {
+          ticket = early_ticket;
+        } else {
+          // One cumulative fence per ticket after the barrier publishes
+          // every thread's partials.
+          __threadfence();
+          ticket = atomicAdd(&p.ws_cnt[pd.x], 1u);
+        }
         last_flag[t] = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
         __threadfence();
       }
@@ -719,8 +767,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
       const int ca = pd.y, np = pd.z - pd.y + 1, wa = pd.w;
       constexpr int kElems = (NREP * D + 127) / 128;
-      constexpr int kChunk = C::kPBytes / (kN * 2 * 4);  // pieces staged per round in the idle P^T buffer
-      float* stage = reinterpret_cast<float*>(p_s);        // [kChunk][16][2]
+      constexpr int kChunk = 4;                       // pieces per round: one round trip each
+      float* stage = reinterpret_cast<float*>(p_s);  // [kChunk][16][2] (m, l) in the idle P^T buffer
       float mrun[kElems], orun[kElems], lrun[kElems];
 #pragma unroll
       for (int q = 0; q < kElems; ++q) {
@@ -730,55 +778,57 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       }
       for (int kb = 0; kb < np; kb += kChunk) {
         const int nk = min(kChunk, np - kb);
-        for (int e = t; e < nk * NREP; e += 128) {
-          const int k = e / NREP, h = e - (e / NREP) * NREP;
-          const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
-          stage[(k * kN + h) * 2 + 0] = ld_cg(p.ws_ml + sl * 2 + 0);
-          stage[(k * kN + h) * 2 + 1] = ld_cg(p.ws_ml + sl * 2 + 1);
-        }
-        tc::named_sync(1, 128);
-        for (int k0 = 0; k0 < nk; k0 += 4) {
-          // Every O load of this round first (kElems x 4 in flight), then the math.
-          float ov4[kElems][4];
+        // This round's O loads and (m, l) loads all in flight together.
+        float ov4[kElems][kChunk];
 #pragma unroll
-          for (int q = 0; q < kElems; ++q) {
-            const int e = t + q * 128;
-            const int h = e / D, d = e - (e / D) * D;
+        for (int q = 0; q < kElems; ++q) {
+          const int e = t + q * 128;
+          const int h = e / D, d = e - (e / D) * D;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int k = k0 + u;
-              ov4[q][u] = 0.0f;
-              if (e < NREP * D && k < nk) {
-                const int64_t sl = (static_cast<int64_t>(ca + kb + k) * 2 + (kb + k == 0 ? wa : 0)) * kN + h;
-                ov4[q][u] = ld_cg(p.ws_o + sl * D + d);
-              }
+          for (int u = 0; u < kChunk; ++u) {
+            const int k = kb + u;
+            ov4[q][u] = 0.0f;
+            if (e < NREP * D && u < nk) {
+              const int64_t sl = (static_cast<int64_t>(ca + k) * 2 + (k == 0 ? wa : 0)) * kN + h;
+              ov4[q][u] = ld_cg(p.ws_o + sl * D + d);
             }
           }
+        }
+        float2 ml = make_float2(-INFINITY, 0.0f);
+        const int mk_ = t / NREP, mh = t - (t / NREP) * NREP;
+        if (t < nk * NREP) {
+          const int k = kb + mk_;
+          const int64_t sl = (static_cast<int64_t>(ca + k) * 2 + (k == 0 ? wa : 0)) * kN + mh;
+          ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + sl * 2));
+        }
+        if (t < nk * NREP) {
+          stage[(mk_ * kN + mh) * 2 + 0] = ml.x;
+          stage[(mk_ * kN + mh) * 2 + 1] = ml.y;
+        }
+        tc::named_sync(1, 128);
 #pragma unroll
-          for (int q = 0; q < kElems; ++q) {
-            const int e = t + q * 128;
-            if (e >= NREP * D) continue;
-            const int h = e / D;
-            float mc = -INFINITY;
+        for (int q = 0; q < kElems; ++q) {
+          const int e = t + q * 128;
+          if (e >= NREP * D) continue;
+          const int h = e / D;
+          float mc = -INFINITY;
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (k0 + u < nk) mc = fmaxf(mc, stage[((k0 + u) * kN + h) * 2]);
-            if (mc == -INFINITY) continue;
-            const float mnew = fmaxf(mrun[q], mc);
-            const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
-            orun[q] *= a_old;
-            lrun[q] *= a_old;
-            mrun[q] = mnew;
+          for (int u = 0; u < kChunk; ++u)
+            if (u < nk) mc = fmaxf(mc, stage[(u * kN + h) * 2]);
+          if (mc == -INFINITY) continue;
+          const float mnew = fmaxf(mrun[q], mc);
+          const float a_old = (mrun[q] == -INFINITY) ? 0.0f : exp2f(mrun[q] - mnew);
+          orun[q] *= a_old;
+          lrun[q] *= a_old;
+          mrun[q] = mnew;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int k = k0 + u;
-              if (k >= nk) break;
-              const float mk = stage[(k * kN + h) * 2];
-              if (mk == -INFINITY) continue;
-              const float a = exp2f(mk - mnew);
-              orun[q] += ov4[q][u] * a;
-              lrun[q] += stage[(k * kN + h) * 2 + 1] * a;
-            }
+          for (int u = 0; u < kChunk; ++u) {
+            if (u >= nk) break;
+            const float mk = stage[(u * kN + h) * 2];
+            if (mk == -INFINITY) continue;
+            const float a = exp2f(mk - mnew);
+            orun[q] += ov4[q][u] * a;
+            lrun[q] += stage[(u * kN + h) * 2 + 1] * a;
           }
         }
         tc::named_sync(1, 128);  // the stage is rewritten by the next round
