@@ -98,7 +98,7 @@ struct DCfg {
   static constexpr int kPBytes = kN * kTile * 2;           // P^T operand: 16 rows x 128 tokens
   // Small state first, then the 1 KiB-aligned operand area.
   static constexpr int kOffBar = 0;                        // 16 mbarriers
-  static constexpr int kOffMisc = kOffBar + 16 * 8;        // tmem base, abort, last flag, start info
+  static constexpr int kOffMisc = kOffBar + 24 * 8;        // tmem base, abort, last flag, start info
   static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums
   static constexpr int kOffScan = kOffRed + (2 * 4 * kN + 4 * kN) * 4;  // [6] warp totals
   static constexpr int kOffPend = kOffScan + 64;                         // [2] int4 deferred merges
@@ -107,7 +107,7 @@ struct DCfg {
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKVBytes;
   static constexpr int kOffP = kOffV + kStages * kKVBytes;
-  static constexpr int kBigBytes = kOffP + kPBytes;
+  static constexpr int kBigBytes = kOffP + 2 * kPBytes;  // P^T double-buffered
   static constexpr int kSmem = kSmallBytes + 1023 + kBigBytes;
   static constexpr int kMO = D == 64 ? 64 : 128;           // MMA2 M
   static constexpr int kTmemS = 0;                          // [2] x 16 columns
@@ -120,12 +120,12 @@ enum Bar {
   kKVFull0 = 0,   // [3]
   kKVEmpty0 = 3,  // [3]
   kSFull0 = 6,    // [2]
-  kPFull = 8,
-  kODone = 9,
-  kQFull0 = 10,   // [2]
-  kQEmpty0 = 12,  // [2]
-  kOFree0 = 14,   // [2]
-  kNumBars = 16
+  kPFull0 = 8,    // [2] P^T buffer i&1 written (softmax -> MMA)
+  kODone0 = 10,   // [2] P V of tile i done: P^T buffer i&1 free, O^T current
+  kQFull0 = 12,   // [2]
+  kQEmpty0 = 14,  // [2]
+  kOFree0 = 16,   // [2]
+  kNumBars = 18
 };
 
 // Final normalisation of one output element: o/l with the phantom key folded in.
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i == kPFull || i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
+      mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1 || i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
     *abort_flag = 0;
     *start_s = -1;
     fence_barrier_init();
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     // softmax roles; the producer starts loading meanwhile.
     const int tid160 = warp == 5 ? 128 + lane : tid;
     uint4* pz = reinterpret_cast<uint4*>(p_s);
-    for (int e = tid160; e < C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+    for (int e = tid160; e < 2 * C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_shared();
     tc::named_sync(2, 160);
   }
@@ -498,12 +498,18 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kTile, kN, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(C::kMO, kN, false, true);
-      const uint32_t p_addr = smem_u32(p_s);
       Walker wsw, wo;  // wsw: tiles whose S^T is issued; wo: tiles whose O^T is issued
       wsw.start(p, s0, pre0, t0, len0, pbeg0);
       wo.start(p, s0, pre0, t0, len0, pbeg0);
       int q_seg = -1;  // segment counter of the S^T issue
       int o_seg = -1;  // segment counter of the O^T issue
+      // Operand descriptors of stage 0 / buffer 0 at k = 0; the others add
+      // their byte offset >> 4 to the start-address field (shared addresses
+      // stay below 256 KB, so the 14-bit field never carries).
+      const uint64_t dK = tc::sdesc_sw128(smem_u32(big + C::kOffK), 16, 1024);
+      const uint64_t dQ = tc::sdesc_sw128(smem_u32(big + C::kOffQ), 16, 1024);
+      const uint64_t dV = tc::sdesc_sw128(smem_u32(big + C::kOffV), kTile * 128, 1024);
+      const uint64_t dP = tc::sdesc_sw128(smem_u32(p_s), 16, 1024);
       // S^T(i) = K_i Q^T into S buffer i&1: both operands K-major; 16-wide
       // k steps walk 32 bytes inside a 128-byte swizzle row, then the next block.
       auto issue_s = [&](int i) -> bool {
@@ -516,14 +522,12 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         const int st = i % C::kStages;
         if (!tc::wait_bounded(&bars[kKVFull0 + st], (i / C::kStages) & 1, abort_flag, p.err, 20)) return false;
         tc::fence_after_sync();
-        const uint32_t k_s = smem_u32(big + C::kOffK + st * C::kKVBytes);
-        const uint32_t q_s = smem_u32(big + C::kOffQ + (q_seg & 1) * C::kQBytes);
+        const uint64_t a0 = dK + ((st * C::kKVBytes) >> 4);
+        const uint64_t b0 = dQ + (((q_seg & 1) * C::kQBytes) >> 4);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint64_t a = tc::sdesc_sw128(k_s + (k >> 2) * kTile * 128 + (k & 3) * 32, 16, 1024);
-          const uint64_t b = tc::sdesc_sw128(q_s + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
-          tc::mma_bf16(tmem + C::kTmemS + (i & 1) * kN, a, b, idS, k > 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < D / 16; ++k)
+          tc::mma_bf16(tmem + C::kTmemS + (i & 1) * kN, a0 + (((k >> 2) * kTile * 128 + (k & 3) * 32) >> 4),
+                       b0 + (((k >> 2) * kN * 128 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
         tc::mma_commit(&bars[kSFull0 + (i & 1)]);
         if (last) tc::mma_commit(&bars[kQEmpty0 + (q_seg & 1)]);
         if (i + 1 < n_local) wsw.next(p);
@@ -535,16 +539,14 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (first && !mbar_test_wait(&bars[kQFull0 + ((q_seg + 1) & 1)], ((q_seg + 1) >> 1) & 1)) return false;
         return mbar_test_wait(&bars[kKVFull0 + j % C::kStages], (j / C::kStages) & 1);
       };
-      bool ok = issue_s(0);
-      int next_s = 1;  // next tile whose S^T is not issued yet
+      bool ok = true;
+      int next_s = 0;  // next tile whose S^T is not issued yet
       for (int i = 0; ok && i < n_local; ++i) {
-        // Overlap the next tile's S^T with this tile's softmax when its K/V
-        // already landed (its S buffer was released by the softmax of tile
-        // i-1, waited on below), but never let that wait hold up this P V.
-        if (C::kStages > 1 && next_s == i + 1 && next_s < n_local && s_ready(next_s)) {
-          if (!issue_s(next_s)) break;
+        while (ok && next_s <= i) {
+          ok = issue_s(next_s);
           ++next_s;
         }
+        if (!ok) break;
         const bool first = (i == 0) || wo.j == 0;
         if (first) {
           ++o_seg;
@@ -552,30 +554,54 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               !tc::wait_bounded(&bars[kOFree0 + (o_seg & 1)], ((o_seg >> 1) - 1) & 1, abort_flag, p.err, 23))
             break;
         }
-        if (!tc::wait_bounded(&bars[kPFull], i & 1, abort_flag, p.err, 21)) break;
+        // Wait for P^T(i); meanwhile issue S^T(i+1) as soon as its K/V land
+        // (its S buffer was released by the softmax of tile i-1, whose P^T
+        // was waited on in the previous iteration).
+        {
+          uint64_t* pf = &bars[kPFull0 + (i & 1)];
+          const uint32_t par = (i >> 1) & 1;
+          uint64_t t_start = 0;
+          for (uint32_t it = 0;; ++it) {
+            if (next_s == i + 1 && next_s < n_local && s_ready(next_s)) {
+              ok = issue_s(next_s);
+              ++next_s;
+              if (!ok) break;
+            }
+            if (mbar_test_wait(pf, par)) break;
+            if ((it & 255u) == 0) {
+              const uint64_t now = tc::global_timer_ns();
+              if (it == 0) t_start = now;
+              if (*abort_flag) {
+                ok = false;
+                break;
+              }
+              if (now - t_start > 1000000000ull) {
+                record_error(p.err, kDevErrTimeout, 21);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+            }
+          }
+          if (!ok) break;
+        }
         tc::fence_after_sync();
         const int st = i % C::kStages;
-        const uint32_t v_s = smem_u32(big + C::kOffV + st * C::kKVBytes);
+        const uint64_t a0 = dV + ((st * C::kKVBytes) >> 4);
+        const uint64_t b0 = dP + (((i & 1) * C::kPBytes) >> 4);
         const uint32_t o_col = C::kTmemO + (o_seg & 1) * 32;
         // O^T += V^T P^T: A = V^T (MN-major: head dim contiguous; 64-wide
         // blocks kTile*128 bytes apart), B = P^T (K-major over tokens).
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
-          const uint64_t b = tc::sdesc_sw128(p_addr + (k >> 2) * kN * 128 + (k & 3) * 32, 16, 1024);
 #pragma unroll
-          for (int mb = 0; mb < D / C::kMO; ++mb) {
-            const uint64_t a =
-                tc::sdesc_sw128(v_s + mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128, kTile * 128, 1024);
-            tc::mma_bf16(tmem + o_col + mb * kN, a, b, idO, (!first || k > 0) ? 1u : 0u);
-          }
+          for (int mb = 0; mb < D / C::kMO; ++mb)
+            tc::mma_bf16(tmem + o_col + mb * kN, a0 + ((mb * (C::kMO / 64) * kTile * 128 + k * 16 * 128) >> 4),
+                         b0 + (((k >> 2) * kN * 128 + (k & 3) * 32) >> 4), idO, (!first || k > 0) ? 1u : 0u);
         }
-        tc::mma_commit(&bars[kODone]);
+        tc::mma_commit(&bars[kODone0 + (i & 1)]);
         tc::mma_commit(&bars[kKVEmpty0 + st]);
         if (i + 1 < n_local) wo.next(p);
-        if (next_s == i + 1 && next_s < n_local) {
-          if (!issue_s(next_s)) break;
-          ++next_s;
-        }
       }
     }
   } else {
@@ -612,34 +638,49 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       float sv[16];
       tmem_ld16(lane_addr + C::kTmemS + (i & 1) * kN, sv);
       const bool valid = w.j * kTile + t < w.len;
-      float* rm = red_max + (i & 1) * 4 * kN;
+      bool need = false;
 #pragma unroll
       for (int h = 0; h < NREP; ++h) {
         sv[h] = valid ? sv[h] * p.qscale : -INFINITY;
-        const float wm = warp_max(sv[h]);
-        if (lane == 0) rm[warp * kN + h] = wm;
+        need |= (m_ref[h] == -INFINITY) || (sv[h] > m_ref[h] + kRescaleLog2);
       }
-      tc::named_sync(1, 128);
+      // CTA-uniform: must a reference max move on this tile?  Usually not,
+      // and then P = exp2(s - m_ref) <= 2^8 needs no exchange of maxima.
+      const bool moved = tc::named_sync_or(1, 128, need);
       float alpha[NREP];
       bool rescale = false;
 #pragma unroll
-      for (int h = 0; h < NREP; ++h) {
-        const float mt = fmaxf(fmaxf(rm[h], rm[kN + h]), fmaxf(rm[2 * kN + h], rm[3 * kN + h]));
-        alpha[h] = 1.0f;
-        if (mt > m_ref[h] + kRescaleLog2 || m_ref[h] == -INFINITY) {  // CTA-uniform decision
-          alpha[h] = (m_ref[h] == -INFINITY) ? 0.0f : exp2f(m_ref[h] - mt);
-          m_ref[h] = mt;  // finite: every tile holds a valid token
-          rescale |= !first;
+      for (int h = 0; h < NREP; ++h) alpha[h] = 1.0f;
+      if (moved) {
+        float* rm = red_max + (i & 1) * 4 * kN;
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+          const float wm = warp_max(sv[h]);
+          if (lane == 0) rm[warp * kN + h] = wm;
         }
+        tc::named_sync(1, 128);
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+          const float mt = fmaxf(fmaxf(rm[h], rm[kN + h]), fmaxf(rm[2 * kN + h], rm[3 * kN + h]));
+          if (mt > m_ref[h] + kRescaleLog2 || m_ref[h] == -INFINITY) {  // CTA-uniform decision
+            alpha[h] = (m_ref[h] == -INFINITY) ? 0.0f : exp2f(m_ref[h] - mt);
+            m_ref[h] = mt;  // finite: every tile holds a valid token
+            rescale |= !first;
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < NREP; ++h) {
         sv[h] = exp2f(sv[h] - m_ref[h]);  // masked tokens: exp2(-inf) = 0
         l_tok[h] = l_tok[h] * alpha[h] + sv[h];
       }
-      if (i > 0) {
-        // P^T (and O^T, when rescaling) is busy until the previous P V finishes.
-        ok = tc::wait_bounded(&bars[kODone], (i - 1) & 1, abort_flag, p.err, 31);
+      if (rescale) {
+        // O^T is current once the previous P V finishes (and with it every
+        // earlier one, so P^T buffer i&1 is free too).
+        ok = tc::wait_bounded(&bars[kODone0 + ((i - 1) & 1)], ((i - 1) >> 1) & 1, abort_flag, p.err, 31);
         if (!ok) break;
         tc::fence_after_sync();
-        if (rescale) {
+        {
 #pragma unroll
           for (int mb = 0; mb < D / C::kMO; ++mb) {
             float ov[16];
@@ -650,6 +691,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
           tc::tmem_st_wait();
         }
+      } else if (i >= 2) {
+        // P^T buffer i&1 is free once the P V of tile i-2 finishes.
+        ok = tc::wait_bounded(&bars[kODone0 + (i & 1)], ((i - 2) >> 1) & 1, abort_flag, p.err, 33);
+        if (!ok) break;
       }
       // P^T[h][t] (bf16) in the K-major swizzled layout: 64-token sub-tiles
       // of 16 rows x 128 bytes; 16-byte chunk index XOR (row % 8).
@@ -658,16 +703,16 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
 #pragma unroll
         for (int h = 0; h < NREP; ++h) {
           const int off = sub * (kN * 128) + h * 128 + ((((col >> 3) ^ (h & 7))) << 4) + (col & 7) * 2;
-          *reinterpret_cast<__nv_bfloat16*>(p_s + off) = __float2bfloat16_rn(sv[h]);
+          *reinterpret_cast<__nv_bfloat16*>(p_s + (i & 1) * C::kPBytes + off) = __float2bfloat16_rn(sv[h]);
         }
       }
       fence_proxy_async_shared();
       tc::fence_before_sync();
-      tc::mbar_arrive(&bars[kPFull]);
+      tc::mbar_arrive(&bars[kPFull0 + (i & 1)]);
 
       if (last) {
         // ---- segment epilogue: O^T of (s, g) over this CTA's tiles.
-        ok = tc::wait_bounded(&bars[kODone], i & 1, abort_flag, p.err, 32);
+        ok = tc::wait_bounded(&bars[kODone0 + (i & 1)], (i >> 1) & 1, abort_flag, p.err, 32);
         tc::fence_after_sync();
         if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform for tcgen05.ld
         float ov[D / C::kMO][16];

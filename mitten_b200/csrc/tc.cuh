@@ -153,5 +153,19 @@ __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ORs a predicate over its `count` threads.
+__device__ __forceinline__ bool named_sync_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %3, 0;\n\t"
+      "bar.red.or.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
+}
+
 }  // namespace tc
 }  // namespace mtn

@@ -1,7 +1,8 @@
 // Host-side TMA tensor maps.  The pool map views the whole KV pool as a 2-D
-// bf16 tensor [layers*2*pages*kv_heads*page_size rows, head_dim] with one
-// page of one kv head per box (page_size rows x 64 columns, 128B swizzle);
-// maps are cached per pool layout so a decode step encodes nothing.
+// bf16 tensor [layers*2*pages*kv_heads*page_size rows, head_dim]; a box is
+// box_rows rows x 64 columns with 128B swizzle (one page of one kv head for
+// prefill, one page of every kv head for decode).  Maps are cached per pool
+// layout and box height so a decode step encodes nothing.
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -32,9 +33,10 @@ EncodeTiled encoder() {
 struct PoolKey {
   uintptr_t base;
   int64_t pages;
-  int32_t layers, ps, hkv, d;
+  int32_t layers, ps, hkv, d, box_rows;
   bool operator==(const PoolKey& o) const {
-    return base == o.base && pages == o.pages && layers == o.layers && ps == o.ps && hkv == o.hkv && d == o.d;
+    return base == o.base && pages == o.pages && layers == o.layers && ps == o.ps && hkv == o.hkv && d == o.d &&
+           box_rows == o.box_rows;
   }
 };
 
@@ -42,7 +44,7 @@ struct PoolKeyHash {
   size_t operator()(const PoolKey& k) const {
     size_t h = std::hash<uintptr_t>()(k.base);
     h ^= std::hash<int64_t>()(k.pages) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
-    h ^= static_cast<size_t>(k.layers * 131 + k.ps * 7 + k.hkv * 3 + k.d);
+    h ^= static_cast<size_t>(k.layers * 131 + k.ps * 7 + k.hkv * 3 + k.d + k.box_rows * 1009);
     return h;
   }
 };
@@ -56,14 +58,15 @@ int64_t pool_rows(const mtn_kv_layout* pool) {
   return static_cast<int64_t>(pool->num_layers) * 2 * pool->num_pages * pool->num_kv_heads * pool->page_size;
 }
 
-int pool_tensor_map(const mtn_kv_layout* pool, CUtensorMap* out) {
+int pool_tensor_map(const mtn_kv_layout* pool, CUtensorMap* out, int box_rows) {
   const int64_t rows = pool_rows(pool);
   if (rows >= (int64_t(1) << 31))
     return set_error(MTN_EINVAL, "pool has %lld rows; TMA coordinates need < 2^31", (long long)rows);
-  if (pool->page_size > 256 || pool->page_size % 8 != 0)
-    return set_error(MTN_EINVAL, "page_size %d: TMA page boxes need a multiple of 8 up to 256", pool->page_size);
+  if (box_rows <= 0) box_rows = pool->page_size;
+  if (box_rows > 256 || box_rows % 8 != 0)
+    return set_error(MTN_EINVAL, "TMA pool boxes of %d rows: need a multiple of 8 up to 256", box_rows);
   const PoolKey key{reinterpret_cast<uintptr_t>(pool->base), pool->num_pages, pool->num_layers, pool->page_size,
-                    pool->num_kv_heads, pool->head_dim};
+                    pool->num_kv_heads, pool->head_dim, box_rows};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_pool_maps.find(key);
@@ -76,7 +79,7 @@ int pool_tensor_map(const mtn_kv_layout* pool, CUtensorMap* out) {
   if (enc == nullptr) return set_error(MTN_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(pool->head_dim), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pool->head_dim) * 2};
-  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(pool->page_size)};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   CUtensorMap m;
   CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pool->base, dims, strides, box, estr,

@@ -10,8 +10,10 @@ namespace mtn {
 // Rows of the pool's 2-D [rows, head_dim] view.
 int64_t pool_rows(const mtn_kv_layout* pool);
 
-// Cached map over the whole pool: box = one page of one kv head x 64 columns, 128B swizzle.
-int pool_tensor_map(const mtn_kv_layout* pool, CUtensorMap* out);
+// Cached map over the whole pool: box = box_rows rows x 64 columns, 128B swizzle.  box_rows 0
+// means one page of one kv head (page_size rows); num_kv_heads * page_size rows is one page
+// of every kv head, which the pool layout keeps contiguous.
+int pool_tensor_map(const mtn_kv_layout* pool, CUtensorMap* out, int box_rows = 0);
 
 // Map over q [total_q][hq][d] bf16: box = box_rows tokens of one head x 64 columns, 128B swizzle.
 int q_tensor_map(const void* q, int64_t total_q, int hq, int d, int box_rows, CUtensorMap* out);
