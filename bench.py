@@ -6,11 +6,16 @@ Workload: one attention layer, bf16 K/V,
 14 query / 2 KV heads, head_dim 64, page size 16, a pool of 65 536 pages,
 64 sequences with context lengths U[256, 4096] (seed 2) whose block tables
 are a random permutation of the free page ids (seed 3), Q/K/V ~ N(0, 1)
-(seed 4).  One step = append one token per sequence (KV append kernel),
-then paged decode attention over every sequence (decode kernel).
+(seed 4).  One step = append one token per sequence, then paged decode
+attention over every sequence, in one kernel launch (the append is fused
+into the decode kernel).
 
-  value  decode tokens/s over all ranks, device-timed with CUDA events, inputs
-         resident in HBM, L2 flushed (256 MiB write) before every step.
+  value  decode tokens/s over all ranks: the K timed steps replayed back to
+         back (one CUDA graph each) between two CUDA events, inputs resident
+         in HBM.  The steps rotate through 6 disjoint 64-sequence batches, so
+         no step finds its K/V in L2 (inputs larger than L2, no flush);
+         per_step_l2_flushed_us re-times the same steps one by one after an
+         L2-flushing 256 MiB write.
   e2e    the same step through the C ABI with pinned HOST buffers: Q, new
          K/V, slots and seq_lens copied host->device and the output copied
          back inside the timed region.
@@ -53,7 +58,9 @@ def workload_config(extra=None):
                     "page 16, pool 65536 pages, 64 seqs, ctx U[256,4096]; step = append 1 token/seq + decode",
         "n_seqs": N_SEQS, "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D, "page_size": PS,
         "num_pages": NUM_PAGES, "ctx_range": [L_LO, L_HI], "seeds": {"lens": 2, "tables": 3, "qkv": 4},
-        "l2": "flushed before every step by a 256 MiB device write (per-step KV read ~71 MB < 126 MB L2)",
+        "l2": f"inputs larger than L2, no flush: steps rotate through {N_BATCHES} disjoint 64-sequence batches "
+              f"(~71 MB of K/V each), so a step's K/V were last read {N_BATCHES - 1} steps (~355 MB) earlier; "
+              "per_step_l2_flushed_us re-times the same steps one by one after a 256 MiB L2-flushing write",
     }
     if extra:
         cfg.update(extra)
@@ -183,44 +190,62 @@ def sum_over_ranks(pg, x: float) -> float:
 
 
 # ---------------------------------------------------------------- our arm
-def build_state(steps_total: int, device):
+N_BATCHES = 6  # disjoint 64-sequence batches the steps rotate through (inputs > L2 without a flush)
+
+
+def build_state(steps_total: int, device, n_batches: int = N_BATCHES):
+    """The pool and n_batches disjoint batches of the config-2 workload.
+
+    Every batch has the same 64 context lengths (seed 2); the block tables of
+    all batches are disjoint slices of one random permutation of the pool's
+    page ids (seed 3).  Step j runs batch j % n_batches, whose sequences then
+    grow by one token, so a step's K/V were last read n_batches - 1 steps
+    (about 355 MB of other K/V) earlier: more than the 126 MB L2 holds.
+    """
     import torch
 
     from mitten_b200 import paged
 
     lens0 = make_lens()
+    per_batch_steps = (steps_total + n_batches - 1) // n_batches
+    need = [(int(L) + per_batch_steps + 1 + PS - 1) // PS for L in lens0]
+    assert sum(need) * n_batches <= NUM_PAGES
     rng = np.random.default_rng(3)
     perm = rng.permutation(NUM_PAGES).astype(np.int32)
-    need = [(int(L) + steps_total + 1 + PS - 1) // PS for L in lens0]
-    assert sum(need) <= NUM_PAGES
     indptr = np.zeros(N_SEQS + 1, np.int32)
     indptr[1:] = np.cumsum(need)
-    tables = perm[: indptr[-1]]
     pool = paged.PagedKVPool(1, NUM_PAGES, PS, HKV, D, device=device)
     gen = torch.Generator(device=device)
     gen.manual_seed(4)
-    # initial context: L_s tokens per sequence, written with the append kernel
-    slots = np.concatenate([tables[indptr[s] + np.arange(L) // PS].astype(np.int64) * PS + np.arange(L) % PS
-                            for s, L in enumerate(lens0)])
-    n0 = len(slots)
-    for lo in range(0, n0, 1 << 18):
-        hi = min(n0, lo + (1 << 18))
-        k = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
-        v = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
-        pool.append(0, k, v, torch.from_numpy(slots[lo:hi]).to(device))
+    batches = []
+    for b in range(n_batches):
+        tables = perm[b * indptr[-1]: (b + 1) * indptr[-1]]
+        # initial context: L_s tokens per sequence, written with the append kernel
+        slots = np.concatenate([tables[indptr[s] + np.arange(L) // PS].astype(np.int64) * PS + np.arange(L) % PS
+                                for s, L in enumerate(lens0)])
+        n0 = len(slots)
+        for lo in range(0, n0, 1 << 18):
+            hi = min(n0, lo + (1 << 18))
+            k = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+            v = torch.randn((hi - lo, HKV, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+            pool.append(0, k, v, torch.from_numpy(slots[lo:hi]).to(device))
+        batches.append({"tables": tables.copy(), "indices": torch.from_numpy(tables.copy()).to(device)})
     torch.cuda.synchronize()
-    st = {
-        "pool": pool, "lens0": lens0, "indptr": torch.from_numpy(indptr).to(device),
-        "indices": torch.from_numpy(tables.copy()).to(device), "max_pages": int(max(need)), "gen": gen,
-        "tables": tables, "indptr_np": indptr,
-    }
-    return st
+    return {"pool": pool, "lens0": lens0, "indptr": torch.from_numpy(indptr).to(device), "indptr_np": indptr,
+            "batches": batches, "n_batches": n_batches, "gen": gen,
+            # batch 0 under the names the single-batch tools use
+            "indices": batches[0]["indices"], "tables": batches[0]["tables"]}
+
+
+def step_batch(st, step: int) -> int:
+    return step % st["n_batches"]
 
 
 def step_inputs(st, step: int, device):
-    """Slots and seq_lens for step `step` (host numpy)."""
-    pos = st["lens0"] + step  # position of the appended token
-    tables, indptr = st["tables"], st["indptr_np"]
+    """Slots and seq_lens (host numpy) of step `step`: batch step % n_batches, grown step // n_batches times."""
+    b = step_batch(st, step)
+    pos = st["lens0"] + step // st["n_batches"]  # position of the appended token
+    tables, indptr = st["batches"][b]["tables"], st["indptr_np"]
     slots = (tables[indptr[:-1] + pos // PS].astype(np.int64) * PS + pos % PS).astype(np.int64)
     return slots, (pos + 1).astype(np.int32)
 
@@ -247,11 +272,11 @@ def run_ours(args, rank, world, local, pg):
 
     def step(i):
         # One launch: append this step's K/V at position len-1, then decode.
-        paged.paged_decode(pool, 0, q_all[i], st["indptr"], st["indices"], lens_all[i], scale=scale,
+        b = st["batches"][step_batch(st, i)]
+        paged.paged_decode(pool, 0, q_all[i], st["indptr"], b["indices"], lens_all[i], scale=scale,
                            phantom=False, k_new=k_all[i], v_new=v_all[i], out=out, workspace=ws)
 
     for i in range(args.warmup):  # also configures the kernel before capture
-        flush.zero_()
         step(i)
     torch.cuda.synchronize()
     graphs = []
@@ -263,18 +288,26 @@ def run_ours(args, rank, world, local, pg):
     torch.cuda.synchronize()
     barrier(pg)
     stream = torch.cuda.current_stream()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier(pg)
+        ev0.record(stream)
         for j in range(args.steps):
-            flush.zero_()
-            evs[j][0].record(stream)
             graphs[j].replay()
-            evs[j][1].record(stream)
+        ev1.record(stream)
         torch.cuda.synchronize()
     barrier(pg)
-    t_decode = [evs[j][0].elapsed_time(evs[j][1]) * 1e-3 for j in range(args.steps)]
-    t_step = sum(t_decode)
+    t_step = ev0.elapsed_time(ev1) * 1e-3
+    # The same steps again, one at a time after an L2-flushing write, for
+    # comparison (their appends rewrite the same rows with the same values).
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    for j in range(args.steps):
+        flush.zero_()
+        evs[j][0].record(stream)
+        graphs[j].replay()
+        evs[j][1].record(stream)
+    torch.cuda.synchronize()
+    t_flushed = sum(evs[j][0].elapsed_time(evs[j][1]) * 1e-3 for j in range(args.steps))
     code, detail = paged.device_error(local)
     if code:
         raise SystemExit(f"device error {code} (detail {detail}) during the bench")
@@ -291,22 +324,25 @@ def run_ours(args, rank, world, local, pg):
     e2e_t = max_over_ranks(pg, e2e["t"])
     e2e_tokens = sum_over_ranks(pg, float(N_SEQS * e2e["steps"]))
     peaks = load_peaks()
-    achieved = (sum(dec_bytes) / len(dec_bytes)) / (t_step / len(t_decode)) / 1e9
+    achieved = (sum(dec_bytes) / len(dec_bytes)) / (t_step / args.steps) / 1e9
     res = {
         "metric": METRIC, "value": tokens / t_max, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q/K/V)",
         "config": workload_config({"parallelism": f"replicas{world}",
-                                   "step": "one fused append+decode launch, replayed from a CUDA graph"}),
+                                   "step": "one fused append+decode launch per step, CUDA graphs replayed "
+                                           "back to back between two events"}),
         "kv_read_gbs": sum_over_ranks(pg, kv_bytes) / t_max / 1e9,
         "decode_us_per_step": 1e6 * t_step / args.steps,
+        "per_step_l2_flushed_us": 1e6 * t_flushed / args.steps,
         "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<64,7> (append fused)", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_source": peaks["source"], "traffic": traffic_from_profile(),
                      "algorithmic_bytes_per_launch": sum(dec_bytes) / len(dec_bytes)},
         "e2e": {"value": e2e_tokens / e2e_t, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
-                "path": "pinned host Q/K/V/seq_lens -> H2D -> mtn_paged_decode (C ABI) -> D2H output, per step"},
+                "path": "per step: pinned host Q/K/V/seq_lens -> H2D -> mtn_paged_decode (C ABI) -> D2H output, "
+                        "steps back to back, batches rotating as above"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
@@ -335,11 +371,11 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
     q_d, k_d, v_d = (torch.empty_like(x, device=device) for x in (q_h, k_h, v_h))
     o_d = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
     l_d = torch.empty(N_SEQS, dtype=torch.int32, device=device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     scale = D ** -0.5
 
     def one(i):
         sp = int(torch.cuda.current_stream().cuda_stream)
+        b = st["batches"][step_batch(st, i)]
         q_d.copy_(q_h, non_blocking=True)
         k_d.copy_(k_h, non_blocking=True)
         v_d.copy_(v_h, non_blocking=True)
@@ -347,30 +383,29 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
         _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_d.data_ptr(), _lib.MTN_DTYPE_BF16,
                                         o_d.data_ptr(), _lib.MTN_DTYPE_BF16, k_d.data_ptr(), v_d.data_ptr(),
                                         _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
-                                        st["indices"].data_ptr(), l_d.data_ptr(), scale, 0, ws.buf.data_ptr(),
+                                        b["indices"].data_ptr(), l_d.data_ptr(), scale, 0, ws.buf.data_ptr(),
                                         ws.nbytes, sp))
         o_h.copy_(o_d, non_blocking=True)
 
     # the pool already holds the device arm's appends: these steps rewrite the same positions
-    for i in range(min(3, total_steps)):
-        one(i)
+    first = total_steps - steps
+    for i in range(min(3, steps)):
+        one(first + i)
     torch.cuda.synchronize()
     graphs = []
     for j in range(steps):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            one(j % total_steps)
+            one(first + j)
         graphs.append(g)
     torch.cuda.synchronize()
-    t = 0.0
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
     for j in range(steps):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
         graphs[j].replay()
-        b.record(stream)
-        b.synchronize()
-        t += a.elapsed_time(b) * 1e-3
+    b.record(stream)
+    b.synchronize()
+    t = a.elapsed_time(b) * 1e-3
     del graphs
     h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, len_h[0]))
     d2h = o_h.numel() * o_h.element_size()
