@@ -35,11 +35,14 @@ class KvCachePool:
         h = C.c_void_p()
         L.check(L.lib().mtn_page_pool_create(num_pages, page_size, C.byref(h)))
         self._h = h
+        self._destroy = L.lib().mtn_page_pool_destroy
         self.num_pages, self.page_size = num_pages, page_size
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            L.lib().mtn_page_pool_destroy(self._h)
+        # the destroy function is bound at construction: module globals may
+        # already be gone when the interpreter shuts down
+        if getattr(self, "_h", None) and getattr(self, "_destroy", None):
+            self._destroy(self._h)
             self._h = None
 
     def allocate(self, owner) -> int | None:
@@ -90,11 +93,14 @@ class RadixCache:
         h = C.c_void_p()
         L.check(L.lib().mtn_radix_create(page_size, max_pages, C.byref(h)))
         self._h = h
+        self._destroy = L.lib().mtn_radix_destroy
         self.page_size = page_size
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            L.lib().mtn_radix_destroy(self._h)
+        # the destroy function is bound at construction: module globals may
+        # already be gone when the interpreter shuts down
+        if getattr(self, "_h", None) and getattr(self, "_destroy", None):
+            self._destroy(self._h)
             self._h = None
 
     def match_prefix(self, tokens) -> tuple[int, list[int], list[int]]:
@@ -182,11 +188,14 @@ class Scheduler:
         h = C.c_void_p()
         L.check(L.lib().mtn_sched_create(C.byref(cfg), C.byref(h)))
         self._h = h
+        self._destroy = L.lib().mtn_sched_destroy
         self.page_size = page_size
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            L.lib().mtn_sched_destroy(self._h)
+        # the destroy function is bound at construction: module globals may
+        # already be gone when the interpreter shuts down
+        if getattr(self, "_h", None) and getattr(self, "_destroy", None):
+            self._destroy(self._h)
             self._h = None
 
     def add_request(self, req_id: int, input_ids, temperature: float = 0.0, max_new_tokens: int = 512) -> None:

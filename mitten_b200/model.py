@@ -1,0 +1,210 @@
+"""Model call sites over the paged KV pool: the CUDA backend's forward.
+
+`QwenPagedModel.forward(batch)` is the B200 form of
+`BackendHandle::forward` (inference-backend/src/backend.rs:16-21) for
+Qwen3_5Model with full-attention layers (inference-model-qwen/src/model.rs):
+one call serves the scheduler's whole CSR batch (prefill rows first, then
+decode rows) instead of the reference's per-request loop with private
+contiguous caches (burn_backend.rs:31-80), and returns one logits row per
+request (the last token of its rows), like `Logits` (backend.rs:8-12).
+
+Per layer, the dense work stays on the device's BLAS in f32 (q/k/v/o
+projections, q/k RMSNorm (1 + w), RoPE, SwiGLU); the paged-KV path is this
+library's kernels:
+  prefill rows  mtn_build_slot_mapping + mtn_kv_append, then
+                mtn_paged_prefill (causal over the pool, phantom zero key)
+  decode rows   mtn_paged_decode with the step's K/V appended in the same
+                launch (phantom zero key)
+The reference's cache starts with one all-zero K/V row per layer
+(model.rs:207-220); MTN_ATTN_PHANTOM_ZERO_SLOT reproduces that key without
+storing it, so position p of a sequence lives in pool slot p.
+
+`GemmaPagedModel` is the attention call site the Gemma crate lacks
+(inference-model-gemma/src/model.rs:82-94 has none): the same layer with
+Gemma-2B shapes (MQA, head_dim 256, GeGLU MLP, theta 1e4).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from . import paged
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    hidden: int
+    layers: int
+    hq: int
+    hkv: int
+    head_dim: int
+    inter: int
+    vocab: int
+    eps: float = 1e-6
+    theta: float = 1e6
+    partial_rotary: float = 1.0
+    gated_q: bool = True      # Qwen3.5 q_proj carries a sigmoid gate per head
+    mlp: str = "swiglu"       # "swiglu" (Qwen) or "geglu" (Gemma)
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary)
+
+
+def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RmsNorm::forward (model.rs:98-108): x / sqrt(mean(x^2) + eps) * (1 + w), last axis."""
+    var = x.square().mean(dim=-1, keepdim=True)
+    return x * torch.rsqrt(var + eps) * (w + 1.0)
+
+
+class QwenPagedModel:
+    """Qwen3_5Model (all layers full attention) over a PagedKVPool."""
+
+    def __init__(self, shape: DecoderShape, weights: dict, num_pages: int, page_size: int = 16,
+                 device: torch.device | str = "cuda"):
+        self.s = shape
+        self.dev = torch.device(device)
+        self.w = {k: torch.as_tensor(v).to(self.dev, torch.float32) for k, v in weights.items()}
+        self.pool = paged.PagedKVPool(shape.layers, num_pages, page_size, shape.hkv, shape.head_dim, device=self.dev)
+        half = shape.rotary_dim // 2
+        i = np.arange(half, dtype=np.float32)
+        # 1 / theta^(2i / rotary_dim) in f32, as model.rs:511-514 computes it
+        inv = np.float32(1.0) / np.power(np.float32(shape.theta), np.float32(2.0) * i / np.float32(shape.rotary_dim),
+                                         dtype=np.float32)
+        self.inv_freq = torch.from_numpy(inv.astype(np.float32)).to(self.dev)
+        self.scale = shape.head_dim ** -0.5
+        self._ws = None
+        self._ws_seqs = 0
+
+    # ------------------------------------------------------------ pieces
+    def _rope(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """apply_rope (model.rs:508-540): rotate-half over the first rotary_dim of each head."""
+        rd, half = self.s.rotary_dim, self.s.rotary_dim // 2
+        ang = pos.to(torch.float32)[:, None, None] * self.inv_freq[None, None, :]
+        c, s = torch.cos(ang), torch.sin(ang)
+        x1, x2 = x[..., :half], x[..., half:rd]
+        out = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+        if rd < x.shape[-1]:
+            out = torch.cat([out, x[..., rd:]], dim=-1)
+        return out
+
+    def _decode_ws(self, n: int) -> paged.DecodeWorkspace:
+        if self._ws is None or n > self._ws_seqs:
+            self._ws = paged.DecodeWorkspace.for_shape(self.pool, n, self.s.hq)
+            self._ws_seqs = n
+        return self._ws
+
+    def _mlp(self, h: torch.Tensor, p: str) -> torch.Tensor:
+        g = h @ self.w[f"{p}.mlp.gate_proj.weight"].T
+        u = h @ self.w[f"{p}.mlp.up_proj.weight"].T
+        act = torch.nn.functional.silu(g) if self.s.mlp == "swiglu" else torch.nn.functional.gelu(g, approximate="tanh")
+        return (act * u) @ self.w[f"{p}.mlp.down_proj.weight"].T
+
+    def _attention(self, li: int, h: torch.Tensor, pos: torch.Tensor, meta: dict) -> torch.Tensor:
+        """GatedAttention::forward (model.rs:369-422) for every row of the batch."""
+        s, w = self.s, self.w
+        m = f"layers.{li}.mixer"
+        T = h.shape[0]
+        qp = h @ w[f"{m}.q_proj.weight"].T
+        if s.gated_q:
+            qg = qp.view(T, s.hq, 2, s.head_dim)  # per head: q then gate (model.rs:372-375)
+            q, gate = qg[:, :, 0, :], qg[:, :, 1, :].reshape(T, s.hq * s.head_dim)
+        else:
+            q, gate = qp.view(T, s.hq, s.head_dim), None
+        k = (h @ w[f"{m}.k_proj.weight"].T).view(T, s.hkv, s.head_dim)
+        v = (h @ w[f"{m}.v_proj.weight"].T).view(T, s.hkv, s.head_dim)
+        q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
+        k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
+        q, k = self._rope(q, pos), self._rope(k, pos)
+        attn = torch.empty((T, s.hq, s.head_dim), dtype=torch.float32, device=self.dev)
+        tp = meta["tp"]
+        if tp:
+            self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
+            paged.paged_prefill(self.pool, li, q[:tp].to(torch.bfloat16).contiguous(), meta["qo_p"], meta["kv_p"],
+                                meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=True,
+                                out=attn[:tp])
+        if T > tp:
+            paged.paged_decode(self.pool, li, q[tp:].contiguous(), meta["kv_d"], meta["kv_indices"], meta["len_d"],
+                               scale=self.scale, phantom=True, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
+                               out=attn[tp:], workspace=meta["ws"])
+        o = attn.view(T, s.hq * s.head_dim)
+        if gate is not None:
+            o = torch.sigmoid(gate) * o
+        return o @ w[f"{m}.o_proj.weight"].T
+
+    # ------------------------------------------------------------ forward
+    def batch_meta(self, b) -> dict:
+        """Device copies of the batch's CSR metadata, split into prefill and decode rows."""
+        dev = self.dev
+        n, npf = b.n_reqs, b.n_prefill
+        qo = b.qo_indptr
+        tp = int(qo[npf])
+        meta = {"tp": tp, "kv_indices": torch.from_numpy(np.ascontiguousarray(b.kv_indices, np.int32)).to(dev)}
+        if npf:
+            meta["qo_p"] = torch.from_numpy(np.ascontiguousarray(qo[:npf + 1], np.int32)).to(dev)
+            meta["kv_p"] = torch.from_numpy(np.ascontiguousarray(b.kv_indptr[:npf + 1], np.int32)).to(dev)
+            meta["len_p"] = torch.from_numpy(np.ascontiguousarray(b.seq_lens[:npf], np.int32)).to(dev)
+            meta["max_q"] = int(np.max(np.diff(qo[:npf + 1])))
+            pos_p = torch.from_numpy(np.ascontiguousarray(b.position_ids[:tp], np.int32)).to(dev)
+            meta["slots"] = paged.build_slot_mapping(meta["qo_p"], pos_p, meta["kv_p"], meta["kv_indices"],
+                                                     self.pool.page_size)
+        if n > npf:
+            meta["kv_d"] = torch.from_numpy(np.ascontiguousarray(b.kv_indptr[npf:], np.int32)).to(dev)
+            meta["len_d"] = torch.from_numpy(np.ascontiguousarray(b.seq_lens[npf:], np.int32)).to(dev)
+            meta["ws"] = self._decode_ws(n - npf)
+        return meta
+
+    @torch.no_grad()
+    def forward(self, b) -> torch.Tensor:
+        """Logits [n_reqs, vocab] (f32, on the device) of each request's last row."""
+        s, w = self.s, self.w
+        if len(b.cow_src):
+            self.pool.page_copy(torch.from_numpy(np.ascontiguousarray(b.cow_src, np.int32)).to(self.dev),
+                                torch.from_numpy(np.ascontiguousarray(b.cow_dst, np.int32)).to(self.dev))
+        meta = self.batch_meta(b)
+        ids = torch.from_numpy(b.input_ids.astype(np.int64)).to(self.dev)
+        pos = torch.from_numpy(np.ascontiguousarray(b.position_ids, np.int32)).to(self.dev)
+        x = w["embedding.weight"][ids]  # the vocab-split lookup of model.rs:159-183 is a plain lookup
+        for li in range(s.layers):
+            p = f"layers.{li}"
+            x = x + self._attention(li, _rms(x, w[f"{p}.norm.weight"], s.eps), pos, meta)
+            x = x + self._mlp(_rms(x, w[f"{p}.ffn_norm.weight"], s.eps), p)
+        last = torch.from_numpy(b.qo_indptr[1:].astype(np.int64) - 1).to(self.dev)
+        h = _rms(x[last], w["norm.weight"], s.eps)
+        return (h @ w["embedding.weight"].T).contiguous()  # tied LM head (model.rs:262-276)
+
+
+class Engine:
+    """engine_loop.rs:28-107 over the scheduler mirror and a paged model.
+
+    Each iteration: schedule a batch, run its copy-on-write page copies and
+    the model forward, sample greedily on the device (first strict max,
+    scheduler.rs:186-199) and hand the tokens back to the scheduler.  A
+    backend error aborts every request of the batch (engine_loop.rs:47-57).
+    """
+
+    def __init__(self, model: QwenPagedModel, sched):
+        self.model, self.sched = model, sched
+        self.iterations = 0
+
+    def step(self) -> bool:
+        b = self.sched.schedule()
+        if b is None:
+            return False
+        try:
+            logits = self.model.forward(b)
+            tokens = paged.argmax_rows(logits).cpu().numpy().astype(np.uint32)
+        except (L.MittenError, RuntimeError):
+            self.sched.abort_batch()
+            raise
+        self.sched.process_tokens(tokens)
+        self.iterations += 1
+        return True
+
+    def run(self, max_iterations: int = 1 << 20) -> None:
+        while self.sched.num_active() and self.iterations < max_iterations:
+            if not self.step():
+                break
