@@ -318,6 +318,8 @@ def run_ours(args, rank, world, local, pg):
 
     # ---- e2e through the C ABI with pinned host buffers
     e2e = run_e2e(args, st, pool, ws, device, stream, total_steps)
+    # ---- the other two HBM-bound kernels of the path, on free pages
+    extras = run_append_and_copy(st, pool, device, stream)
 
     t_max = max_over_ranks(pg, t_step)
     tokens = sum_over_ranks(pg, float(N_SEQS * args.steps))
@@ -345,9 +347,82 @@ def run_ours(args, rank, world, local, pg):
                         "steps back to back, batches rotating as above"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
+        "kv_append_bulk": extras["append"],
+        "page_copy": extras["copy"],
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    return res
+
+
+def run_append_and_copy(st, pool, device, stream) -> dict:
+    """Bandwidth of the bulk KV append (64 sequences x 512 tokens per call, the prefill-append shape)
+    and of the copy-on-write page copy (3072 pages per call), each timed as 24 calls captured in one
+    CUDA graph (so host launch cost is not timed) that rotate through sources and destinations larger
+    than L2 together.  Destinations are pool pages no batch uses; page-copy sources are batch pages
+    (read only)."""
+    import torch
+
+    peak = load_peaks()["hbm_gbs"]
+    used = st["n_batches"] * int(st["indptr_np"][-1])
+    free = np.random.default_rng(3).permutation(NUM_PAGES).astype(np.int64)[used:]
+    res = {}
+    # bulk append: 32768 tokens, 2 x 32768 x HKV x D bf16 read + the same written + 8 B slots
+    n_tok, n_calls = 64 * 512, 24
+    pages_per_call = n_tok // PS
+    gen = torch.Generator(device=device)
+    gen.manual_seed(6)
+    srcs = [(torch.randn((n_tok, HKV, D), generator=gen, device=device).to(torch.bfloat16),
+             torch.randn((n_tok, HKV, D), generator=gen, device=device).to(torch.bfloat16)) for _ in range(6)]
+    dsts = []
+    for j in range(max(1, min(3, len(free) // pages_per_call))):
+        pg = free[j * pages_per_call:(j + 1) * pages_per_call]
+        dsts.append(torch.from_numpy((np.repeat(pg, PS) * PS + np.tile(np.arange(PS), len(pg))).astype(np.int64))
+                    .to(device))
+
+    def app(i):
+        k, v = srcs[i % len(srcs)]
+        pool.append(0, k, v, dsts[i % len(dsts)])
+
+    def timed(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n_calls):
+                fn(i)
+        g.replay()  # warm
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+        b.synchronize()
+        del g
+        return a.elapsed_time(b) * 1e-3 / n_calls
+
+    t = timed(app)
+    nbytes = append_bytes(n_tok) * 2 + 8 * n_tok
+    res["append"] = {"kernel": "kv_append_kernel<bf16>", "tokens_per_call": n_tok, "bytes_per_call": nbytes,
+                     "us_per_call": 1e6 * t, "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / peak,
+                     "peak_gbs": peak}
+    # page copy: 3072 pages of one layer, K and V (2 x 3072 x PS x HKV x D x 2 B read, the same written)
+    n_pg = 3072
+    n_dst = max(1, min(3, len(free) // n_pg))
+    batch_pages = np.random.default_rng(3).permutation(NUM_PAGES).astype(np.int32)[:used]
+    src_sets = [torch.from_numpy(batch_pages[j * n_pg:(j + 1) * n_pg].copy()).to(device)
+                for j in range(min(6, used // n_pg))]
+    dst_sets = [torch.from_numpy(free[j * n_pg:(j + 1) * n_pg].astype(np.int32)).to(device) for j in range(n_dst)]
+
+    def cp(i):
+        pool.page_copy(src_sets[i % len(src_sets)], dst_sets[i % len(dst_sets)])
+
+    t = timed(cp)
+    nbytes = 2 * n_pg * 2 * PS * HKV * D * 2 + 8 * n_pg
+    res["copy"] = {"kernel": "page_copy_kernel", "pages_per_call": n_pg, "bytes_per_call": nbytes,
+                   "us_per_call": 1e6 * t, "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / peak,
+                   "peak_gbs": peak}
     return res
 
 

@@ -86,25 +86,27 @@ __device__ __forceinline__ uint4 load_chunk<float>(const float* p) {
   return r;
 }
 
-template <typename SrcT>
+// Idx is the work-item index type: 32-bit when every index fits (the
+// common case; a 64-bit division per 16 bytes would dominate the kernel).
+template <typename SrcT, typename Idx>
 __global__ void __launch_bounds__(kThreads) kv_append_kernel(
     __nv_bfloat16* __restrict__ kdst, __nv_bfloat16* __restrict__ vdst, int64_t num_pages, int hkv, int ps,
     int d, const SrcT* __restrict__ k, const SrcT* __restrict__ v, int64_t src_stride,
     const int64_t* __restrict__ slots, int64_t n_tokens, int* err) {
   const int chunks = d >> 3;
-  const int64_t per_tok = static_cast<int64_t>(hkv) * chunks;
-  const int64_t total = n_tokens * per_tok;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+  const Idx per_tok = static_cast<Idx>(hkv) * chunks;
+  const Idx total = static_cast<Idx>(n_tokens) * per_tok;
+  const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
+  for (Idx base = blockIdx.x * static_cast<Idx>(blockDim.x) + threadIdx.x; base < total;
        base += stride * kUnroll) {
     uint4 kv[kUnroll], vv[kUnroll];
     int64_t dst[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const int64_t i = base + u * stride;
+      const Idx i = base + u * stride;
       dst[u] = -1;
       if (i < total) {
-        const int64_t t = i / per_tok;
+        const Idx t = i / per_tok;
         const int rem = static_cast<int>(i - t * per_tok);
         const int h = rem / chunks;
         const int c = rem - h * chunks;
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(kThreads) kv_append_kernel(
           const int64_t page = slot / ps;
           const int off = static_cast<int>(slot - page * ps);
           if (page < num_pages) {
-            const int64_t so = t * src_stride + static_cast<int64_t>(h) * d + c * 8;
+            const int64_t so = static_cast<int64_t>(t) * src_stride + static_cast<int64_t>(h) * d + c * 8;
             kv[u] = load_chunk<SrcT>(k + so);
             vv[u] = load_chunk<SrcT>(v + so);
             dst[u] = ((page * hkv + h) * ps + off) * static_cast<int64_t>(d) + c * 8;
@@ -134,28 +136,30 @@ __global__ void __launch_bounds__(kThreads) kv_append_kernel(
 }
 
 // One work item = 16 bytes of one (pair, layer, K|V) page block.
+template <typename Idx>
 __global__ void __launch_bounds__(kThreads) page_copy_kernel(__nv_bfloat16* __restrict__ pool, int64_t num_pages,
                                                              int num_layers, int64_t page_vecs,
                                                              const int32_t* __restrict__ src,
                                                              const int32_t* __restrict__ dst, int64_t n_pairs,
                                                              int* err) {
   uint4* p4 = reinterpret_cast<uint4*>(pool);
-  const int64_t units = n_pairs * num_layers * 2;
-  const int64_t total = units * page_vecs;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+  const Idx pv = static_cast<Idx>(page_vecs);
+  const Idx units = static_cast<Idx>(n_pairs) * num_layers * 2;
+  const Idx total = units * pv;
+  const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
+  for (Idx base = blockIdx.x * static_cast<Idx>(blockDim.x) + threadIdx.x; base < total;
        base += stride * kUnroll) {
     uint4 val[kUnroll];
     int64_t to[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const int64_t i = base + u * stride;
+      const Idx i = base + u * stride;
       to[u] = -1;
       if (i < total) {
-        const int64_t unit = i / page_vecs;
-        const int64_t w = i - unit * page_vecs;
-        const int64_t pair = unit / (num_layers * 2);
-        const int64_t lk = unit - pair * (num_layers * 2);  // layer * 2 + kv
+        const Idx unit = i / pv;
+        const int64_t w = i - unit * pv;
+        const Idx pair = unit / static_cast<Idx>(num_layers * 2);
+        const int64_t lk = unit - pair * static_cast<Idx>(num_layers * 2);  // layer * 2 + kv
         const int64_t s = src[pair], t = dst[pair];
         if (s < 0 || s >= num_pages || t < 0 || t >= num_pages) {
           record_error(err, kDevErrBadPage, static_cast<int>(pair));
@@ -300,15 +304,30 @@ int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer, const void* k, const
   const int64_t work = n_tokens * pool->num_kv_heads * (pool->head_dim / 8);
   const int grid = mtn::grid_for(work, mtn::kThreads * mtn::kUnroll);
   auto s = static_cast<cudaStream_t>(stream);
+  // 32-bit work indices while every index (plus one grid stride) stays below 2^31.
+  const bool narrow = work + static_cast<int64_t>(grid) * mtn::kThreads * mtn::kUnroll < (int64_t(1) << 31);
   if (src_dtype == MTN_DTYPE_BF16) {
-    mtn::kv_append_kernel<__nv_bfloat16><<<grid, mtn::kThreads, 0, s>>>(
-        kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim,
-        static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), src_stride, slots, n_tokens,
-        mtn::device_error_ptr());
+    auto kb = static_cast<const __nv_bfloat16*>(k);
+    auto vb = static_cast<const __nv_bfloat16*>(v);
+    if (narrow)
+      mtn::kv_append_kernel<__nv_bfloat16, uint32_t><<<grid, mtn::kThreads, 0, s>>>(
+          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kb, vb, src_stride, slots,
+          n_tokens, mtn::device_error_ptr());
+    else
+      mtn::kv_append_kernel<__nv_bfloat16, int64_t><<<grid, mtn::kThreads, 0, s>>>(
+          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kb, vb, src_stride, slots,
+          n_tokens, mtn::device_error_ptr());
   } else {
-    mtn::kv_append_kernel<float><<<grid, mtn::kThreads, 0, s>>>(
-        kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, static_cast<const float*>(k),
-        static_cast<const float*>(v), src_stride, slots, n_tokens, mtn::device_error_ptr());
+    auto kf = static_cast<const float*>(k);
+    auto vf = static_cast<const float*>(v);
+    if (narrow)
+      mtn::kv_append_kernel<float, uint32_t><<<grid, mtn::kThreads, 0, s>>>(
+          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kf, vf, src_stride, slots,
+          n_tokens, mtn::device_error_ptr());
+    else
+      mtn::kv_append_kernel<float, int64_t><<<grid, mtn::kThreads, 0, s>>>(
+          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kf, vf, src_stride, slots,
+          n_tokens, mtn::device_error_ptr());
   }
   return mtn::check_launch("kv_append_kernel");
 }
@@ -323,9 +342,15 @@ int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages, const int
   const int64_t page_vecs = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * pool->head_dim / 8;
   const int64_t work = n_pages * pool->num_layers * 2 * page_vecs;
   const int grid = mtn::grid_for(work, mtn::kThreads * mtn::kUnroll);
-  mtn::page_copy_kernel<<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
-      n_pages, mtn::device_error_ptr());
+  const bool narrow = work + static_cast<int64_t>(grid) * mtn::kThreads * mtn::kUnroll < (int64_t(1) << 31);
+  if (narrow)
+    mtn::page_copy_kernel<uint32_t><<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
+        n_pages, mtn::device_error_ptr());
+  else
+    mtn::page_copy_kernel<int64_t><<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
+        n_pages, mtn::device_error_ptr());
   return mtn::check_launch("page_copy_kernel");
 }
 

@@ -19,9 +19,11 @@ The reference's cache starts with one all-zero K/V row per layer
 (model.rs:207-220); MTN_ATTN_PHANTOM_ZERO_SLOT reproduces that key without
 storing it, so position p of a sequence lives in pool slot p.
 
-`GemmaPagedModel` is the attention call site the Gemma crate lacks
-(inference-model-gemma/src/model.rs:82-94 has none): the same layer with
-Gemma-2B shapes (MQA, head_dim 256, GeGLU MLP, theta 1e4).
+The same class is the attention call site the Gemma crate lacks
+(inference-model-gemma/src/model.rs:82-94 has none): `GEMMA_2B` runs the
+layer at Gemma-2B shapes (MQA, head_dim 256, GeGLU MLP, theta 1e4) without
+the Qwen gate, q/k norms or phantom row (Gemma's caches start empty,
+model.rs:96-105).
 """
 from __future__ import annotations
 
@@ -47,11 +49,18 @@ class DecoderShape:
     theta: float = 1e6
     partial_rotary: float = 1.0
     gated_q: bool = True      # Qwen3.5 q_proj carries a sigmoid gate per head
+    qk_norm: bool = True      # RMSNorm (1 + w) over each head of q and k
+    phantom: bool = True      # Qwen caches start with one zero row; Gemma's start empty
     mlp: str = "swiglu"       # "swiglu" (Qwen) or "geglu" (Gemma)
 
     @property
     def rotary_dim(self) -> int:
         return int(self.head_dim * self.partial_rotary)
+
+
+QWEN_CONFIG1 = DecoderShape(hidden=896, layers=24, hq=14, hkv=2, head_dim=64, inter=4864, vocab=151936)
+GEMMA_2B = DecoderShape(hidden=2048, layers=18, hq=8, hkv=1, head_dim=256, inter=16384, vocab=256000, theta=1e4,
+                        gated_q=False, qk_norm=False, phantom=False, mlp="geglu")
 
 
 def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -116,19 +125,20 @@ class QwenPagedModel:
             q, gate = qp.view(T, s.hq, s.head_dim), None
         k = (h @ w[f"{m}.k_proj.weight"].T).view(T, s.hkv, s.head_dim)
         v = (h @ w[f"{m}.v_proj.weight"].T).view(T, s.hkv, s.head_dim)
-        q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
-        k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
+        if s.qk_norm:
+            q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
+            k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
         q, k = self._rope(q, pos), self._rope(k, pos)
         attn = torch.empty((T, s.hq, s.head_dim), dtype=torch.float32, device=self.dev)
         tp = meta["tp"]
         if tp:
             self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
             paged.paged_prefill(self.pool, li, q[:tp].to(torch.bfloat16).contiguous(), meta["qo_p"], meta["kv_p"],
-                                meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=True,
+                                meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=s.phantom,
                                 out=attn[:tp])
         if T > tp:
             paged.paged_decode(self.pool, li, q[tp:].contiguous(), meta["kv_d"], meta["kv_indices"], meta["len_d"],
-                               scale=self.scale, phantom=True, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
+                               scale=self.scale, phantom=s.phantom, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
                                out=attn[tp:], workspace=meta["ws"])
         o = attn.view(T, s.hq * s.head_dim)
         if gate is not None:

@@ -40,6 +40,10 @@ class QwenShape:
     eps: float = 1e-6
     theta: float = 1e6
     partial_rotary: float = 1.0
+    gated_q: bool = True    # q_proj carries a sigmoid gate per head (model.rs:372-375, 417)
+    qk_norm: bool = True    # RMSNorm (1 + w) over each head of q and k (model.rs:380-381)
+    phantom: bool = True    # caches start with one zero row (model.rs:207-220)
+    mlp: str = "swiglu"     # silu(gate) * up; "geglu": gelu_tanh(gate) * up
 
     @property
     def rotary_dim(self) -> int:
@@ -48,6 +52,12 @@ class QwenShape:
 
 # Qwen2.5-0.5B-shaped decoder.
 CONFIG1 = QwenShape(hidden=896, layers=24, hq=14, hkv=2, head_dim=64, inter=4864, vocab=151936)
+# Gemma-2B shapes.  The reference Gemma model has no attention
+# (inference-model-gemma/src/model.rs:82-94) and empty caches (:96-105); this is the
+# attention layer above at these shapes, without the Qwen gate and q/k norms, RoPE theta 1e4,
+# GeGLU MLP and no phantom row.
+GEMMA_2B = QwenShape(hidden=2048, layers=18, hq=8, hkv=1, head_dim=256, inter=16384, vocab=256000, theta=1e4,
+                     gated_q=False, qk_norm=False, phantom=False, mlp="geglu")
 
 
 def weight_names(cfg: QwenShape) -> list[tuple[str, tuple[int, ...]]]:
@@ -59,12 +69,14 @@ def weight_names(cfg: QwenShape) -> list[tuple[str, tuple[int, ...]]]:
         m = f"{p}.mixer"
         names += [
             (f"{p}.norm.weight", (h,)),
-            (f"{m}.q_proj.weight", (cfg.hq * d * 2, h)),
+            (f"{m}.q_proj.weight", (cfg.hq * d * (2 if cfg.gated_q else 1), h)),
             (f"{m}.k_proj.weight", (cfg.hkv * d, h)),
             (f"{m}.v_proj.weight", (cfg.hkv * d, h)),
             (f"{m}.o_proj.weight", (h, cfg.hq * d)),
-            (f"{m}.q_norm.weight", (d,)),
-            (f"{m}.k_norm.weight", (d,)),
+        ]
+        if cfg.qk_norm:
+            names += [(f"{m}.q_norm.weight", (d,)), (f"{m}.k_norm.weight", (d,))]
+        names += [
             (f"{p}.ffn_norm.weight", (h,)),
             (f"{p}.mlp.gate_proj.weight", (cfg.inter, h)),
             (f"{p}.mlp.up_proj.weight", (cfg.inter, h)),
@@ -125,6 +137,12 @@ def silu(x: np.ndarray) -> np.ndarray:
     return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
 
 
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    x = x.astype(np.float32)
+    return (np.float32(0.5) * x * (np.float32(1.0) + np.tanh(np.float32(0.7978845608028654) *
+                                                            (x + np.float32(0.044715) * x * x * x)))).astype(np.float32)
+
+
 def sigmoid(x: np.ndarray) -> np.ndarray:
     return (np.float32(1.0) / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
 
@@ -145,7 +163,7 @@ class RefModel:
     def init_cache(self, rid: int) -> None:
         """model.rs:207-220: every layer's K and V start as one zero row per kv head."""
         c = self.cfg
-        z = np.zeros((c.hkv, 1, c.head_dim), np.float32)
+        z = np.zeros((c.hkv, 1 if c.phantom else 0, c.head_dim), np.float32)
         self.caches[rid] = [(z.copy(), z.copy()) for _ in range(c.layers)]
 
     def attention(self, li: int, rid: int, x: np.ndarray, pos: np.ndarray) -> np.ndarray:
@@ -153,12 +171,16 @@ class RefModel:
         c, w = self.cfg, self.w
         m = f"layers.{li}.mixer"
         seq = x.shape[0]
-        qg = (x @ w[f"{m}.q_proj.weight"].T).reshape(seq, c.hq, 2, c.head_dim)
-        q, gate = qg[:, :, 0, :], qg[:, :, 1, :].reshape(seq, c.hq * c.head_dim)
+        if c.gated_q:
+            qg = (x @ w[f"{m}.q_proj.weight"].T).reshape(seq, c.hq, 2, c.head_dim)
+            q, gate = qg[:, :, 0, :], qg[:, :, 1, :].reshape(seq, c.hq * c.head_dim)
+        else:
+            q, gate = (x @ w[f"{m}.q_proj.weight"].T).reshape(seq, c.hq, c.head_dim), None
         k = (x @ w[f"{m}.k_proj.weight"].T).reshape(seq, c.hkv, c.head_dim)
         v = (x @ w[f"{m}.v_proj.weight"].T).reshape(seq, c.hkv, c.head_dim)
-        q = rms_norm(q, w[f"{m}.q_norm.weight"], c.eps)
-        k = rms_norm(k, w[f"{m}.k_norm.weight"], c.eps)
+        if c.qk_norm:
+            q = rms_norm(q, w[f"{m}.q_norm.weight"], c.eps)
+            k = rms_norm(k, w[f"{m}.k_norm.weight"], c.eps)
         q, k = apply_rope(q, pos, c), apply_rope(k, pos, c)
         if self.q_round or (self.q_round_prefill and seq > 1):
             q = rne_bf16(q)
@@ -185,7 +207,8 @@ class RefModel:
         p = p / l
         o = np.matmul(p, vx).transpose(1, 0, 2).reshape(seq, c.hq * c.head_dim).astype(np.float32)
         self.last_attn.setdefault(rid, [None] * c.layers)[li] = o
-        o = sigmoid(gate) * o
+        if gate is not None:
+            o = sigmoid(gate) * o
         return (o @ w[f"{m}.o_proj.weight"].T).astype(np.float32)
 
     def forward(self, rid: int, ids: np.ndarray, pos: np.ndarray) -> np.ndarray:
@@ -200,7 +223,8 @@ class RefModel:
             h = rms_norm(x, w[f"{p}.ffn_norm.weight"], c.eps)
             g = h @ w[f"{p}.mlp.gate_proj.weight"].T
             u = h @ w[f"{p}.mlp.up_proj.weight"].T
-            x = x + (silu(g) * u) @ w[f"{p}.mlp.down_proj.weight"].T
+            act = silu(g) if c.mlp == "swiglu" else gelu_tanh(g)
+            x = x + (act * u) @ w[f"{p}.mlp.down_proj.weight"].T
         last = rms_norm(x[-1:], w["norm.weight"], c.eps)
         return (last @ w["embedding.weight"].T)[0].astype(np.float32)
 

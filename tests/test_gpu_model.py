@@ -34,7 +34,9 @@ LOGIT_TOL_CONFIG1 = 5e-2  # 24 layers of N(0, 0.02) weights: measured 3.3e-2
 
 def shape_of(cfg: R.QwenShape) -> M.DecoderShape:
     return M.DecoderShape(hidden=cfg.hidden, layers=cfg.layers, hq=cfg.hq, hkv=cfg.hkv, head_dim=cfg.head_dim,
-                          inter=cfg.inter, vocab=cfg.vocab, eps=cfg.eps, theta=cfg.theta)
+                          inter=cfg.inter, vocab=cfg.vocab, eps=cfg.eps, theta=cfg.theta,
+                          partial_rotary=cfg.partial_rotary, gated_q=cfg.gated_q, qk_norm=cfg.qk_norm,
+                          phantom=cfg.phantom, mlp=cfg.mlp)
 
 
 def run_engine(cfg, weights, prompts, steps, num_pages=256, budget=512, max_decode=8):
@@ -102,6 +104,18 @@ def test_small_model_chunked_prefill_and_mixed_batches(cuda_device):
     prompts = [rng.integers(0, cfg.vocab, n).astype(np.int64) for n in (40, 17, 63, 5)]
     # a 48-token prefill budget cuts prompts into chunks and mixes prefill with decode rows
     compare(cfg, w, prompts, 12, LOGIT_TOL_SMALL, budget=48)
+
+
+def test_gemma_shaped_mqa_call_site(cuda_device):
+    """The Gemma attention call site (MQA, head_dim 256, GeGLU, theta 1e4, no phantom row) at reduced
+    width and depth, with chunked prefill mixed into decode batches."""
+    import dataclasses
+
+    cfg = dataclasses.replace(R.GEMMA_2B, hidden=512, layers=3, inter=1024, vocab=8192)
+    w = R.random_weights(cfg, seed=7)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, cfg.vocab, n).astype(np.int64) for n in (90, 33, 140, 12)]
+    compare(cfg, w, prompts, 10, LOGIT_TOL_SMALL, budget=96)
 
 
 def test_config1_greedy_32_steps(cuda_device):
