@@ -550,6 +550,198 @@ def run_reference(args, rank, world):
     }
 
 
+# ------------------------------------------------ configs 3 and 4 (kernels only)
+def _graph_steps(fns, stream):
+    """Capture each step function in its own CUDA graph; time all replays back to back."""
+    import torch
+
+    for f in fns[:3]:
+        f()
+    torch.cuda.synchronize()
+    graphs = []
+    for f in fns:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            f()
+        graphs.append(g)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for g in graphs:
+        g.replay()
+    b.record(stream)
+    b.synchronize()
+    del graphs
+    return a.elapsed_time(b) * 1e-3
+
+
+def run_cfg3(args, local) -> dict:
+    """BASELINE config 3's attention layer: 128 sequences share a 1032-token prefix (64 full pages and
+    a partial one, refcounted), each with its own suffix U[64, 512] (seed 6) and its own copy of the
+    partial page (copy-on-write), Qwen2.5-7B attention shapes (28 q / 4 kv heads, head_dim 128).
+    One step = fused append + decode over all 128 sequences of one layer; steps rotate through 3
+    disjoint copies of the workload (logical K/V per step far above L2; the shared prefix is read 128
+    times within a step, which is the reuse the shared pages exist for)."""
+    import torch
+
+    from mitten_b200 import paged
+
+    dev = torch.device("cuda", local)
+    hq, hkv, d, ps, n = 28, 4, 128, 16, 128
+    prefix = 1032
+    suf = np.random.default_rng(6).integers(64, 513, size=n)
+    steps = args.steps
+    per_copy_pages = (prefix + ps - 1) // ps + sum((prefix + int(s) + steps + ps) // ps - prefix // ps for s in suf)
+    n_copies = 3
+    num_pages = n_copies * per_copy_pages + 64
+    pool = paged.PagedKVPool(1, num_pages, ps, hkv, d, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    pool.storage.normal_(generator=gen)
+    copies, nxt, cow_src, cow_dst = [], 0, [], []
+    for c in range(n_copies):
+        shared = list(range(nxt, nxt + (prefix + ps - 1) // ps))
+        nxt += len(shared)
+        tables = []
+        for s in suf:
+            own = list(shared[:-1]) + [nxt]  # private copy of the partial prefix page
+            cow_src.append(shared[-1])
+            cow_dst.append(nxt)
+            nxt += 1
+            need = (prefix + int(s) + steps + ps) // ps
+            while len(own) < need:
+                own.append(nxt)
+                nxt += 1
+            tables.append(own)
+        indptr = np.concatenate([[0], np.cumsum([len(t) for t in tables])]).astype(np.int32)
+        copies.append({"indptr": torch.from_numpy(indptr).to(dev),
+                       "indices": torch.from_numpy(np.concatenate(tables).astype(np.int32)).to(dev)})
+    assert nxt <= num_pages
+    # copy-on-write of every sequence's partial prefix page (128 pages per copy of the workload)
+    src_t = torch.tensor(cow_src[:n], dtype=torch.int32, device=dev)
+    dst_t = torch.tensor(cow_dst[:n], dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    t_cow = _graph_steps([lambda: pool.page_copy(src_t, dst_t)] * 8, stream) / 8
+    ws = paged.DecodeWorkspace.for_shape(pool, n, hq)
+    q = torch.randn((n, hq, d), generator=gen, device=dev).to(torch.bfloat16)
+    kn = torch.randn((n, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    vn = torch.randn((n, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=dev)
+    lens = [torch.from_numpy((prefix + suf + 1 + j // n_copies).astype(np.int32)).to(dev)
+            for j in range(args.warmup + steps)]
+
+    def step(j):
+        c = copies[j % n_copies]
+        return lambda: paged.paged_decode(pool, 0, q, c["indptr"], c["indices"], lens[j], k_new=kn, v_new=vn,
+                                          out=out, workspace=ws)
+
+    for j in range(args.warmup):
+        step(j)()
+    t = _graph_steps([step(args.warmup + j) for j in range(steps)], stream)
+    b_tok = 2 * hkv * d * 2
+    logical = float(sum((prefix + suf + 1).astype(np.int64))) * b_tok
+    unique = (prefix + float(np.sum(suf + 1))) * b_tok
+    peak = load_peaks()["hbm_gbs"]
+    code, detail = paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail})")
+    return {"metric": "config 3 decode attention over shared prefix pages", "value": n * steps / t,
+            "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 3 attention layer: 128 seqs, 1032-token shared prefix "
+                                   "(64 full + 1 partial page, copy-on-write), suffix U[64,512] seed 6, "
+                                   "Hq 28 / Hkv 4 / D 128, page 16, 1 layer, append fused",
+                       "l2": "3 disjoint copies of the workload rotate step to step"},
+            "logical_kv_gbs": logical / (t / steps) / 1e9, "unique_kv_gbs": unique / (t / steps) / 1e9,
+            "unique_frac_of_hbm": unique / (t / steps) / 1e9 / peak,
+            "cow_page_copy_us_per_128_pages": 1e6 * t_cow, "gpu_launches": steps}
+
+
+def run_cfg4(args, local) -> dict:
+    """BASELINE config 4's attention layer (Gemma-2B shapes: 8 q / 1 kv head, head_dim 256): per step
+    96 decoding sequences with context U[512, 8192] (seed 7) plus 4 prefill chunks of 512 tokens whose
+    prior context is U{0, 512, ..., 7680} (seed 8), over one pool.  Decode (append fused) and prefill
+    are timed separately: decode as KV GB/s, prefill as TFLOP/s against the measured bf16 peak."""
+    import torch
+
+    from mitten_b200 import paged
+
+    dev = torch.device("cuda", local)
+    hq, hkv, d, ps = 8, 1, 256, 16
+    n_dec, n_pf, chunk = 96, 4, 512
+    dl = np.random.default_rng(7).integers(512, 8193, size=n_dec)
+    pp = np.random.default_rng(8).integers(0, 16, size=n_pf) * 512
+    steps = args.steps
+    dec_pages = [(int(L) + args.warmup + steps + 1 + ps - 1) // ps for L in dl]
+    pf_pages = [(int(P) + chunk + ps - 1) // ps for P in pp]
+    num_pages = sum(dec_pages) + sum(pf_pages) + 16
+    perm = np.random.default_rng(3).permutation(num_pages).astype(np.int32)
+    pool = paged.PagedKVPool(1, num_pages, ps, hkv, d, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(9)
+    pool.storage.normal_(generator=gen)
+    off = 0
+
+    def take(k):
+        nonlocal off
+        t = perm[off:off + k]
+        off += k
+        return t
+
+    dec_tables = [take(k) for k in dec_pages]
+    pf_tables = [take(k) for k in pf_pages]
+    d_indptr = torch.from_numpy(np.concatenate([[0], np.cumsum(dec_pages)]).astype(np.int32)).to(dev)
+    d_indices = torch.from_numpy(np.concatenate(dec_tables)).to(dev)
+    p_indptr = torch.from_numpy(np.concatenate([[0], np.cumsum(pf_pages)]).astype(np.int32)).to(dev)
+    p_indices = torch.from_numpy(np.concatenate(pf_tables)).to(dev)
+    qo = torch.from_numpy(np.arange(0, (n_pf + 1) * chunk, chunk).astype(np.int32)).to(dev)
+    p_lens = torch.from_numpy((pp + chunk).astype(np.int32)).to(dev)
+    qd = torch.randn((n_dec, hq, d), generator=gen, device=dev).to(torch.bfloat16)
+    kn = torch.randn((n_dec, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    vn = torch.randn((n_dec, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    qp = torch.randn((n_pf * chunk, hq, d), generator=gen, device=dev).to(torch.bfloat16)
+    od = torch.empty((n_dec, hq, d), dtype=torch.bfloat16, device=dev)
+    op = torch.empty((n_pf * chunk, hq, d), dtype=torch.bfloat16, device=dev)
+    ws = paged.DecodeWorkspace.for_shape(pool, n_dec, hq)
+    pws = torch.zeros(max(256, paged.L.lib().mtn_paged_prefill_workspace_bytes(n_pf, n_pf * chunk, hq, hkv, d)),
+                      dtype=torch.uint8, device=dev)
+    lens = [torch.from_numpy((dl + 1 + j).astype(np.int32)).to(dev) for j in range(args.warmup + steps)]
+    stream = torch.cuda.current_stream()
+
+    def dec(j):
+        return lambda: paged.paged_decode(pool, 0, qd, d_indptr, d_indices, lens[j], k_new=kn, v_new=vn, out=od,
+                                          workspace=ws)
+
+    def pre():
+        paged.paged_prefill(pool, 0, qp, qo, p_indptr, p_indices, p_lens, chunk, out=op, workspace=pws)
+
+    for j in range(args.warmup):
+        dec(j)()
+        pre()
+    t_dec = _graph_steps([dec(args.warmup + j) for j in range(steps)], stream)
+    t_pre = _graph_steps([pre] * steps, stream)
+    peaks = load_peaks()
+    kv = float(np.sum(dl + 1)) * 2 * hkv * d * 2
+    flops = sum(4.0 * hq * d * chunk * (int(P) + (chunk + 1) / 2) for P in pp)
+    code, detail = paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail})")
+    return {"metric": "config 4 mixed step: decode KV GB/s and chunked-prefill TFLOP/s", "value":
+            (n_dec + n_pf * chunk) * steps / (t_dec + t_pre), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * (t_dec + t_pre) / steps, "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 4 attention layer: 96 decode seqs ctx U[512,8192] seed 7 + "
+                                   "4 prefill chunks of 512 with prior ctx U{0,512..7680} seed 8, Hq 8 / Hkv 1 / "
+                                   "D 256, page 16, 1 layer",
+                       "l2": "decode reads ~430 MB of K/V per step (above L2)"},
+            "decode": {"us_per_step": 1e6 * t_dec / steps, "kv_gbs": kv / (t_dec / steps) / 1e9,
+                       "frac": kv / (t_dec / steps) / 1e9 / peaks["hbm_gbs"], "peak_gbs": peaks["hbm_gbs"]},
+            "prefill": {"us_per_step": 1e6 * t_pre / steps, "tflops": flops / (t_pre / steps) / 1e12,
+                        "frac": flops / (t_pre / steps) / 1e12 / peaks["bf16_tflops"],
+                        "peak_tflops": peaks["bf16_tflops"]},
+            "gpu_launches": 2 * steps}
+
+
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -578,6 +770,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
+                    help="cfg2 (default) is the headline; cfg3 / cfg4 time those configs' attention layers")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
@@ -589,6 +783,13 @@ def main(argv=None) -> int:
         print(json.dumps(run_reference(args, rank, world)), flush=True)
         return 0
     rank, world, local, pg = dist_setup(args.gpus)
+    if args.workload != "cfg2":
+        res = (run_cfg3 if args.workload == "cfg3" else run_cfg4)(args, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if pg is not None:
+            pg.destroy_process_group()
+        return 0
     try:
         res = run_ours(args, rank, world, local, pg)
         if rank == 0:
