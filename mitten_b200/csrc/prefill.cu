@@ -9,15 +9,20 @@
 //
 // CTA = (128-row query tile, query head, sequence); 6 warps in 3 roles:
 //   warps 0-3  softmax: one TMEM lane (= one query row) per thread; online
-//              softmax in the exp2 domain, rescale of the TMEM O accumulator,
-//              bf16 P written to shared memory in the 128B-swizzled K-major
-//              layout, final normalisation and store.
+//              softmax in the exp2 domain against a per-row reference max
+//              that moves only when a tile exceeds it by 2^8 (so the TMEM O
+//              accumulator is rarely rescaled), bf16 P written to shared
+//              memory in the 128B-swizzled K-major layout (double-buffered),
+//              final normalisation and store.
 //   warp 4     TMA producer: Q tile once, then K and V pages of each KV tile
-//              (one 2-D box per page per 64-wide head-dim block) into a
-//              2-stage ring; pages come straight from the block table.
+//              (one 4-D box per page covers every head-dim block) into a
+//              2-stage ring with separate K and V barriers; pages come
+//              straight from the block table.
 //   warp 5     MMA issuer (one thread): S = Q K^T and O += P V with
 //              tcgen05.mma (M=128, kind::f16, f32 accumulators in TMEM),
-//              completion signalled with tcgen05.commit on mbarriers.
+//              completion signalled with tcgen05.commit on mbarriers.  S is
+//              double-buffered in TMEM: the next tile's Q K^T runs on the
+//              tensor cores while the softmax works on this one.
 // Every wait is bounded (~1 s); a timeout records kDevErrTimeout, releases
 // the other roles, frees TMEM and returns.
 #include <mutex>
@@ -51,6 +56,10 @@ struct PrefillParams {
   int* err;
 };
 
+// P is exponentiated against a per-row reference max that moves only when a
+// tile's max exceeds it by more than 2^8, so P <= 256 and O is rarely rescaled.
+constexpr float kRescaleLog2 = 8.0f;
+
 template <int D>
 struct PCfg {
   static constexpr int kBN = D <= 128 ? 128 : 64;       // kv tokens per tile
@@ -58,20 +67,32 @@ struct PCfg {
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKVBytes = kBN * D * 2;          // one of K or V per stage
   static constexpr int kPBytes = kBM * kBN * 2;
+  static constexpr int kGroupBytes = kDB * 1024;        // 8 kv rows, all head-dim blocks
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;         // [2][kKVBytes]
   static constexpr int kOffV = kOffK + 2 * kKVBytes;
-  static constexpr int kOffP = kOffV + 2 * kKVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;       // 10 mbarriers
+  static constexpr int kOffP = kOffV + 2 * kKVBytes;    // [2][kPBytes]
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;   // 15 mbarriers
   static constexpr int kOffMisc = kOffBar + 16 * 8;     // tmem base, abort flag
   static constexpr int kSmem = kOffMisc + 64 + 1024;    // + slack for 1024-byte alignment
-  static constexpr int kTmemS = 0;
-  static constexpr int kTmemO = kBN;
-  static constexpr int kTmemCols = (kBN + D) <= 256 ? 256 : 512;
-  static_assert(kBN + D <= kTmemCols, "TMEM budget");
+  static constexpr int kTmemS = 0;                      // [2] x kBN columns
+  static constexpr int kTmemO = 2 * kBN;
+  static constexpr int kTmemCols = 512;
+  static_assert(2 * kBN + D <= kTmemCols, "TMEM budget");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
-enum Bar { kQFull = 0, kKVFull0 = 1, kKVFull1 = 2, kKVEmpty0 = 3, kKVEmpty1 = 4, kSFull = 5, kPFull = 6, kODone = 7 };
+enum Bar {
+  kQFull = 0,
+  kKFull0 = 1,    // [2] K of tile j landed in stage j&1
+  kVFull0 = 3,    // [2]
+  kKEmpty0 = 5,   // [2] S of tile j done: K stage free
+  kVEmpty0 = 7,   // [2] P V of tile j done: V stage free
+  kSFull0 = 9,    // [2] S buffer j&1 holds tile j's scores
+  kPFull0 = 11,   // [2] P buffer j&1 written (128 softmax threads)
+  kODone0 = 13,   // [2] P V of tile j done: P buffer j&1 free, O current
+  kNumBars = 15
+};
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -106,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pages_per_tile = C::kBN / p.ps;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == kPFull ? kBM : 1);
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1) ? kBM : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -121,72 +142,108 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
+    // One 4-D box per page brings a page of this kv head, all head-dim
+    // blocks, as [8-row groups][64-column blocks][8 rows][128 bytes]; the
+    // pages of a tile sit back to back, so every 8-row group of the tile is
+    // kGroupBytes after the previous one.  K of a stage is refilled once S of
+    // the tile two back is done, V once its P V is done.
+    // Page ids are fetched by the whole warp, 32 at a time and one window
+    // ahead, so no load of the block table sits on the issue path; lane 0
+    // issues the copies.
+    const int ppt = pages_per_tile;
+    const int lim = min(npages, n_tiles * ppt) - 1;  // last page the CTA reads
+    auto fetch = [&](int first) -> int { return p.kv_indices[kv_beg + min(first + lane, lim)]; };
+    auto to_row = [&](int page) -> int {  // first pool row / 8 of this kv head's slice of the page (K)
+      if (page < 0 || page >= p.num_pages) {
+        record_error(p.err, kDevErrBadPage, s);
+        page = 0;
+      }
+      return static_cast<int>((p.row_k + (static_cast<int64_t>(page) * p.hkv + g) * p.ps) >> 3);
+    };
     if (lane == 0) {
       tc::prefetch_tmap(&tm_q);
       tc::prefetch_tmap(&tm_kv);
       mbar_arrive_expect_tx(&bars[kQFull], C::kQBytes);
       for (int b = 0; b < C::kDB; ++b)
         tc::tma_load_3d(smem + C::kOffQ + b * kBM * 128, &tm_q, b * 64, h, q0 + tile * kBM, &bars[kQFull]);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !tc::wait_bounded(&bars[kKVEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 10)) break;
-        mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
-        uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
-        uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
-        for (int pi = 0; pi < pages_per_tile; ++pi) {
-          int pidx = min(j * pages_per_tile + pi, npages - 1);  // past the end: any valid page, masked later
-          int64_t page = p.kv_indices[kv_beg + pidx];
-          if (page < 0 || page >= p.num_pages) {
-            record_error(p.err, kDevErrBadPage, s);
-            page = 0;
-          }
-          const int64_t rk = p.row_k + (page * p.hkv + g) * p.ps;
-          const int64_t rv = p.row_v + (page * p.hkv + g) * p.ps;
-          for (int b = 0; b < C::kDB; ++b) {
-            const int off = b * C::kBN * 128 + pi * p.ps * 128;
-            tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
-            tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
-          }
-        }
+    }
+    const int page_bytes = p.ps * D * 2;
+    const int dv = static_cast<int>((p.row_v - p.row_k) >> 3);
+    int cur = to_row(fetch(0));
+    int nxt = fetch(32);
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      const int first = j * ppt;
+      if (j > 0 && (first & 31) == 0) {
+        cur = to_row(nxt);
+        nxt = fetch(first + 32);
+      }
+      bool ok = true;
+      if (lane == 0 && j >= 2) ok = tc::wait_bounded(&bars[kKEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 10);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
+      if (lane == 0) mbar_arrive_expect_tx(&bars[kKFull0 + st], C::kKVBytes);
+      for (int pi = 0; pi < ppt; ++pi) {
+        const int r = __shfl_sync(0xffffffffu, cur, (first & 31) + pi);
+        if (lane == 0) tc::tma_load_4d_w(kst + pi * page_bytes, &tm_kv, r, &bars[kKFull0 + st]);
+      }
+      if (lane == 0 && j >= 2) ok = tc::wait_bounded(&bars[kVEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 11);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
+      if (lane == 0) mbar_arrive_expect_tx(&bars[kVFull0 + st], C::kKVBytes);
+      for (int pi = 0; pi < ppt; ++pi) {
+        const int r = __shfl_sync(0xffffffffu, cur, (first & 31) + pi);
+        if (lane == 0) tc::tma_load_4d_w(vst + pi * page_bytes, &tm_kv, r + dv, &bars[kVFull0 + st]);
       }
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
+    // S(j+1) = Q K^T runs on the tensor cores while the softmax works on
+    // tile j; P(j) V follows once P(j) is written.
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kBM, C::kBN, false);
       constexpr uint32_t idO = tc::idesc_bf16(kBM, D, true);
-      const uint32_t q_s = smem_u32(smem + C::kOffQ);
-      const uint32_t p_s = smem_u32(smem + C::kOffP);
-      bool ok = tc::wait_bounded(&bars[kQFull], 0, abort_flag, p.err, 20);
-      for (int j = 0; ok && j < n_tiles; ++j) {
+      const uint64_t dQ = tc::sdesc_sw128(smem_u32(smem + C::kOffQ), 16, 1024);
+      // K as the K-major B operand: 8-row groups kGroupBytes apart (SBO).
+      const uint64_t dK = tc::sdesc_sw128(smem_u32(smem + C::kOffK), 16, C::kGroupBytes);
+      const uint64_t dP = tc::sdesc_sw128(smem_u32(smem + C::kOffP), 16, 1024);
+      // V as the MN-major B operand: 64-wide head-dim blocks 1024 bytes
+      // apart (LBO), 8-row groups kGroupBytes apart (SBO).
+      const uint64_t dV = tc::sdesc_sw128(smem_u32(smem + C::kOffV), 1024, C::kGroupBytes);
+      // S = Q K^T: 16-wide k steps walk 32 bytes inside a 128-byte swizzle
+      // row, then the next 64-wide head-dim block (Q: kBM*128 bytes on, K:
+      // 1024 bytes on).
+      auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!tc::wait_bounded(&bars[kKVFull0 + st], (j >> 1) & 1, abort_flag, p.err, 21)) break;
+        if (!tc::wait_bounded(&bars[kKFull0 + st], (j >> 1) & 1, abort_flag, p.err, 21)) return false;
         tc::fence_after_sync();
-        const uint32_t k_s = smem_u32(smem + C::kOffK + st * C::kKVBytes);
-        const uint32_t v_s = smem_u32(smem + C::kOffV + st * C::kKVBytes);
-        // S = Q K^T: K-major A and B; 16-wide k steps walk 32 bytes inside a
-        // 128-byte swizzle row, then the next 64-wide head-dim block.
+        const uint64_t b0 = dK + ((st * C::kKVBytes) >> 4);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t koff = (k >> 2) * 0 + (k & 3) * 32;
-          const uint64_t a = tc::sdesc_sw128(q_s + (k >> 2) * kBM * 128 + koff, 16, 1024);
-          const uint64_t b = tc::sdesc_sw128(k_s + (k >> 2) * C::kBN * 128 + koff, 16, 1024);
-          tc::mma_bf16(tmem + C::kTmemS, a, b, idS, k > 0 ? 1u : 0u);
-        }
-        tc::mma_commit(&bars[kSFull]);
-        if (!tc::wait_bounded(&bars[kPFull], j & 1, abort_flag, p.err, 22)) break;
+        for (int k = 0; k < D / 16; ++k)
+          tc::mma_bf16(tmem + C::kTmemS + (j & 1) * C::kBN, dQ + (((k >> 2) * kBM * 128 + (k & 3) * 32) >> 4),
+                       b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
+        tc::mma_commit(&bars[kSFull0 + (j & 1)]);
+        tc::mma_commit(&bars[kKEmpty0 + st]);
+        return true;
+      };
+      // Order per tile: S(j+1) (its K is normally resident by now), then
+      // wait for P(j) and issue P(j) V.  Waits suspend in try_wait.
+      bool ok = tc::wait_bounded(&bars[kQFull], 0, abort_flag, p.err, 20) && issue_s(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        if (!tc::wait_bounded(&bars[kPFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 22)) break;
+        if (!tc::wait_bounded(&bars[kVFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 23)) break;
         tc::fence_after_sync();
-        // O += P V: P K-major (kv tokens contiguous), V MN-major (head dim
-        // contiguous): 16 kv rows = 2048 bytes per k step; 64-wide head-dim
-        // blocks kBN*128 bytes apart (LBO).
+        // O += P V: P K-major (kv tokens contiguous); a 16-token k step is
+        // two 8-row groups of V.
+        const uint64_t a0 = dP + (((j & 1) * C::kPBytes) >> 4);
+        const uint64_t b0 = dV + (((j & 1) * C::kKVBytes) >> 4);
 #pragma unroll
-        for (int k = 0; k < C::kBN / 16; ++k) {
-          const uint64_t a = tc::sdesc_sw128(p_s + (k >> 2) * kBM * 128 + (k & 3) * 32, 16, 1024);
-          const uint64_t b = tc::sdesc_sw128(v_s + k * 16 * 128, C::kBN * 128, 1024);
-          tc::mma_bf16(tmem + C::kTmemO, a, b, idO, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        tc::mma_commit(&bars[kODone]);
-        tc::mma_commit(&bars[kKVEmpty0 + st]);
+        for (int k = 0; k < C::kBN / 16; ++k)
+          tc::mma_bf16(tmem + C::kTmemO, a0 + (((k >> 2) * kBM * 128 + (k & 3) * 32) >> 4),
+                       b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, (j > 0 || k > 0) ? 1u : 0u);
+        tc::mma_commit(&bars[kODone0 + (j & 1)]);
+        tc::mma_commit(&bars[kVEmpty0 + (j & 1)]);
       }
     }
   } else {
@@ -194,59 +251,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x;  // 0..127 == TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int row_pos = min(pos0 + row, last_pos);
-    float m_run = -INFINITY, l_run = 0.0f;
-    uint8_t* p_tile = smem + C::kOffP;
+    float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      ok = tc::wait_bounded(&bars[kSFull], j & 1, abort_flag, p.err, 30);
-      if (!ok) break;
+      ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
+      if (!__all_sync(0xffffffffu, ok)) break;  // TMEM loads below are warp-collective
       tc::fence_after_sync();
       float sv[C::kBN];
+      {
+        uint32_t r[C::kBN / 32][32];
 #pragma unroll
-      for (int c = 0; c < C::kBN / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(lane_base + C::kTmemS + c * 32, r);
+        for (int c = 0; c < C::kBN / 32; ++c) tc::tmem_ld32(lane_base + C::kTmemS + (j & 1) * C::kBN + c * 32, r[c]);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
+        for (int c = 0; c < C::kBN; ++c) sv[c] = __uint_as_float(r[c >> 5][c & 31]);
       }
       const int key0 = j * C::kBN;
-      float mt = -INFINITY;
+      if (key0 + C::kBN - 1 > pos0) {  // diagonal tile: keys after a row's position are masked
+#pragma unroll
+        for (int c = 0; c < C::kBN; ++c) sv[c] = (key0 + c <= row_pos) ? sv[c] : -INFINITY;
+      }
+      // Row max of the raw scores in 8 independent chains (scale > 0 commutes with max).
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < C::kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+      const float mt =
+          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+          p.qscale;
+      // Lazy rescale, per row: the reference max moves only when this tile
+      // exceeds it by 2^8 (tile 0 always sets it: key 0 is visible to every row).
+      float alpha = 1.0f;
+      bool moved = false;
+      if (m_ref == -INFINITY) {
+        m_ref = mt;
+      } else if (mt > m_ref + kRescaleLog2) {
+        alpha = exp2f(m_ref - mt);
+        m_ref = mt;
+        moved = true;
+      }
+      const float neg_m = -m_ref;
+      float ps8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps8[i] = 0.0f;
 #pragma unroll
       for (int c = 0; c < C::kBN; ++c) {
-        sv[c] = (key0 + c <= row_pos) ? sv[c] * p.qscale : -INFINITY;
-        mt = fmaxf(mt, sv[c]);
+        sv[c] = tc::ex2_approx(fmaf(sv[c], p.qscale, neg_m));  // masked keys: 2^-inf = 0
+        ps8[c & 7] += sv[c];
       }
-      const float mn = fmaxf(m_run, mt);  // finite: key 0 is visible to every row
-      const float alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - mn);
-      float psum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < C::kBN; ++c) {
-        sv[c] = exp2f(sv[c] - mn);
-        psum += sv[c];
-      }
+      const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l_run = l_run * alpha + psum;
-      m_run = mn;
-      if (j > 0) {
-        // O and the P buffer are busy until the previous P V finishes.
-        ok = tc::wait_bounded(&bars[kODone], (j - 1) & 1, abort_flag, p.err, 31);
-        if (!ok) break;
+      if (__any_sync(0xffffffffu, moved)) {
+        // O is current once P V of tile j-1 finishes (and with it P buffer j&1 is free).
+        ok = tc::wait_bounded(&bars[kODone0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, abort_flag, p.err, 31);
+        if (!__all_sync(0xffffffffu, ok)) break;
         tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
-            tc::tmem_ld_wait();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
+          tc::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tc::tmem_st32(lane_base + C::kTmemO + c * 32, r);
-          }
-          tc::tmem_st_wait();
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tc::tmem_st32(lane_base + C::kTmemO + c * 32, r);
         }
+        tc::tmem_st_wait();
+      }
+      if (j >= 2) {
+        // P buffer j&1 is free once P V of tile j-2 finishes.
+        ok = tc::wait_bounded(&bars[kODone0 + (j & 1)], ((j - 2) >> 1) & 1, abort_flag, p.err, 33);
+        if (!__all_sync(0xffffffffu, ok)) break;
       }
       // P (bf16) into the 128B-swizzled K-major tile: 64-key sub-tiles of
       // 128 rows x 128 bytes; 16-byte chunk index XOR (row % 8).
+      uint8_t* p_tile = smem + C::kOffP + (j & 1) * C::kPBytes;
 #pragma unroll
       for (int c8 = 0; c8 < C::kBN / 8; ++c8) {
         const int sub = c8 >> 3, chunk = c8 & 7;
@@ -259,16 +338,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_shared();
       tc::fence_before_sync();
-      tc::mbar_arrive(&bars[kPFull]);
+      tc::mbar_arrive(&bars[kPFull0 + (j & 1)]);
     }
     // ---- epilogue: O / l (phantom key folded in), one row per thread.
-    if (ok) ok = tc::wait_bounded(&bars[kODone], (n_tiles - 1) & 1, abort_flag, p.err, 32);
+    if (ok) ok = tc::wait_bounded(&bars[kODone0 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, abort_flag, p.err, 32);
     tc::fence_after_sync();
-    if (ok) {
+    if (__all_sync(0xffffffffu, ok)) {
       float l = l_run, a = 1.0f;
       if (p.phantom) {
-        const float mf = fmaxf(m_run, 0.0f);
-        a = exp2f(m_run - mf);
+        const float mf = fmaxf(m_ref, 0.0f);
+        a = exp2f(m_ref - mf);
         l = l * a + exp2f(-mf);
       }
       const float inv = l > 0.0f ? a / l : 0.0f;
@@ -366,7 +445,7 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
                 "mtn_paged_prefill: q/o must be 16-byte aligned");
   CUtensorMap tq, tkv;
-  st = mtn::pool_tensor_map(pool, &tkv);
+  st = mtn::pool_tensor_map_paged(pool, &tkv);
   if (st != MTN_OK) return st;
   st = mtn::q_tensor_map(q, total_q, num_q_heads, D, mtn::kBM, &tq);
   if (st != MTN_OK) return st;

@@ -29,6 +29,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 4-D tile whose innermost three coordinates are 0: one page of the paged pool map.
+__device__ __forceinline__ void tma_load_4d_w(void* dst, const CUtensorMap* map, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %2, %2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -61,6 +70,13 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, vol
       }
     }
   }
+}
+
+// 2^x on the SFU (PTX ex2.approx.ftz.f32): 2^-inf = +0, subnormal results flush to 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ------------------------------------------------------------ tcgen05
