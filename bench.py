@@ -742,6 +742,64 @@ def run_cfg4(args, local) -> dict:
             "gpu_launches": 2 * steps}
 
 
+def run_cfg5(args, local) -> dict:
+    """BASELINE config 5's decode attention on one replica: with 1024 requests (prompts U[1024, 16384],
+    seed 11) and the 16 long-context requests of 32768 tokens sharded round-robin over 8 replicas, a
+    replica decodes 128 + 2 of them concurrently.  Qwen2.5-7B attention shapes (28 q / 4 kv heads,
+    head_dim 128), page 16, block tables a random permutation of the pool, one layer.  One step =
+    fused append of one token per sequence + split-KV decode over all 130 sequences; K/V read per
+    step (~2.4 GB) is far above L2."""
+    import torch
+
+    from mitten_b200 import paged
+
+    dev = torch.device("cuda", local)
+    hq, hkv, d, ps = 28, 4, 128, 16
+    lens0 = np.concatenate([np.random.default_rng(11).integers(1024, 16385, size=1024)[::8], [32768, 32768]])
+    n = len(lens0)
+    steps = args.steps
+    pages = [(int(L) + args.warmup + steps + 1 + ps - 1) // ps for L in lens0]
+    num_pages = sum(pages) + 16
+    perm = np.random.default_rng(12).permutation(num_pages).astype(np.int32)
+    pool = paged.PagedKVPool(1, num_pages, ps, hkv, d, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    pool.storage.normal_(generator=gen)
+    indptr = torch.from_numpy(np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)).to(dev)
+    indices = torch.from_numpy(perm[:sum(pages)].copy()).to(dev)
+    q = torch.randn((n, hq, d), generator=gen, device=dev).to(torch.bfloat16)
+    kn = torch.randn((n, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    vn = torch.randn((n, hkv, d), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=dev)
+    ws = paged.DecodeWorkspace.for_shape(pool, n, hq)
+    lens = [torch.from_numpy((lens0 + 1 + j).astype(np.int32)).to(dev) for j in range(args.warmup + steps)]
+    stream = torch.cuda.current_stream()
+
+    def step(j):
+        return lambda: paged.paged_decode(pool, 0, q, indptr, indices, lens[j], k_new=kn, v_new=vn, out=out,
+                                          workspace=ws)
+
+    for j in range(args.warmup):
+        step(j)()
+    t = _graph_steps([step(args.warmup + j) for j in range(steps)], stream)
+    kv = float(np.mean([np.sum(lens0 + 1 + args.warmup + j) for j in range(steps)])) * 2 * hkv * d * 2
+    peak = load_peaks()["hbm_gbs"]
+    code, detail = paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail})")
+    gbs = kv / (t / steps) / 1e9
+    return {"metric": "config 5 replica decode attention: tokens/s and KV-read GB/s", "value": n * steps / t,
+            "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 5, one replica's share at 8 GPUs: 128 seqs ctx U[1024,16384] "
+                                   "seed 11 + 2 seqs at 32768, Hq 28 / Hkv 4 / D 128, page 16, 1 layer, "
+                                   "append fused",
+                       "l2": "K/V read per step ~2.4 GB, far above L2"},
+            "kv_gbs": gbs, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                        "frac": gbs / peak, "traffic": None},
+            "gpu_launches": steps}
+
+
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -770,8 +828,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
-                    help="cfg2 (default) is the headline; cfg3 / cfg4 time those configs' attention layers")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                    help="cfg2 (default) is the headline; cfg3 / cfg4 / cfg5 time those configs' attention layers")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
@@ -784,7 +842,7 @@ def main(argv=None) -> int:
         return 0
     rank, world, local, pg = dist_setup(args.gpus)
     if args.workload != "cfg2":
-        res = (run_cfg3 if args.workload == "cfg3" else run_cfg4)(args, local)
+        res = {"cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5}[args.workload](args, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if pg is not None:
