@@ -39,6 +39,7 @@ constexpr int kBM = 128;   // query rows per CTA (TMEM lanes)
 constexpr int kThreads = 192;
 
 struct PrefillParams {
+  const __nv_bfloat16* q;  // [total_q][hq][head_dim]
   const int32_t* qo_indptr;
   const int32_t* kv_indptr;
   const int32_t* kv_indices;
@@ -64,41 +65,41 @@ template <int D>
 struct PCfg {
   static constexpr int kBN = D <= 128 ? 128 : 64;       // kv tokens per tile
   static constexpr int kDB = D / 64;                    // 64-wide head-dim blocks
-  static constexpr int kQBytes = kBM * D * 2;
+  static constexpr int kStages = 3;                     // K/V ring depth
   static constexpr int kKVBytes = kBN * D * 2;          // one of K or V per stage
-  static constexpr int kPBytes = kBM * kBN * 2;
   static constexpr int kGroupBytes = kDB * 1024;        // 8 kv rows, all head-dim blocks
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;         // [2][kKVBytes]
-  static constexpr int kOffV = kOffK + 2 * kKVBytes;
-  static constexpr int kOffP = kOffV + 2 * kKVBytes;    // [2][kPBytes]
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;   // 15 mbarriers
-  static constexpr int kOffMisc = kOffBar + 16 * 8;     // tmem base, abort flag
+  static constexpr int kOffK = 0;                       // [kStages][kKVBytes]
+  static constexpr int kOffV = kOffK + kStages * kKVBytes;
+  static constexpr int kOffBar = kOffV + kStages * kKVBytes;
+  static constexpr int kOffMisc = kOffBar + 24 * 8;     // tmem base, abort flag
   static constexpr int kSmem = kOffMisc + 64 + 1024;    // + slack for 1024-byte alignment
-  static constexpr int kTmemS = 0;                      // [2] x kBN columns
+  // TMEM columns: S[2] (P of a tile overwrites the first kBN/2 columns of its
+  // S buffer as bf16 pairs), the O accumulator, and Q as bf16 pairs.
+  static constexpr int kTmemS = 0;
   static constexpr int kTmemO = 2 * kBN;
+  static constexpr int kTmemQ = 2 * kBN + D;
   static constexpr int kTmemCols = 512;
-  static_assert(2 * kBN + D <= kTmemCols, "TMEM budget");
+  static_assert(kTmemQ + D / 2 <= kTmemCols, "TMEM budget");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 enum Bar {
-  kQFull = 0,
-  kKFull0 = 1,    // [2] K of tile j landed in stage j&1
-  kVFull0 = 3,    // [2]
-  kKEmpty0 = 5,   // [2] S of tile j done: K stage free
-  kVEmpty0 = 7,   // [2] P V of tile j done: V stage free
-  kSFull0 = 9,    // [2] S buffer j&1 holds tile j's scores
-  kPFull0 = 11,   // [2] P buffer j&1 written (128 softmax threads)
-  kODone0 = 13,   // [2] P V of tile j done: P buffer j&1 free, O current
-  kNumBars = 15
+  kQReady = 0,    // Q in TMEM (128 softmax threads)
+  kKFull0 = 1,    // [3] K of tile j landed in stage j%3
+  kVFull0 = 4,    // [3]
+  kKEmpty0 = 7,   // [3] S of tile j done: K stage free
+  kVEmpty0 = 10,  // [3] P V of tile j done: V stage free
+  kSFull0 = 13,   // [2] S buffer j&1 holds tile j's scores
+  kPFull0 = 15,   // [2] P(j) written over S buffer j&1 (128 softmax threads)
+  kODone0 = 17,   // [2] P V of tile j done: O current
+  kNumBars = 19
 };
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
-    paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
-                         const __grid_constant__ PrefillParams p) {
+    paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
+  constexpr int kS = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
@@ -127,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pages_per_tile = C::kBN / p.ps;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1) ? kBM : 1);
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(&bars[i], (i == kQReady || i == kPFull0 || i == kPFull0 + 1) ? kBM : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -146,10 +148,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // blocks, as [8-row groups][64-column blocks][8 rows][128 bytes]; the
     // pages of a tile sit back to back, so every 8-row group of the tile is
     // kGroupBytes after the previous one.  K of a stage is refilled once S of
-    // the tile two back is done, V once its P V is done.
-    // Page ids are fetched by the whole warp, 32 at a time and one window
-    // ahead, so no load of the block table sits on the issue path; lane 0
-    // issues the copies.
+    // the tile kStages back is done, V once its P V is done.  Page ids are
+    // fetched by the whole warp, 32 at a time and one window ahead, so no
+    // load of the block table sits on the issue path; lane 0 issues.
     const int ppt = pages_per_tile;
     const int lim = min(npages, n_tiles * ppt) - 1;  // last page the CTA reads
     auto fetch = [&](int first) -> int { return p.kv_indices[kv_beg + min(first + lane, lim)]; };
@@ -160,26 +161,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return static_cast<int>((p.row_k + (static_cast<int64_t>(page) * p.hkv + g) * p.ps) >> 3);
     };
-    if (lane == 0) {
-      tc::prefetch_tmap(&tm_q);
-      tc::prefetch_tmap(&tm_kv);
-      mbar_arrive_expect_tx(&bars[kQFull], C::kQBytes);
-      for (int b = 0; b < C::kDB; ++b)
-        tc::tma_load_3d(smem + C::kOffQ + b * kBM * 128, &tm_q, b * 64, h, q0 + tile * kBM, &bars[kQFull]);
-    }
+    if (lane == 0) tc::prefetch_tmap(&tm_kv);
     const int page_bytes = p.ps * D * 2;
     const int dv = static_cast<int>((p.row_v - p.row_k) >> 3);
     int cur = to_row(fetch(0));
     int nxt = fetch(32);
     for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
+      const int st = j % kS;
+      const uint32_t par = ((j / kS) - 1) & 1;  // phase of the use kStages tiles back
       const int first = j * ppt;
       if (j > 0 && (first & 31) == 0) {
         cur = to_row(nxt);
         nxt = fetch(first + 32);
       }
       bool ok = true;
-      if (lane == 0 && j >= 2) ok = tc::wait_bounded(&bars[kKEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 10);
+      if (lane == 0 && j >= kS) ok = tc::wait_bounded(&bars[kKEmpty0 + st], par, abort_flag, p.err, 10);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
       if (lane == 0) mbar_arrive_expect_tx(&bars[kKFull0 + st], C::kKVBytes);
@@ -187,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = __shfl_sync(0xffffffffu, cur, (first & 31) + pi);
         if (lane == 0) tc::tma_load_4d_w(kst + pi * page_bytes, &tm_kv, r, &bars[kKFull0 + st]);
       }
-      if (lane == 0 && j >= 2) ok = tc::wait_bounded(&bars[kVEmpty0 + st], ((j - 2) >> 1) & 1, abort_flag, p.err, 11);
+      if (lane == 0 && j >= kS) ok = tc::wait_bounded(&bars[kVEmpty0 + st], par, abort_flag, p.err, 11);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
       if (lane == 0) mbar_arrive_expect_tx(&bars[kVFull0 + st], C::kKVBytes);
@@ -198,52 +194,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
-    // S(j+1) = Q K^T runs on the tensor cores while the softmax works on
-    // tile j; P(j) V follows once P(j) is written.
+    // Both contractions take their M x K operand from TMEM (Q for S = Q K^T,
+    // P for O += P V), so the tensor core reads only K and V from shared
+    // memory.  S(j+1) runs while the softmax works on tile j; P(j) V follows
+    // once P(j) is written.  tcgen05.mma of one thread execute in issue
+    // order, so S(j+2) overwrites P(j) only after P(j) V has read it.
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kBM, C::kBN, false);
       constexpr uint32_t idO = tc::idesc_bf16(kBM, D, true);
-      const uint64_t dQ = tc::sdesc_sw128(smem_u32(smem + C::kOffQ), 16, 1024);
       // K as the K-major B operand: 8-row groups kGroupBytes apart (SBO).
       const uint64_t dK = tc::sdesc_sw128(smem_u32(smem + C::kOffK), 16, C::kGroupBytes);
-      const uint64_t dP = tc::sdesc_sw128(smem_u32(smem + C::kOffP), 16, 1024);
       // V as the MN-major B operand: 64-wide head-dim blocks 1024 bytes
       // apart (LBO), 8-row groups kGroupBytes apart (SBO).
       const uint64_t dV = tc::sdesc_sw128(smem_u32(smem + C::kOffV), 1024, C::kGroupBytes);
-      // S = Q K^T: 16-wide k steps walk 32 bytes inside a 128-byte swizzle
-      // row, then the next 64-wide head-dim block (Q: kBM*128 bytes on, K:
-      // 1024 bytes on).
+      // S = Q K^T: a 16-wide k step is 8 TMEM columns of Q, and 32 bytes
+      // inside a 128-byte swizzle row of K (then the next 64-wide block).
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!tc::wait_bounded(&bars[kKFull0 + st], (j >> 1) & 1, abort_flag, p.err, 21)) return false;
+        const int st = j % kS;
+        if (!tc::wait_bounded(&bars[kKFull0 + st], (j / kS) & 1, abort_flag, p.err, 21)) return false;
         tc::fence_after_sync();
         const uint64_t b0 = dK + ((st * C::kKVBytes) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
-          tc::mma_bf16(tmem + C::kTmemS + (j & 1) * C::kBN, dQ + (((k >> 2) * kBM * 128 + (k & 3) * 32) >> 4),
-                       b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
+          tc::mma_bf16_ts(tmem + C::kTmemS + (j & 1) * C::kBN, tmem + C::kTmemQ + k * 8,
+                          b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
         tc::mma_commit(&bars[kSFull0 + (j & 1)]);
         tc::mma_commit(&bars[kKEmpty0 + st]);
         return true;
       };
-      // Order per tile: S(j+1) (its K is normally resident by now), then
-      // wait for P(j) and issue P(j) V.  Waits suspend in try_wait.
-      bool ok = tc::wait_bounded(&bars[kQFull], 0, abort_flag, p.err, 20) && issue_s(0);
+      bool ok = tc::wait_bounded(&bars[kQReady], 0, abort_flag, p.err, 20);
+      if (ok) tc::fence_after_sync();
+      ok = ok && issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int st = j % kS;
         if (!tc::wait_bounded(&bars[kPFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 22)) break;
-        if (!tc::wait_bounded(&bars[kVFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 23)) break;
+        if (!tc::wait_bounded(&bars[kVFull0 + st], (j / kS) & 1, abort_flag, p.err, 23)) break;
         tc::fence_after_sync();
-        // O += P V: P K-major (kv tokens contiguous); a 16-token k step is
-        // two 8-row groups of V.
-        const uint64_t a0 = dP + (((j & 1) * C::kPBytes) >> 4);
-        const uint64_t b0 = dV + (((j & 1) * C::kKVBytes) >> 4);
+        // O += P V: a 16-token k step is 8 TMEM columns of P and two 8-row
+        // groups of V.
+        const uint64_t b0 = dV + ((st * C::kKVBytes) >> 4);
 #pragma unroll
         for (int k = 0; k < C::kBN / 16; ++k)
-          tc::mma_bf16(tmem + C::kTmemO, a0 + (((k >> 2) * kBM * 128 + (k & 3) * 32) >> 4),
-                       b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, (j > 0 || k > 0) ? 1u : 0u);
+          tc::mma_bf16_ts(tmem + C::kTmemO, tmem + C::kTmemS + (j & 1) * C::kBN + k * 8,
+                          b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, (j > 0 || k > 0) ? 1u : 0u);
         tc::mma_commit(&bars[kODone0 + (j & 1)]);
-        tc::mma_commit(&bars[kVEmpty0 + (j & 1)]);
+        tc::mma_commit(&bars[kVEmpty0 + st]);
       }
     }
   } else {
@@ -251,17 +247,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x;  // 0..127 == TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int row_pos = min(pos0 + row, last_pos);
+    // Q row (bf16 pairs) into TMEM; rows past the chunk are zero.
+    {
+      const uint4* qrow = reinterpret_cast<const uint4*>(
+          p.q + ((static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h) * D);
+#pragma unroll 1
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 v = row < nrows ? qrow[c * 8 + i] : make_uint4(0u, 0u, 0u, 0u);
+          r[4 * i] = v.x;
+          r[4 * i + 1] = v.y;
+          r[4 * i + 2] = v.z;
+          r[4 * i + 3] = v.w;
+        }
+        tc::tmem_st32(lane_base + C::kTmemQ + c * 32, r);
+      }
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::mbar_arrive(&bars[kQReady]);
+    }
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
       if (!__all_sync(0xffffffffu, ok)) break;  // TMEM loads below are warp-collective
       tc::fence_after_sync();
+      const uint32_t s_col = lane_base + C::kTmemS + (j & 1) * C::kBN;
       float sv[C::kBN];
       {
         uint32_t r[C::kBN / 32][32];
 #pragma unroll
-        for (int c = 0; c < C::kBN / 32; ++c) tc::tmem_ld32(lane_base + C::kTmemS + (j & 1) * C::kBN + c * 32, r[c]);
+        for (int c = 0; c < C::kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, r[c]);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < C::kBN; ++c) sv[c] = __uint_as_float(r[c >> 5][c & 31]);
@@ -303,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l_run = l_run * alpha + psum;
       if (__any_sync(0xffffffffu, moved)) {
-        // O is current once P V of tile j-1 finishes (and with it P buffer j&1 is free).
+        // O is current once P V of tile j-1 finishes.
         ok = tc::wait_bounded(&bars[kODone0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, abort_flag, p.err, 31);
         if (!__all_sync(0xffffffffu, ok)) break;
         tc::fence_after_sync();
@@ -316,27 +334,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           tc::tmem_st32(lane_base + C::kTmemO + c * 32, r);
         }
-        tc::tmem_st_wait();
       }
-      if (j >= 2) {
-        // P buffer j&1 is free once P V of tile j-2 finishes.
-        ok = tc::wait_bounded(&bars[kODone0 + (j & 1)], ((j - 2) >> 1) & 1, abort_flag, p.err, 33);
-        if (!__all_sync(0xffffffffu, ok)) break;
-      }
-      // P (bf16) into the 128B-swizzled K-major tile: 64-key sub-tiles of
-      // 128 rows x 128 bytes; 16-byte chunk index XOR (row % 8).
-      uint8_t* p_tile = smem + C::kOffP + (j & 1) * C::kPBytes;
+      // P (bf16 pairs) over the first kBN/2 columns of this tile's S buffer.
 #pragma unroll
-      for (int c8 = 0; c8 < C::kBN / 8; ++c8) {
-        const int sub = c8 >> 3, chunk = c8 & 7;
-        uint4 w;
-        w.x = f2_to_bf2(sv[c8 * 8 + 0], sv[c8 * 8 + 1]);
-        w.y = f2_to_bf2(sv[c8 * 8 + 2], sv[c8 * 8 + 3]);
-        w.z = f2_to_bf2(sv[c8 * 8 + 4], sv[c8 * 8 + 5]);
-        w.w = f2_to_bf2(sv[c8 * 8 + 6], sv[c8 * 8 + 7]);
-        *reinterpret_cast<uint4*>(p_tile + sub * kBM * 128 + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+      for (int c = 0; c < C::kBN / 64; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = f2_to_bf2(sv[c * 64 + 2 * i], sv[c * 64 + 2 * i + 1]);
+        tc::tmem_st32(s_col + c * 32, r);
       }
-      fence_proxy_async_shared();
+      tc::tmem_st_wait();
       tc::fence_before_sync();
       tc::mbar_arrive(&bars[kPFull0 + (j & 1)]);
     }
@@ -393,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // --------------------------------------------------------------- host side
 
 template <int D>
-int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
+int launch_prefill(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
                    cudaStream_t stream) {
   using C = PCfg<D>;
   static bool configured[64] = {};
@@ -405,7 +412,7 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tkv, const PrefillP
     configured[dev] = true;
   }
   dim3 grid(n_tiles, prm.hq, n_seqs);
-  paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tq, tkv, prm);
+  paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
   return check_launch("paged_prefill_kernel");
 }
 
@@ -444,12 +451,11 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
                 "mtn_paged_prefill: page_size %d must be a multiple of 8 dividing %d", pool->page_size, bn);
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
                 "mtn_paged_prefill: q/o must be 16-byte aligned");
-  CUtensorMap tq, tkv;
+  CUtensorMap tkv;
   st = mtn::pool_tensor_map_paged(pool, &tkv);
   if (st != MTN_OK) return st;
-  st = mtn::q_tensor_map(q, total_q, num_q_heads, D, mtn::kBM, &tq);
-  if (st != MTN_OK) return st;
   mtn::PrefillParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(q);
   prm.qo_indptr = qo_indptr;
   prm.kv_indptr = kv_indptr;
   prm.kv_indices = kv_indices;
@@ -470,9 +476,9 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
   MTN_CHECK_ARG(n_tiles <= 65535 * 32, "mtn_paged_prefill: max_q_len too large");
   auto s = static_cast<cudaStream_t>(stream);
   switch (D) {
-    case 64: return mtn::launch_prefill<64>(tq, tkv, prm, n_tiles, n_seqs, s);
-    case 128: return mtn::launch_prefill<128>(tq, tkv, prm, n_tiles, n_seqs, s);
-    default: return mtn::launch_prefill<256>(tq, tkv, prm, n_tiles, n_seqs, s);
+    case 64: return mtn::launch_prefill<64>(tkv, prm, n_tiles, n_seqs, s);
+    case 128: return mtn::launch_prefill<128>(tkv, prm, n_tiles, n_seqs, s);
+    default: return mtn::launch_prefill<256>(tkv, prm, n_tiles, n_seqs, s);
   }
 }
 
