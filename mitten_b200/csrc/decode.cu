@@ -91,7 +91,14 @@ struct DecodeParams {
 template <int D>
 struct DCfg {
   static constexpr int kDB = D / 64;                       // 64-wide head-dim blocks
+  // D = 256: K and V of a tile are staged as head-dim halves (32 KB items,
+  // 4 per tile) in a 6-slot ring, so 1.5 tiles are in flight; otherwise
+  // kStages whole-tile K+V stages.  kStages is also how many tiles ahead the
+  // producer fetches page ids.
+  static constexpr bool kHalf = D == 256;
   static constexpr int kStages = D == 256 ? 1 : 3;
+  static constexpr int kRingSlots = 6;
+  static constexpr int kHalfBytes = kTile * 128 * 2;       // 128 tokens x two 64-column blocks
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
   static constexpr int kQBytes = kN * D * 2;               // Q^T operand: 16 rows x D
   static constexpr int kKVBytes = kTile * D * 2;           // one of K or V per stage
@@ -105,8 +112,8 @@ struct DCfg {
   static constexpr int kSmallBytes = kOffPend + 32 + 16;
   static constexpr int kOffQ = 0;                          // [2] relative to the aligned operand area
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
-  static constexpr int kOffV = kOffK + kStages * kKVBytes;
-  static constexpr int kOffP = kOffV + kStages * kKVBytes;
+  static constexpr int kOffV = kHalf ? kOffK : kOffK + kStages * kKVBytes;
+  static constexpr int kOffP = kHalf ? kOffK + kRingSlots * kHalfBytes : kOffV + kStages * kKVBytes;
   static constexpr int kBigBytes = kOffP + 2 * kPBytes;  // P^T double-buffered
   static constexpr int kSmem = kSmallBytes + 1023 + kBigBytes;
   static constexpr int kMO = D == 64 ? 64 : 128;           // MMA2 M
@@ -117,15 +124,15 @@ struct DCfg {
 };
 
 enum Bar {
-  kKVFull0 = 0,   // [3]
-  kKVEmpty0 = 3,  // [3]
-  kSFull0 = 6,    // [2]
-  kPFull0 = 8,    // [2] P^T buffer i&1 written (softmax -> MMA)
-  kODone0 = 10,   // [2] P V of tile i done: P^T buffer i&1 free, O^T current
-  kQFull0 = 12,   // [2]
-  kQEmpty0 = 14,  // [2]
-  kOFree0 = 16,   // [2]
-  kNumBars = 18
+  kKVFull0 = 0,   // [6] stage (or ring slot) loaded
+  kKVEmpty0 = 6,  // [6] stage (or ring slot) consumed
+  kSFull0 = 12,   // [2]
+  kPFull0 = 14,   // [2] P^T buffer i&1 written (softmax -> MMA)
+  kODone0 = 16,   // [2] P V of tile i done: P^T buffer i&1 free, O^T current
+  kQFull0 = 18,   // [2]
+  kQEmpty0 = 20,  // [2]
+  kOFree0 = 22,   // [2]
+  kNumBars = 24
 };
 
 // Final normalisation of one output element: o/l with the phantom key folded in.
@@ -445,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
           ++qcnt;
         }
-        if (i >= C::kStages) {
+        if (!C::kHalf && i >= C::kStages) {
           bool ok = true;
           if (lane == 0)
             ok = tc::wait_bounded(&bars[kKVEmpty0 + st], ((i / C::kStages) - 1) & 1, abort_flag, p.err, 10);
@@ -467,6 +474,40 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
           __syncwarp();
         }
+        if constexpr (C::kHalf) {
+          // Items 4i..4i+3 of the ring: K blocks 0-1, K blocks 2-3, V blocks
+          // 0-1, V blocks 2-3; item n sits in slot n % 6, refilled once the
+          // MMA that read item n - 6 is done.
+          int64_t page = lane < tile_pages ? pg[st] : 0;
+          if (lane < tile_pages && (page < 0 || page >= p.num_pages)) {
+            record_error(p.err, kDevErrBadPage, w.s);
+            page = 0;  // past the sequence's last page: reload a valid page (masked)
+          }
+          const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
+          const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
+          for (int hh = 0; hh < 4; ++hh) {
+            const int n = 4 * i + hh;
+            const int slot = n % C::kRingSlots;
+            bool ok = true;
+            if (lane == 0 && n >= C::kRingSlots)
+              ok = tc::wait_bounded(&bars[kKVEmpty0 + slot], ((n / C::kRingSlots) - 1) & 1, abort_flag, p.err, 12);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+              run = false;
+              break;
+            }
+            if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + slot], C::kHalfBytes);
+            __syncwarp();
+            if (lane < tile_pages) {
+              uint8_t* dst = big + C::kOffK + slot * C::kHalfBytes + lane * p.ps * 128;
+              const int row = static_cast<int>(hh < 2 ? rk : rv);
+#pragma unroll
+              for (int bb = 0; bb < 2; ++bb)
+                tc::tma_load_2d(dst + bb * kTile * 128, &tm_kv, ((hh & 1) * 2 + bb) * 64, row,
+                                &bars[kKVFull0 + slot]);
+            }
+          }
+          if (!run) break;
+        } else {
         if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
         __syncwarp();
         if (lane < tile_pages) {
@@ -485,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             tc::tma_load_2d(kst + off, &tm_kv, b * 64, static_cast<int>(rk), &bars[kKVFull0 + st]);
             tc::tma_load_2d(vst + off, &tm_kv, b * 64, static_cast<int>(rv), &bars[kKVFull0 + st]);
           }
+        }
         }
         if (i + C::kStages < n_local) {
           fetch(pg[st], apg[st], apos[st], ak[st], av[st]);  // wp is at tile i + kStages
@@ -519,16 +561,35 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           ++q_seg;
           if (!tc::wait_bounded(&bars[kQFull0 + (q_seg & 1)], (q_seg >> 1) & 1, abort_flag, p.err, 22)) return false;
         }
+        const uint64_t b0 = dQ + (((q_seg & 1) * C::kQBytes) >> 4);
+        if constexpr (C::kHalf) {
+          // K halves: ring items 4i (blocks 0-1) and 4i+1 (blocks 2-3).
+          const int s0 = (4 * i) % C::kRingSlots, s1 = (4 * i + 1) % C::kRingSlots;
+          if (!tc::wait_bounded(&bars[kKVFull0 + s0], ((4 * i) / C::kRingSlots) & 1, abort_flag, p.err, 24) ||
+              !tc::wait_bounded(&bars[kKVFull0 + s1], ((4 * i + 1) / C::kRingSlots) & 1, abort_flag, p.err, 25))
+            return false;
+          tc::fence_after_sync();
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const int slot = (k >> 3) ? s1 : s0;
+            tc::mma_bf16(tmem + C::kTmemS + (i & 1) * kN,
+                         dK + ((slot * C::kHalfBytes + ((k >> 2) & 1) * kTile * 128 + (k & 3) * 32) >> 4),
+                         b0 + (((k >> 2) * kN * 128 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
+          }
+          tc::mma_commit(&bars[kSFull0 + (i & 1)]);
+          tc::mma_commit(&bars[kKVEmpty0 + s0]);
+          tc::mma_commit(&bars[kKVEmpty0 + s1]);
+        } else {
         const int st = i % C::kStages;
         if (!tc::wait_bounded(&bars[kKVFull0 + st], (i / C::kStages) & 1, abort_flag, p.err, 20)) return false;
         tc::fence_after_sync();
         const uint64_t a0 = dK + ((st * C::kKVBytes) >> 4);
-        const uint64_t b0 = dQ + (((q_seg & 1) * C::kQBytes) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
           tc::mma_bf16(tmem + C::kTmemS + (i & 1) * kN, a0 + (((k >> 2) * kTile * 128 + (k & 3) * 32) >> 4),
                        b0 + (((k >> 2) * kN * 128 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
         tc::mma_commit(&bars[kSFull0 + (i & 1)]);
+        }
         if (last) tc::mma_commit(&bars[kQEmpty0 + (q_seg & 1)]);
         if (i + 1 < n_local) wsw.next(p);
         return true;
@@ -537,6 +598,9 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       auto s_ready = [&](int j) -> bool {
         const bool first = (j == 0) || wsw.j == 0;
         if (first && !mbar_test_wait(&bars[kQFull0 + ((q_seg + 1) & 1)], ((q_seg + 1) >> 1) & 1)) return false;
+        if constexpr (C::kHalf)
+          return mbar_test_wait(&bars[kKVFull0 + (4 * j) % C::kRingSlots], ((4 * j) / C::kRingSlots) & 1) &&
+                 mbar_test_wait(&bars[kKVFull0 + (4 * j + 1) % C::kRingSlots], ((4 * j + 1) / C::kRingSlots) & 1);
         return mbar_test_wait(&bars[kKVFull0 + j % C::kStages], (j / C::kStages) & 1);
       };
       bool ok = true;
@@ -585,11 +649,32 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
           if (!ok) break;
         }
+        const uint64_t b0 = dP + (((i & 1) * C::kPBytes) >> 4);
+        const uint32_t o_col = C::kTmemO + (o_seg & 1) * 32;
+        if constexpr (C::kHalf) {
+          // V halves: ring items 4i+2 (head dims 0-127) and 4i+3 (128-255),
+          // one M = 128 block of O^T each.
+          const int s2 = (4 * i + 2) % C::kRingSlots, s3 = (4 * i + 3) % C::kRingSlots;
+          if (!tc::wait_bounded(&bars[kKVFull0 + s2], ((4 * i + 2) / C::kRingSlots) & 1, abort_flag, p.err, 26) ||
+              !tc::wait_bounded(&bars[kKVFull0 + s3], ((4 * i + 3) / C::kRingSlots) & 1, abort_flag, p.err, 27))
+            break;
+          tc::fence_after_sync();
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k) {
+#pragma unroll
+            for (int mb = 0; mb < 2; ++mb)
+              tc::mma_bf16(tmem + o_col + mb * kN, dV + ((((mb ? s3 : s2) * C::kHalfBytes) + k * 16 * 128) >> 4),
+                           b0 + (((k >> 2) * kN * 128 + (k & 3) * 32) >> 4), idO, (!first || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&bars[kODone0 + (i & 1)]);
+          tc::mma_commit(&bars[kKVEmpty0 + s2]);
+          tc::mma_commit(&bars[kKVEmpty0 + s3]);
+          if (i + 1 < n_local) wo.next(p);
+          continue;
+        }
         tc::fence_after_sync();
         const int st = i % C::kStages;
         const uint64_t a0 = dV + ((st * C::kKVBytes) >> 4);
-        const uint64_t b0 = dP + (((i & 1) * C::kPBytes) >> 4);
-        const uint32_t o_col = C::kTmemO + (o_seg & 1) * 32;
         // O^T += V^T P^T: A = V^T (MN-major: head dim contiguous; 64-wide
         // blocks kTile*128 bytes apart), B = P^T (K-major over tokens).
 #pragma unroll

@@ -247,20 +247,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x;  // 0..127 == TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int row_pos = min(pos0 + row, last_pos);
-    // Q row (bf16 pairs) into TMEM; rows past the chunk are zero.
+    // Q row (bf16 pairs) into TMEM, every load in flight at once; rows past
+    // the chunk are zero.
     {
       const uint4* qrow = reinterpret_cast<const uint4*>(
           p.q + ((static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h) * D);
-#pragma unroll 1
+      uint4 v[D / 8];
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) v[i] = row < nrows ? qrow[i] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         uint32_t r[32];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const uint4 v = row < nrows ? qrow[c * 8 + i] : make_uint4(0u, 0u, 0u, 0u);
-          r[4 * i] = v.x;
-          r[4 * i + 1] = v.y;
-          r[4 * i + 2] = v.z;
-          r[4 * i + 3] = v.w;
+          r[4 * i] = v[c * 8 + i].x;
+          r[4 * i + 1] = v[c * 8 + i].y;
+          r[4 * i + 2] = v[c * 8 + i].z;
+          r[4 * i + 3] = v[c * 8 + i].w;
         }
         tc::tmem_st32(lane_base + C::kTmemQ + c * 32, r);
       }

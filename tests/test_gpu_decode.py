@@ -61,6 +61,17 @@ def test_decode_shapes(cuda_device, hq, hkv, d):
     assert paged.device_error(0) == (0, 0)
 
 
+def test_decode_head_dim_256_many_tiles_per_cta(cuda_device):
+    # ~700 tiles of 128 tokens over the persistent grid: every CTA streams
+    # several tiles, so the 6-slot ring of head-dim halves wraps many times.
+    rng = np.random.default_rng(31)
+    lens = [int(x) for x in rng.integers(1500, 2600, size=40)]
+    case = make_case(lens, 1, 256, seed=32)
+    q, qu, out = run_decode(case, 8, 256)
+    check(case, 8, 256, q, qu, out)
+    assert paged.device_error(0) == (0, 0)
+
+
 def test_decode_one_long_sequence_split_over_many_ctas(cuda_device):
     # 79 tiles x 2 kv heads < the CTA count: every CTA holds a piece of a
     # segment, so the cross-CTA merge runs for both segments.
