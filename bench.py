@@ -788,6 +788,7 @@ def run_cfg5(args, local) -> dict:
     if code:
         raise SystemExit(f"device error {code} (detail {detail})")
     gbs = kv / (t / steps) / 1e9
+    pre = run_cfg5_prefill(args, dev, stream)
     return {"metric": "config 5 replica decode attention: tokens/s and KV-read GB/s", "value": n * steps / t,
             "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * t / steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
@@ -797,7 +798,47 @@ def run_cfg5(args, local) -> dict:
                        "l2": "K/V read per step ~2.4 GB, far above L2"},
             "kv_gbs": gbs, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                                         "frac": gbs / peak, "traffic": None},
-            "gpu_launches": steps}
+            "prefill": pre, "gpu_launches": steps + pre["launches"]}
+
+
+def run_cfg5_prefill(args, dev, stream) -> dict:
+    """Chunked prefill at config 5's shapes: 16 requests each with a 512-token chunk after a prior
+    context drawn from its prompt range (U{0, 512, ..., 15872}, seed 14), Qwen2.5-7B attention shapes
+    (28 q / 4 kv heads, head_dim 128), page 16, one layer.  1792 (query tile, head, sequence) units
+    fill the grid several times over, so the kernel's per-SM rate shows rather than one unit's length."""
+    import torch
+
+    from mitten_b200 import paged
+
+    hq, hkv, d, ps, n_pf, chunk = 28, 4, 128, 16, 16, 512
+    pp = np.random.default_rng(14).integers(0, 32, size=n_pf) * 512
+    pf_pages = [(int(P) + chunk + ps - 1) // ps for P in pp]
+    num_pages = sum(pf_pages) + 16
+    perm = np.random.default_rng(15).permutation(num_pages).astype(np.int32)
+    pool = paged.PagedKVPool(1, num_pages, ps, hkv, d, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(16)
+    pool.storage.normal_(generator=gen)
+    p_indptr = torch.from_numpy(np.concatenate([[0], np.cumsum(pf_pages)]).astype(np.int32)).to(dev)
+    p_indices = torch.from_numpy(perm[:sum(pf_pages)].copy()).to(dev)
+    qo = torch.from_numpy(np.arange(0, (n_pf + 1) * chunk, chunk).astype(np.int32)).to(dev)
+    p_lens = torch.from_numpy((pp + chunk).astype(np.int32)).to(dev)
+    qp = torch.randn((n_pf * chunk, hq, d), generator=gen, device=dev).to(torch.bfloat16)
+    op = torch.empty((n_pf * chunk, hq, d), dtype=torch.bfloat16, device=dev)
+
+    def pre():
+        paged.paged_prefill(pool, 0, qp, qo, p_indptr, p_indices, p_lens, chunk, out=op)
+
+    for _ in range(args.warmup):
+        pre()
+    steps = max(3, min(args.steps, 10))
+    t = _graph_steps([pre] * steps, stream)
+    flops = sum(4.0 * hq * d * chunk * (int(P) + (chunk + 1) / 2) for P in pp)
+    peak = load_peaks()["bf16_tflops"]
+    tf = flops / (t / steps) / 1e12
+    return {"workload": "16 chunks of 512 after prior U{0,512..15872} seed 14, Hq 28 / Hkv 4 / D 128, page 16",
+            "us_per_step": 1e6 * t / steps, "tflops": tf, "frac": tf / peak, "peak_tflops": peak,
+            "launches": steps}
 
 
 def load_peaks() -> dict:
