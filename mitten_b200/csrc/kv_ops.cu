@@ -15,7 +15,7 @@ namespace mtn {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 1;     // vectors per thread per pass: measured best for these short, HBM-bound calls
 
 int grid_for(int64_t work_items, int64_t items_per_block) {
   const int sms = sm_count();
@@ -88,11 +88,13 @@ __device__ __forceinline__ uint4 load_chunk<float>(const float* p) {
 
 // Idx is the work-item index type: 32-bit when every index fits (the
 // common case; a 64-bit division per 16 bytes would dominate the kernel).
-template <typename SrcT, typename Idx>
+// P2: hkv and head_dim / 8 are powers of two (lg_chunks, lg_per_tok their
+// logs), so the work index splits with shifts instead of divisions.
+template <typename SrcT, typename Idx, bool P2>
 __global__ void __launch_bounds__(kThreads) kv_append_kernel(
     __nv_bfloat16* __restrict__ kdst, __nv_bfloat16* __restrict__ vdst, int64_t num_pages, int hkv, int ps,
     int d, const SrcT* __restrict__ k, const SrcT* __restrict__ v, int64_t src_stride,
-    const int64_t* __restrict__ slots, int64_t n_tokens, int* err) {
+    const int64_t* __restrict__ slots, int64_t n_tokens, int* err, int lg_chunks, int lg_per_tok) {
   const int chunks = d >> 3;
   const Idx per_tok = static_cast<Idx>(hkv) * chunks;
   const Idx total = static_cast<Idx>(n_tokens) * per_tok;
@@ -106,9 +108,9 @@ __global__ void __launch_bounds__(kThreads) kv_append_kernel(
       const Idx i = base + u * stride;
       dst[u] = -1;
       if (i < total) {
-        const Idx t = i / per_tok;
+        const Idx t = P2 ? (i >> lg_per_tok) : i / per_tok;
         const int rem = static_cast<int>(i - t * per_tok);
-        const int h = rem / chunks;
+        const int h = P2 ? (rem >> lg_chunks) : rem / chunks;
         const int c = rem - h * chunks;
         const int64_t slot = slots[t];
         if (slot >= 0) {
@@ -306,29 +308,29 @@ int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer, const void* k, const
   auto s = static_cast<cudaStream_t>(stream);
   // 32-bit work indices while every index (plus one grid stride) stays below 2^31.
   const bool narrow = work + static_cast<int64_t>(grid) * mtn::kThreads * mtn::kUnroll < (int64_t(1) << 31);
+  const int chunks = pool->head_dim / 8;
+  const int per_tok = pool->num_kv_heads * chunks;
+  const bool p2 = (chunks & (chunks - 1)) == 0 && (per_tok & (per_tok - 1)) == 0;
+  const int lg_c = p2 ? __builtin_ctz(static_cast<unsigned>(chunks)) : 0;
+  const int lg_t = p2 ? __builtin_ctz(static_cast<unsigned>(per_tok)) : 0;
+#define MTN_APPEND_LAUNCH(SRC, IDX, P2F, KP, VP)                                                              \
+  mtn::kv_append_kernel<SRC, IDX, P2F><<<grid, mtn::kThreads, 0, s>>>(                                       \
+      kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, KP, VP, src_stride, slots, \
+      n_tokens, mtn::device_error_ptr(), lg_c, lg_t)
   if (src_dtype == MTN_DTYPE_BF16) {
     auto kb = static_cast<const __nv_bfloat16*>(k);
     auto vb = static_cast<const __nv_bfloat16*>(v);
-    if (narrow)
-      mtn::kv_append_kernel<__nv_bfloat16, uint32_t><<<grid, mtn::kThreads, 0, s>>>(
-          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kb, vb, src_stride, slots,
-          n_tokens, mtn::device_error_ptr());
-    else
-      mtn::kv_append_kernel<__nv_bfloat16, int64_t><<<grid, mtn::kThreads, 0, s>>>(
-          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kb, vb, src_stride, slots,
-          n_tokens, mtn::device_error_ptr());
+    if (narrow && p2) MTN_APPEND_LAUNCH(__nv_bfloat16, uint32_t, true, kb, vb);
+    else if (narrow) MTN_APPEND_LAUNCH(__nv_bfloat16, uint32_t, false, kb, vb);
+    else MTN_APPEND_LAUNCH(__nv_bfloat16, int64_t, false, kb, vb);
   } else {
     auto kf = static_cast<const float*>(k);
     auto vf = static_cast<const float*>(v);
-    if (narrow)
-      mtn::kv_append_kernel<float, uint32_t><<<grid, mtn::kThreads, 0, s>>>(
-          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kf, vf, src_stride, slots,
-          n_tokens, mtn::device_error_ptr());
-    else
-      mtn::kv_append_kernel<float, int64_t><<<grid, mtn::kThreads, 0, s>>>(
-          kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, kf, vf, src_stride, slots,
-          n_tokens, mtn::device_error_ptr());
+    if (narrow && p2) MTN_APPEND_LAUNCH(float, uint32_t, true, kf, vf);
+    else if (narrow) MTN_APPEND_LAUNCH(float, uint32_t, false, kf, vf);
+    else MTN_APPEND_LAUNCH(float, int64_t, false, kf, vf);
   }
+#undef MTN_APPEND_LAUNCH
   return mtn::check_launch("kv_append_kernel");
 }
 
