@@ -575,6 +575,94 @@ def _graph_steps(fns, stream):
     return a.elapsed_time(b) * 1e-3
 
 
+def model_weights(shape, device, seed: int = 0, std: float = 0.02) -> dict:
+    """Random N(0, std) weights of a QwenPagedModel shape, generated on the device (norm weights 0, i.e.
+    a (1 + w) scale of 1), under the names the model reads."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    h, d, L = shape.hidden, shape.head_dim, shape.layers
+
+    def rnd(*sz):
+        return torch.randn(sz, generator=g, device=device, dtype=torch.float32) * std
+
+    w = {"embedding.weight": rnd(shape.vocab, h), "norm.weight": torch.zeros(h, device=device)}
+    for li in range(L):
+        m, pfx = f"layers.{li}.mixer", f"layers.{li}"
+        w[f"{m}.q_proj.weight"] = rnd(shape.hq * d * (2 if shape.gated_q else 1), h)
+        w[f"{m}.k_proj.weight"] = rnd(shape.hkv * d, h)
+        w[f"{m}.v_proj.weight"] = rnd(shape.hkv * d, h)
+        w[f"{m}.o_proj.weight"] = rnd(h, shape.hq * d)
+        if shape.qk_norm:
+            w[f"{m}.q_norm.weight"] = torch.zeros(d, device=device)
+            w[f"{m}.k_norm.weight"] = torch.zeros(d, device=device)
+        w[f"{pfx}.norm.weight"] = torch.zeros(h, device=device)
+        w[f"{pfx}.ffn_norm.weight"] = torch.zeros(h, device=device)
+        w[f"{pfx}.mlp.gate_proj.weight"] = rnd(shape.inter, h)
+        w[f"{pfx}.mlp.up_proj.weight"] = rnd(shape.inter, h)
+        w[f"{pfx}.mlp.down_proj.weight"] = rnd(h, shape.inter)
+    return w
+
+
+def run_cfg1(args, local) -> dict:
+    """BASELINE config 1 end to end through the engine: the Qwen2.5-0.5B-shaped model (24 layers, hidden
+    896, 14 q / 2 kv heads, head_dim 64, SwiGLU 4864, vocab 151936, tied embeddings, random N(0, 0.02)
+    f32 weights), page 16, 4 requests of 128 random prompt tokens (seed 1) and 32 greedy decode steps.
+    Each engine iteration is the scheduler mirror (C++) -> QwenPagedModel.forward (dense parts on the
+    device BLAS in f32, attention on the paged kernels) -> device argmax -> token hand-back.  Reported:
+    decode tokens/s over the 32 decode iterations (CUDA events around the loop, so host scheduling and
+    launches count) and the prefill iteration's time."""
+    import torch
+
+    from mitten_b200 import host, model as M
+
+    dev = torch.device("cuda", local)
+    shape = M.QWEN_CONFIG1
+    n_req, prompt_len, steps = 4, 128, 32
+    weights = model_weights(shape, dev, seed=0)
+    prompts = np.random.default_rng(1).integers(0, shape.vocab, size=(n_req, prompt_len)).astype(np.uint32)
+    times = []
+    for trial in range(2):  # the first pass warms the kernels and the BLAS
+        mdl = M.QwenPagedModel(shape, weights, num_pages=256, page_size=16, device=dev)
+        sched = host.Scheduler(256, 16, max_prefill_tokens_per_iter=512, max_decode_batch_size=8,
+                               eos_token_ids=(shape.vocab,))
+        for rid in range(n_req):
+            sched.add_request(rid, prompts[rid], temperature=0.0, max_new_tokens=steps)
+        eng = M.Engine(mdl, sched)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        eng.step()  # the prefill iteration (all four prompts fit the 512-token budget)
+        ev[1].record()
+        eng.run()
+        ev[2].record()
+        torch.cuda.synchronize()
+        times.append((ev[0].elapsed_time(ev[1]) * 1e-3, ev[1].elapsed_time(ev[2]) * 1e-3, eng.iterations))
+        outs = [sched.request_output(r) for r in range(n_req)]
+    t_pre, t_dec, iters = times[-1]
+    dec_tokens = n_req * (steps - 1)  # the prefill iteration already emitted each request's first token
+    # device time of one decode step alone: the batch-4 graph replayed back to back
+    g = mdl._graphs.get(n_req)
+    replay_ms = None
+    if g is not None and g.graph is not None:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for _ in range(10):
+            g.graph.replay()
+        ev[1].record()
+        torch.cuda.synchronize()
+        replay_ms = ev[0].elapsed_time(ev[1]) / 10
+    return {"metric": "config 1 engine decode tokens/s (Qwen2.5-0.5B shape, random weights)",
+            "value": dec_tokens / t_dec, "unit": "tokens/s", "n_gpus": 1, "steps": iters - 1, "warmup": 1,
+            "ms_per_step": 1e3 * t_dec / max(iters - 1, 1), "higher_is_better": True, "dtype": "f32 dense, bf16 K/V",
+            "data": "synthetic (random N(0,0.02) weights seed 0, random prompt tokens seed 1)",
+            "config": {"workload": "BASELINE config 1: 4 requests x 128-token prompts, 32 greedy decode steps, "
+                                   "page 16, whole engine loop (scheduler, model forward, device argmax)"},
+            "prefill_iteration_ms": 1e3 * t_pre, "decode_graph_replay_ms": replay_ms,
+            "outputs_per_request": [len(o) for o in outs],
+            "gpu_launches": None}
+
+
 def run_cfg3(args, local) -> dict:
     """BASELINE config 3's attention layer: 128 sequences share a 1032-token prefix (64 full pages and
     a partial one, refcounted), each with its own suffix U[64, 512] (seed 6) and its own copy of the
@@ -869,8 +957,9 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
-                    help="cfg2 (default) is the headline; cfg3 / cfg4 / cfg5 time those configs' attention layers")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                    help="cfg2 (default) is the headline; cfg3 / cfg4 / cfg5 time those configs' attention "
+                         "layers; cfg1 runs config 1's model through the engine")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
@@ -883,7 +972,7 @@ def main(argv=None) -> int:
         return 0
     rank, world, local, pg = dist_setup(args.gpus)
     if args.workload != "cfg2":
-        res = {"cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5}[args.workload](args, local)
+        res = {"cfg1": run_cfg1, "cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5}[args.workload](args, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if pg is not None:

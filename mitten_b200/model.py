@@ -63,10 +63,9 @@ GEMMA_2B = DecoderShape(hidden=2048, layers=18, hq=8, hkv=1, head_dim=256, inter
                         gated_q=False, qk_norm=False, phantom=False, mlp="geglu")
 
 
-def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """RmsNorm::forward (model.rs:98-108): x / sqrt(mean(x^2) + eps) * (1 + w), last axis."""
-    var = x.square().mean(dim=-1, keepdim=True)
-    return x * torch.rsqrt(var + eps) * (w + 1.0)
+def _rms(x: torch.Tensor, w1: torch.Tensor, eps: float) -> torch.Tensor:
+    """RmsNorm::forward (model.rs:98-108): x / sqrt(mean(x^2) + eps) * (1 + w), last axis; w1 = 1 + w."""
+    return torch.nn.functional.rms_norm(x, (x.shape[-1],), w1, eps)
 
 
 class QwenPagedModel:
@@ -77,6 +76,9 @@ class QwenPagedModel:
         self.s = shape
         self.dev = torch.device(device)
         self.w = {k: torch.as_tensor(v).to(self.dev, torch.float32) for k, v in weights.items()}
+        # RMSNorm scales (1 + w), formed once
+        for k in [k for k in self.w if k.endswith("norm.weight")]:
+            self.w[k] = self.w[k] + 1.0
         self.pool = paged.PagedKVPool(shape.layers, num_pages, page_size, shape.hkv, shape.head_dim, device=self.dev)
         half = shape.rotary_dim // 2
         i = np.arange(half, dtype=np.float32)
@@ -87,13 +89,18 @@ class QwenPagedModel:
         self.scale = shape.head_dim ** -0.5
         self._ws = None
         self._ws_seqs = 0
+        self._graphs: dict[int, _DecodeGraph] = {}
 
     # ------------------------------------------------------------ pieces
-    def _rope(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    def _rope_tables(self, pos: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos and sin of pos * inv_freq [T, 1, rotary_dim/2], shared by q, k and every layer."""
+        ang = pos.to(torch.float32)[:, None, None] * self.inv_freq[None, None, :]
+        return torch.cos(ang), torch.sin(ang)
+
+    def _rope(self, x: torch.Tensor, cs: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
         """apply_rope (model.rs:508-540): rotate-half over the first rotary_dim of each head."""
         rd, half = self.s.rotary_dim, self.s.rotary_dim // 2
-        ang = pos.to(torch.float32)[:, None, None] * self.inv_freq[None, None, :]
-        c, s = torch.cos(ang), torch.sin(ang)
+        c, s = cs
         x1, x2 = x[..., :half], x[..., half:rd]
         out = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
         if rd < x.shape[-1]:
@@ -112,7 +119,7 @@ class QwenPagedModel:
         act = torch.nn.functional.silu(g) if self.s.mlp == "swiglu" else torch.nn.functional.gelu(g, approximate="tanh")
         return (act * u) @ self.w[f"{p}.mlp.down_proj.weight"].T
 
-    def _attention(self, li: int, h: torch.Tensor, pos: torch.Tensor, meta: dict) -> torch.Tensor:
+    def _attention(self, li: int, h: torch.Tensor, cs: tuple[torch.Tensor, torch.Tensor], meta: dict) -> torch.Tensor:
         """GatedAttention::forward (model.rs:369-422) for every row of the batch."""
         s, w = self.s, self.w
         m = f"layers.{li}.mixer"
@@ -128,7 +135,7 @@ class QwenPagedModel:
         if s.qk_norm:
             q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
             k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
-        q, k = self._rope(q, pos), self._rope(k, pos)
+        q, k = self._rope(q, cs), self._rope(k, cs)
         attn = torch.empty((T, s.hq, s.head_dim), dtype=torch.float32, device=self.dev)
         tp = meta["tp"]
         if tp:
@@ -167,24 +174,99 @@ class QwenPagedModel:
             meta["ws"] = self._decode_ws(n - npf)
         return meta
 
-    @torch.no_grad()
-    def forward(self, b) -> torch.Tensor:
-        """Logits [n_reqs, vocab] (f32, on the device) of each request's last row."""
-        s, w = self.s, self.w
+    def _cow(self, b) -> None:
         if len(b.cow_src):
             self.pool.page_copy(torch.from_numpy(np.ascontiguousarray(b.cow_src, np.int32)).to(self.dev),
                                 torch.from_numpy(np.ascontiguousarray(b.cow_dst, np.int32)).to(self.dev))
+
+    def _forward_rows(self, ids: torch.Tensor, pos: torch.Tensor, meta: dict, last: torch.Tensor) -> torch.Tensor:
+        """The device part of the forward: every launch depends only on tensors, so it can be captured."""
+        s, w = self.s, self.w
+        x = w["embedding.weight"][ids]  # the vocab-split lookup of model.rs:159-183 is a plain lookup
+        cs = self._rope_tables(pos)
+        for li in range(s.layers):
+            p = f"layers.{li}"
+            x = x + self._attention(li, _rms(x, w[f"{p}.norm.weight"], s.eps), cs, meta)
+            x = x + self._mlp(_rms(x, w[f"{p}.ffn_norm.weight"], s.eps), p)
+        h = _rms(x[last], w["norm.weight"], s.eps)
+        return (h @ w["embedding.weight"].T).contiguous()  # tied LM head (model.rs:262-276)
+
+    @torch.no_grad()
+    def forward(self, b) -> torch.Tensor:
+        """Logits [n_reqs, vocab] (f32, on the device) of each request's last row."""
+        self._cow(b)
         meta = self.batch_meta(b)
         ids = torch.from_numpy(b.input_ids.astype(np.int64)).to(self.dev)
         pos = torch.from_numpy(np.ascontiguousarray(b.position_ids, np.int32)).to(self.dev)
-        x = w["embedding.weight"][ids]  # the vocab-split lookup of model.rs:159-183 is a plain lookup
-        for li in range(s.layers):
-            p = f"layers.{li}"
-            x = x + self._attention(li, _rms(x, w[f"{p}.norm.weight"], s.eps), pos, meta)
-            x = x + self._mlp(_rms(x, w[f"{p}.ffn_norm.weight"], s.eps), p)
         last = torch.from_numpy(b.qo_indptr[1:].astype(np.int64) - 1).to(self.dev)
-        h = _rms(x[last], w["norm.weight"], s.eps)
-        return (h @ w["embedding.weight"].T).contiguous()  # tied LM head (model.rs:262-276)
+        return self._forward_rows(ids, pos, meta, last)
+
+    @torch.no_grad()
+    def decode_step(self, b) -> torch.Tensor:
+        """forward() for a decode-only batch through a CUDA graph per batch size.
+
+        The first batch of a size runs eagerly, then its forward is captured;
+        later batches of that size copy their token ids, positions and CSR
+        metadata into the graph's static buffers and replay it.  The graph
+        holds the paged kernels' launches like any other, so the whole step
+        (every layer's projections, norms, RoPE, fused append + decode
+        attention, MLP and the LM head) replays without per-launch overhead."""
+        if b.n_prefill:
+            return self.forward(b)
+        self._cow(b)
+        n = b.n_reqs
+        g = self._graphs.get(n)
+        if g is None:
+            g = _DecodeGraph(self, n)
+            self._graphs[n] = g
+        return g.run(b)
+
+
+class _DecodeGraph:
+    """Static buffers and the captured decode forward of one batch size."""
+
+    def __init__(self, model: QwenPagedModel, n: int):
+        dev = model.dev
+        self.model, self.n = model, n
+        self.ids = torch.zeros(n, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.kv_indptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+        self.kv_indices = torch.zeros(max(model.pool.num_pages, 1), dtype=torch.int32, device=dev)
+        self.seq_lens = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.last = torch.arange(n, dtype=torch.int64, device=dev)
+        self.meta = {"tp": 0, "kv_indices": self.kv_indices, "kv_d": self.kv_indptr, "len_d": self.seq_lens,
+                     "ws": paged.DecodeWorkspace.for_shape(model.pool, n, model.s.hq)}
+        self.graph = None
+        self.out = None
+
+    def _fill(self, b) -> None:
+        nk = int(b.kv_indptr[-1])
+        if nk > self.kv_indices.numel():
+            raise ValueError("decode batch lists more pages than the pool holds")
+        self.ids.copy_(torch.from_numpy(b.input_ids.astype(np.int64)))
+        self.pos.copy_(torch.from_numpy(np.ascontiguousarray(b.position_ids, np.int32)))
+        self.kv_indptr.copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indptr, np.int32)))
+        self.kv_indices[:nk].copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indices[:nk], np.int32)))
+        self.seq_lens.copy_(torch.from_numpy(np.ascontiguousarray(b.seq_lens, np.int32)))
+
+    def run(self, b) -> torch.Tensor:
+        self._fill(b)
+        if self.graph is not None:
+            self.graph.replay()
+            return self.out
+        # First batch of this size: run it eagerly on a side stream (its result
+        # is this step's), then capture the same launches (capture does not run them).
+        m = self.model
+        side = torch.cuda.Stream(device=m.dev)
+        side.wait_stream(torch.cuda.current_stream(m.dev))
+        with torch.cuda.stream(side):
+            res = m._forward_rows(self.ids, self.pos, self.meta, self.last)
+        torch.cuda.current_stream(m.dev).wait_stream(side)
+        torch.cuda.synchronize(m.dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = m._forward_rows(self.ids, self.pos, self.meta, self.last)
+        return res
 
 
 class Engine:
@@ -196,8 +278,9 @@ class Engine:
     backend error aborts every request of the batch (engine_loop.rs:47-57).
     """
 
-    def __init__(self, model: QwenPagedModel, sched):
+    def __init__(self, model: QwenPagedModel, sched, cuda_graphs: bool = True):
         self.model, self.sched = model, sched
+        self.cuda_graphs = cuda_graphs
         self.iterations = 0
 
     def step(self) -> bool:
@@ -205,7 +288,7 @@ class Engine:
         if b is None:
             return False
         try:
-            logits = self.model.forward(b)
+            logits = self.model.decode_step(b) if self.cuda_graphs else self.model.forward(b)
             tokens = paged.argmax_rows(logits).cpu().numpy().astype(np.uint32)
         except (L.MittenError, RuntimeError):
             self.sched.abort_batch()
