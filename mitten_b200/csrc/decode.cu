@@ -27,7 +27,8 @@
 //              segment epilogues.
 //   warp 4     producer: per segment the Q^T operand, per tile one TMA box
 //              per page per 64-wide head-dim block straight from the block
-//              table into a STAGES-deep ring, and the fused KV append.
+//              table into a 3-stage ring (at head_dim 256: a 6-slot ring of
+//              head-dim halves, 1.5 tiles), and the fused KV append.
 //   warp 5     MMA issuer (one thread); S^T double-buffered in TMEM so the
 //              next tile's QK^T overlaps this tile's softmax; O^T
 //              double-buffered per segment so an epilogue overlaps the next

@@ -8,16 +8,18 @@
 // q head h reading kv head h / n_rep (model.rs:398-408).
 //
 // CTA = (128-row query tile, query head, sequence); 6 warps in 3 roles:
-//   warps 0-3  softmax: one TMEM lane (= one query row) per thread; online
-//              softmax in the exp2 domain against a per-row reference max
-//              that moves only when a tile exceeds it by 2^8 (so the TMEM O
-//              accumulator is rarely rescaled), bf16 P written to shared
-//              memory in the 128B-swizzled K-major layout (double-buffered),
-//              final normalisation and store.
-//   warp 4     TMA producer: Q tile once, then K and V pages of each KV tile
-//              (one 4-D box per page covers every head-dim block) into a
-//              2-stage ring with separate K and V barriers; pages come
-//              straight from the block table.
+//   warps 0-3  softmax: one TMEM lane (= one query row) per thread.  They
+//              first write the Q tile into TMEM as bf16 pairs (both
+//              contractions take their M x K operand from TMEM, so the tensor
+//              core reads only K and V from shared memory), then per KV tile:
+//              online softmax in the exp2 domain against a per-row reference
+//              max that moves only when a tile exceeds it by 2^8 (so the TMEM
+//              O accumulator is rarely rescaled), and P written as bf16 pairs
+//              over the first half of the tile's S columns; finally O / l.
+//   warp 4     TMA producer: K and V pages of each KV tile (one 4-D box per
+//              page covers every head-dim block) into a 3-stage ring with
+//              separate K and V barriers; page ids fetched by the whole warp
+//              one 32-page window ahead, straight from the block table.
 //   warp 5     MMA issuer (one thread): S = Q K^T and O += P V with
 //              tcgen05.mma (M=128, kind::f16, f32 accumulators in TMEM),
 //              completion signalled with tcgen05.commit on mbarriers.  S is
