@@ -412,7 +412,11 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     // Stage slot st of round i0 is tile i0 + st: unrolled so the ring
     // registers are indexed with constants.
     for (int i0 = 0; run && i0 < n_local; i0 += C::kStages) {
-#pragma unroll
+      // At two CTAs per SM (head_dim 64) the loop body is kept rolled: the
+      // smaller code measured faster there (32.2 vs 33.2 us per config-2
+      // step), while the unrolled body with register-resident ring slots is
+      // faster at head_dim 128 (config 5: 0.80 vs 0.74 of HBM).
+#pragma unroll (C::kCtasPerSm > 1 ? 1 : C::kStages)
       for (int st = 0; st < C::kStages; ++st) {
         const int i = i0 + st;
         if (!run || i >= n_local) break;
