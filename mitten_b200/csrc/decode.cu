@@ -611,30 +611,20 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       bool ok = true;
       int next_s = 0;  // next tile whose S^T is not issued yet
       for (int i = 0; ok && i < n_local; ++i) {
-        while (ok && next_s <= i) {
-          ok = issue_s(next_s);
-          ++next_s;
-        }
-        if (!ok) break;
-        const bool first = (i == 0) || wo.j == 0;
-        if (first) {
-          ++o_seg;
-          if (o_seg >= 2 &&
-              !tc::wait_bounded(&bars[kOFree0 + (o_seg & 1)], ((o_seg >> 1) - 1) & 1, abort_flag, p.err, 23))
-            break;
-        }
-        // Wait for P^T(i); meanwhile issue S^T(i+1) as soon as its K/V land
-        // (its S buffer was released by the softmax of tile i-1, whose P^T
-        // was waited on in the previous iteration).
+        // Issue S^T(i) if it is not out yet (waiting for its K/V), then wait
+        // for P^T(i), issuing S^T(i+1) as soon as its K/V land (its S buffer
+        // was released by the softmax of tile i-1, whose P^T was waited on in
+        // the previous iteration).  One call site keeps the loop's code small.
         {
           uint64_t* pf = &bars[kPFull0 + (i & 1)];
           const uint32_t par = (i >> 1) & 1;
           uint64_t t_start = 0;
           for (uint32_t it = 0;; ++it) {
-            if (next_s == i + 1 && next_s < n_local && s_ready(next_s)) {
+            if (next_s <= i || (next_s == i + 1 && next_s < n_local && s_ready(next_s))) {
               ok = issue_s(next_s);
               ++next_s;
               if (!ok) break;
+              continue;
             }
             if (mbar_test_wait(pf, par)) break;
             // Back off between polls: this warp shares a scheduler with a
@@ -656,6 +646,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             }
           }
           if (!ok) break;
+        }
+        const bool first = (i == 0) || wo.j == 0;
+        if (first) {
+          ++o_seg;
+          if (o_seg >= 2 &&
+              !tc::wait_bounded(&bars[kOFree0 + (o_seg & 1)], ((o_seg >> 1) - 1) & 1, abort_flag, p.err, 23))
+            break;
         }
         const uint64_t b0 = dP + (((i & 1) * C::kPBytes) >> 4);
         const uint32_t o_col = C::kTmemO + (o_seg & 1) * 32;
