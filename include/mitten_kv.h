@@ -204,7 +204,14 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
  *   LAST q_len = qo_indptr[r+1]-qo_indptr[r] tokens out of seq_lens[r]
  *   (their K/V already appended), so query i sits at position
  *   seq_lens[r] - q_len + i and sees keys at positions <= its own
- *   (generate_causal_mask, model.rs:542-555). */
+ *   (generate_causal_mask, model.rs:542-555).
+ *   workspace: launches with few (query tile, head) units (at most 3/4 of
+ *   the SM count, counted as (total_q / 128 + n_seqs) x num_q_heads) cut
+ *   long units into up to 4 pieces of kv tiles on separate CTAs and merge
+ *   them; that takes mtn_paged_prefill_workspace_bytes(...) bytes (0 above
+ *   296 units), 256-byte aligned, zeroed once before first use and left
+ *   zeroed by every call, one stream at a time.  With no or a smaller
+ *   workspace the launch runs unsplit. */
 MTN_API size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                                          int32_t num_kv_heads, int32_t head_dim);
 MTN_API int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer,

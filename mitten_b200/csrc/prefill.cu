@@ -57,7 +57,24 @@ struct PrefillParams {
   float qscale;
   int phantom;
   int* err;
+  // Split of long units, for launches with few units: a (query tile, head,
+  // sequence) unit is cut into k <= kMaxPieces pieces of consecutive kv
+  // tiles, run by CTAs blockIdx.z = piece * n_seqs + sequence (pieces in the
+  // slowest grid dimension, so every unit's first piece is dispatched before
+  // any other).  Each piece leaves (O, m, l) in its workspace slot; the last
+  // to arrive merges them.
+  int split;
+  int split_target;       // CTAs one wave holds (the SM count)
+  int n_seqs;
+  int64_t max_units;      // workspace units (unit index bound)
+  float* ws_o;            // [units * kMaxPieces][D / 32][8][128 rows][4]
+  float* ws_ml;           // [units * kMaxPieces][2][128 rows]: m, l
+  unsigned int* ws_cnt;   // [units] arrival counters, left at zero
 };
+
+constexpr int kMaxPieces = 4;
+constexpr int kMinPiece = 8;        // kv tiles
+constexpr int kSplitMaxUnits = 296; // launches with more units run unsplit
 
 // P is exponentiated against a per-row reference max that moves only when a
 // tile's max exceeds it by more than 2^8, so P <= 256 and O is rarely rescaled.
@@ -97,6 +114,34 @@ enum Bar {
   kNumBars = 19
 };
 
+// Piece length of the split, the same value in every CTA of the launch: the
+// launch's units (query tile, head) and their kv tiles T, each unit's tiles
+// being (last visible position / kBN) + 1; with U units on S SMs a piece
+// length of T / (S - U) keeps every piece in one wave (sum of
+// ceil(n / plen) < T / plen + U <= S).  0 when the units fill the SMs.
+__device__ __forceinline__ int64_t split_piece_len(const PrefillParams& p, int bn, int lane) {
+  int64_t t = 0, u = 0;
+  for (int s = lane; s < p.n_seqs; s += 32) {
+    const int q0 = p.qo_indptr[s];
+    const int ql = p.qo_indptr[s + 1] - q0;
+    if (ql <= 0) continue;
+    const int64_t kl = max(static_cast<int64_t>(p.seq_lens[s]), static_cast<int64_t>(ql));
+    for (int qt = 0; qt * kBM < ql; ++qt) {
+      t += (kl - ql + min(ql, (qt + 1) * kBM) - 1) / bn + 1;
+      ++u;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    t += __shfl_xor_sync(0xffffffffu, t, o);
+    u += __shfl_xor_sync(0xffffffffu, u, o);
+  }
+  t *= p.hq;
+  u *= p.hq;
+  if (u >= p.split_target) return 0;
+  return max(static_cast<int64_t>(kMinPiece), (t + (p.split_target - u) - 1) / (p.split_target - u));
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PrefillParams p) {
@@ -110,15 +155,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-  const int q0 = p.qo_indptr[s];
-  const int q_len = p.qo_indptr[s + 1] - q0;
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int piece = p.split ? static_cast<int>(blockIdx.z) / p.n_seqs : 0;
+  const int s = static_cast<int>(blockIdx.z) - piece * p.n_seqs;
+  // With the split on, the MMA warp (idle until the pipeline starts) computes
+  // the launch's piece length while the other warps load this unit's
+  // metadata, so the two global round trips overlap.
+  int64_t* plen_s = reinterpret_cast<int64_t*>(smem + C::kOffMisc + 16);
+  const bool scan_warp = p.split && warp == 5;
+  if (scan_warp) {
+    const int64_t pl = split_piece_len(p, C::kBN, lane);
+    if (lane == 0) *plen_s = pl;
+  }
+  int q0 = 0, q_len = 0, kv_beg = 0, npages = 0, kv_len = 0;
+  auto load_meta = [&]() {
+    q0 = p.qo_indptr[s];
+    q_len = p.qo_indptr[s + 1] - q0;
+    kv_beg = p.kv_indptr[s];
+    npages = p.kv_indptr[s + 1] - kv_beg;
+    kv_len = p.seq_lens[s];
+  };
+  if (!scan_warp) load_meta();
+  if (p.split) __syncthreads();
+  if (scan_warp) load_meta();
   if (tile * kBM >= q_len) return;
-  const int kv_beg = p.kv_indptr[s];
-  const int npages = p.kv_indptr[s + 1] - kv_beg;
-  int kv_len = p.seq_lens[s];
   if (kv_len < q_len || kv_len > npages * p.ps) {
-    if (tile == 0 && h == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
+    if (tile == 0 && h == 0 && piece == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
     kv_len = max(q_len, min(kv_len, npages * p.ps));
     if (kv_len > npages * p.ps) return;  // not even the chunk fits its pages
   }
@@ -128,6 +190,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = last_pos / C::kBN + 1;
   const int g = h / (p.hq / p.hkv);
   const int pages_per_tile = C::kBN / p.ps;
+  // Unit index for the split's workspace: q0 / 128 + s + tile is distinct
+  // per (sequence, query tile) and below total_q / 128 + n_seqs.
+  const int64_t uid = (static_cast<int64_t>(q0 / kBM) + s + tile) * p.hq + h;
+  int k = 1;  // pieces of this unit
+  if (p.split && uid < p.max_units) {
+    const int64_t plen = *plen_s;
+    if (plen > 0) k = static_cast<int>(min(static_cast<int64_t>(kMaxPieces), (n_tiles + plen - 1) / plen));
+  }
+  if (piece >= k) return;
+  const int ja = piece * n_tiles / k;  // this CTA's kv tiles [ja, jb)
+  const int jb = (piece + 1) * n_tiles / k;
+  const int nt = jb - ja;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
@@ -154,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // fetched by the whole warp, 32 at a time and one window ahead, so no
     // load of the block table sits on the issue path; lane 0 issues.
     const int ppt = pages_per_tile;
-    const int lim = min(npages, n_tiles * ppt) - 1;  // last page the CTA reads
+    const int pb = ja * ppt;                    // first page of the range
+    const int lim = min(npages, jb * ppt) - 1;  // last page the CTA reads
     auto fetch = [&](int first) -> int { return p.kv_indices[kv_beg + min(first + lane, lim)]; };
     auto to_row = [&](int page) -> int {  // first pool row / 8 of this kv head's slice of the page (K)
       if (page < 0 || page >= p.num_pages) {
@@ -166,15 +241,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) tc::prefetch_tmap(&tm_kv);
     const int page_bytes = p.ps * D * 2;
     const int dv = static_cast<int>((p.row_v - p.row_k) >> 3);
-    int cur = to_row(fetch(0));
-    int nxt = fetch(32);
-    for (int j = 0; j < n_tiles; ++j) {
+    int cur = to_row(fetch(pb));
+    int nxt = fetch(pb + 32);
+    for (int j = 0; j < nt; ++j) {  // j counts the range's tiles
       const int st = j % kS;
       const uint32_t par = ((j / kS) - 1) & 1;  // phase of the use kStages tiles back
-      const int first = j * ppt;
+      const int first = j * ppt;                 // page offset inside the range
       if (j > 0 && (first & 31) == 0) {
         cur = to_row(nxt);
-        nxt = fetch(first + 32);
+        nxt = fetch(pb + first + 32);
       }
       bool ok = true;
       if (lane == 0 && j >= kS) ok = tc::wait_bounded(&bars[kKEmpty0 + st], par, abort_flag, p.err, 10);
@@ -227,8 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = tc::wait_bounded(&bars[kQReady], 0, abort_flag, p.err, 20);
       if (ok) tc::fence_after_sync();
       ok = ok && issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+      for (int j = 0; ok && j < nt; ++j) {  // j counts the range's tiles
+        if (j + 1 < nt && !issue_s(j + 1)) break;
         const int st = j % kS;
         if (!tc::wait_bounded(&bars[kPFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 22)) break;
         if (!tc::wait_bounded(&bars[kVFull0 + st], (j / kS) & 1, abort_flag, p.err, 23)) break;
@@ -275,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < nt; ++j) {  // j counts the range's tiles
       ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
       if (!__all_sync(0xffffffffu, ok)) break;  // TMEM loads below are warp-collective
       tc::fence_after_sync();
@@ -289,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::kBN; ++c) sv[c] = __uint_as_float(r[c >> 5][c & 31]);
       }
-      const int key0 = j * C::kBN;
+      const int key0 = (ja + j) * C::kBN;
       if (key0 + C::kBN - 1 > pos0) {  // diagonal tile: keys after a row's position are masked
 #pragma unroll
         for (int c = 0; c < C::kBN; ++c) sv[c] = (key0 + c <= row_pos) ? sv[c] : -INFINITY;
@@ -304,7 +379,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
           p.qscale;
       // Lazy rescale, per row: the reference max moves only when this tile
-      // exceeds it by 2^8 (tile 0 always sets it: key 0 is visible to every row).
+      // exceeds it by 2^8.  Tile 0 always sets it (key 0 is visible to every
+      // row); in the second half of a cut unit a row may see no key yet, and
+      // its m_ref stays -inf with P = 0.
       float alpha = 1.0f;
       bool moved = false;
       if (m_ref == -INFINITY) {
@@ -314,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = mt;
         moved = true;
       }
-      const float neg_m = -m_ref;
+      const float neg_m = m_ref == -INFINITY ? 0.0f : -m_ref;
       float ps8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps8[i] = 0.0f;
@@ -353,43 +430,126 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_arrive(&bars[kPFull0 + (j & 1)]);
     }
     // ---- epilogue: O / l (phantom key folded in), one row per thread.
-    if (ok) ok = tc::wait_bounded(&bars[kODone0 + ((n_tiles - 1) & 1)], ((n_tiles - 1) >> 1) & 1, abort_flag, p.err, 32);
+    if (ok) ok = tc::wait_bounded(&bars[kODone0 + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, abort_flag, p.err, 32);
     tc::fence_after_sync();
-    if (__all_sync(0xffffffffu, ok)) {
-      float l = l_run, a = 1.0f;
+    const bool valid = row < nrows;
+    const int64_t orow = (static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h;
+    auto store_chunk = [&](int c, const float* v, float inv) {
+      if (!valid) return;
+      if (p.o_f32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * D + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 w;
+          w.x = f2_to_bf2(v[8 * i + 0] * inv, v[8 * i + 1] * inv);
+          w.y = f2_to_bf2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
+          w.z = f2_to_bf2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
+          w.w = f2_to_bf2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
+          dst[i] = w;
+        }
+      }
+    };
+    // 1 / l scaled for the phantom zero key (score 0), given the row's max m.
+    auto finish = [&](float m, float l) -> float {
+      float a = 1.0f;
       if (p.phantom) {
-        const float mf = fmaxf(m_ref, 0.0f);
-        a = exp2f(m_ref - mf);
+        const float mf = fmaxf(m, 0.0f);
+        a = m == -INFINITY ? 0.0f : exp2f(m - mf);
         l = l * a + exp2f(-mf);
       }
-      const float inv = l > 0.0f ? a / l : 0.0f;
-      const bool valid = row < nrows;
-      const int64_t orow = (static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h;
+      return l > 0.0f ? a / l : 0.0f;
+    };
+    // Every softmax thread takes the same branch (k is per CTA; a failed
+    // wait anywhere skips the merge's barriers in all four warps).
+    const bool all_ok = !tc::named_sync_or(1, kBM, !ok);
+    if (all_ok && k == 1) {
+      const float inv = finish(m_ref, l_run);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
         tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
         tc::tmem_ld_wait();
-        if (valid) {
-          if (p.o_f32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * D + c * 32);
+        store_chunk(c, reinterpret_cast<const float*>(r), inv);
+      }
+    } else if (all_ok) {
+      // This piece's partial (O unnormalised, m, l), then a ticket; the last
+      // piece to arrive merges all k in piece order.  Partials are laid out
+      // [chunk][float4][row] so a warp's accesses are contiguous.
+      const int64_t base = uid * kMaxPieces;
+      float4* wo = reinterpret_cast<float4*>(p.ws_o);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
+        tc::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
-                                   __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * D + c * 32);
+        for (int i = 0; i < 8; ++i)
+          wo[(((base + piece) * (D / 32) + c) * 8 + i) * kBM + row] =
+              make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                          __uint_as_float(r[4 * i + 3]));
+      }
+      p.ws_ml[((base + piece) * 2) * kBM + row] = m_ref;
+      p.ws_ml[((base + piece) * 2 + 1) * kBM + row] = l_run;
+      __threadfence();
+      volatile int* last_s = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
+      tc::named_sync(1, kBM);
+      if (row == 0) *last_s = atomicAdd(&p.ws_cnt[uid], 1u) == static_cast<unsigned int>(k - 1) ? 1 : 0;
+      tc::named_sync(1, kBM);
+      if (*last_s) {
+        __threadfence();
+        float mi[kMaxPieces], li[kMaxPieces];
+        float M = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = f2_to_bf2(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
-              w.y = f2_to_bf2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
-              w.z = f2_to_bf2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
-              w.w = f2_to_bf2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
-              dst[i] = w;
+        for (int i = 0; i < kMaxPieces; ++i) {
+          mi[i] = -INFINITY;
+          li[i] = 0.0f;
+          if (i < k) {
+            mi[i] = i == piece ? m_ref : __ldcg(&p.ws_ml[((base + i) * 2) * kBM + row]);
+            li[i] = i == piece ? l_run : __ldcg(&p.ws_ml[((base + i) * 2 + 1) * kBM + row]);
+          }
+          M = fmaxf(M, mi[i]);
+        }
+        float L = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMaxPieces; ++i) {
+          mi[i] = mi[i] == -INFINITY ? 0.0f : exp2f(mi[i] - M);  // now the piece's weight
+          L += li[i] * mi[i];
+        }
+        const float inv = finish(M, L);
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
+          tc::tmem_ld_wait();
+          float acc[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
+#pragma unroll
+          for (int i = 0; i < kMaxPieces; ++i) {
+            const float a = mi[i];
+            if (i >= k) {
+            } else if (i == piece) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) acc[e] = fmaf(__uint_as_float(r[e]), a, acc[e]);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 v = __ldcg(&wo[(((base + i) * (D / 32) + c) * 8 + q) * kBM + row]);
+                acc[4 * q] = fmaf(v.x, a, acc[4 * q]);
+                acc[4 * q + 1] = fmaf(v.y, a, acc[4 * q + 1]);
+                acc[4 * q + 2] = fmaf(v.z, a, acc[4 * q + 2]);
+                acc[4 * q + 3] = fmaf(v.w, a, acc[4 * q + 3]);
+              }
             }
           }
+          store_chunk(c, acc, inv);
         }
+        if (row == 0) p.ws_cnt[uid] = 0u;  // ready for the next call on this workspace
       }
     }
   }
@@ -416,9 +576,29 @@ int launch_prefill(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles
                  "cudaFuncSetAttribute(prefill)");
     configured[dev] = true;
   }
-  dim3 grid(n_tiles, prm.hq, n_seqs);
+  dim3 grid(n_tiles, prm.hq, prm.split ? n_seqs * kMaxPieces : n_seqs);
   paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
   return check_launch("paged_prefill_kernel");
+}
+
+// Workspace of the split: counters, then (m, l) rows, then O partials.
+struct SplitLayout {
+  int64_t units = 0;
+  size_t off_ml = 0, off_o = 0, bytes = 0;
+};
+
+SplitLayout split_layout(int32_t n_seqs, int64_t total_q, int32_t num_q_heads, int32_t head_dim) {
+  SplitLayout w;
+  if (n_seqs <= 0 || total_q <= 0 || num_q_heads <= 0 || head_dim <= 0) return w;
+  const int64_t units = (total_q / kBM + n_seqs) * num_q_heads;
+  if (units > kSplitMaxUnits) return w;  // enough units to fill the GPU: no split
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t slots = static_cast<size_t>(units) * kMaxPieces;
+  w.units = units;
+  w.off_ml = up(static_cast<size_t>(units) * 4);
+  w.off_o = w.off_ml + up(slots * 2 * kBM * 4);
+  w.bytes = w.off_o + slots * kBM * static_cast<size_t>(head_dim) * 4;
+  return w;
 }
 
 }  // namespace
@@ -430,16 +610,14 @@ extern "C" {
 
 size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads, int32_t num_kv_heads,
                                          int32_t head_dim) {
-  (void)n_seqs; (void)total_q; (void)num_q_heads; (void)num_kv_heads; (void)head_dim;
-  return 0;  // the prefill kernel keeps all state on chip
+  (void)num_kv_heads;
+  return mtn::split_layout(n_seqs, total_q, num_q_heads, head_dim).bytes;
 }
 
 int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, void* o, int32_t o_dtype,
                       int32_t n_seqs, int64_t total_q, int32_t num_q_heads, const int32_t* qo_indptr,
                       const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens, int32_t max_q_len,
                       float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int st = mtn::validate_layout(pool, layer, "mtn_paged_prefill");
   if (st != MTN_OK) return st;
   MTN_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65535, "mtn_paged_prefill: n_seqs %d outside [0, 65535]", n_seqs);
@@ -479,6 +657,21 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
   prm.err = mtn::device_error_ptr();
   const int n_tiles = (max_q_len + mtn::kBM - 1) / mtn::kBM;
   MTN_CHECK_ARG(n_tiles <= 65535 * 32, "mtn_paged_prefill: max_q_len too large");
+  // Launches whose units (bounded by (total_q / 128 + n_seqs) x heads) leave
+  // a quarter or more of the SMs idle split long units across more CTAs when
+  // the workspace is there; otherwise they run unsplit (same results).
+  const mtn::SplitLayout wl = mtn::split_layout(n_seqs, total_q, num_q_heads, D);
+  if (wl.bytes > 0 && wl.units * 4 <= 3 * static_cast<int64_t>(mtn::sm_count()) && workspace != nullptr &&
+      workspace_bytes >= wl.bytes && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    prm.split = 1;
+    prm.split_target = mtn::sm_count();
+    prm.n_seqs = n_seqs;
+    prm.max_units = wl.units;
+    prm.ws_cnt = reinterpret_cast<unsigned int*>(w);
+    prm.ws_ml = reinterpret_cast<float*>(w + wl.off_ml);
+    prm.ws_o = reinterpret_cast<float*>(w + wl.off_o);
+  }
   auto s = static_cast<cudaStream_t>(stream);
   switch (D) {
     case 64: return mtn::launch_prefill<64>(tkv, prm, n_tiles, n_seqs, s);

@@ -89,6 +89,7 @@ class QwenPagedModel:
         self.scale = shape.head_dim ** -0.5
         self._ws = None
         self._ws_seqs = 0
+        self._pws = None
         self._graphs: dict[int, _DecodeGraph] = {}
 
     # ------------------------------------------------------------ pieces
@@ -106,6 +107,15 @@ class QwenPagedModel:
         if rd < x.shape[-1]:
             out = torch.cat([out, x[..., rd:]], dim=-1)
         return out
+
+    def _prefill_ws(self, n: int, total_q: int) -> torch.Tensor | None:
+        """Split workspace for mtn_paged_prefill (zeroed once, grown on demand; None when not used)."""
+        nb = paged.L.lib().mtn_paged_prefill_workspace_bytes(n, total_q, self.s.hq, self.s.hkv, self.s.head_dim)
+        if nb == 0:
+            return None
+        if self._pws is None or self._pws.numel() < nb:
+            self._pws = torch.zeros(nb, dtype=torch.uint8, device=self.dev)
+        return self._pws
 
     def _decode_ws(self, n: int) -> paged.DecodeWorkspace:
         if self._ws is None or n > self._ws_seqs:
@@ -142,7 +152,7 @@ class QwenPagedModel:
             self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
             paged.paged_prefill(self.pool, li, q[:tp].to(torch.bfloat16).contiguous(), meta["qo_p"], meta["kv_p"],
                                 meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=s.phantom,
-                                out=attn[:tp])
+                                out=attn[:tp], workspace=meta["pws"])
         if T > tp:
             paged.paged_decode(self.pool, li, q[tp:].contiguous(), meta["kv_d"], meta["kv_indices"], meta["len_d"],
                                scale=self.scale, phantom=s.phantom, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
@@ -165,6 +175,7 @@ class QwenPagedModel:
             meta["kv_p"] = torch.from_numpy(np.ascontiguousarray(b.kv_indptr[:npf + 1], np.int32)).to(dev)
             meta["len_p"] = torch.from_numpy(np.ascontiguousarray(b.seq_lens[:npf], np.int32)).to(dev)
             meta["max_q"] = int(np.max(np.diff(qo[:npf + 1])))
+            meta["pws"] = self._prefill_ws(npf, tp)
             pos_p = torch.from_numpy(np.ascontiguousarray(b.position_ids[:tp], np.int32)).to(dev)
             meta["slots"] = paged.build_slot_mapping(meta["qo_p"], pos_p, meta["kv_p"], meta["kv_indices"],
                                                      self.pool.page_size)

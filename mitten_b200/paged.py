@@ -177,7 +177,13 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
                   scale: float | None = None, phantom: bool = False, out: torch.Tensor | None = None,
                   out_dtype: torch.dtype = torch.bfloat16, workspace: torch.Tensor | None = None,
                   stream=None) -> torch.Tensor:
-    """Chunked-prefill attention for q [total_q, num_q_heads, head_dim] (bf16) over the paged cache."""
+    """Chunked-prefill attention for q [total_q, num_q_heads, head_dim] (bf16) over the paged cache.
+
+    Launches with few (query tile, head) units cut long ones into pieces over
+    more CTAs; that needs `workspace` (mtn_paged_prefill_workspace_bytes,
+    zeroed once, reusable, one stream at a time).  A fresh zeroed one is made
+    when none is given; a smaller one runs the launch unsplit.
+    """
     if q.dim() != 3 or not q.is_contiguous() or q.dtype != torch.bfloat16:
         raise ValueError("q must be a contiguous bf16 [total_q, heads, head_dim] tensor")
     tq, hq, d = q.shape

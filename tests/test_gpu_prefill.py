@@ -22,15 +22,16 @@ TOL_SPEC = 2e-2
 TOL_KERNEL = 1e-2
 
 
-def run_prefill(kv_lens, q_lens, hq, hkv, d, phantom=True, seed=0, out_dtype=torch.float32, page_size=16):
-    case = make_case(kv_lens, hkv, d, page_size=page_size, seed=seed)
+def run_prefill(kv_lens, q_lens, hq, hkv, d, phantom=True, seed=0, out_dtype=torch.float32, page_size=16,
+                workspace=None, case=None):
+    case = case or make_case(kv_lens, hkv, d, page_size=page_size, seed=seed)
     rng = np.random.default_rng(seed + 100)
     total_q = sum(q_lens)
     q = rng.standard_normal((total_q, hq, d)).astype(np.float32)
     qt = torch.from_numpy(q).to("cuda").to(torch.bfloat16)
     qo = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32), device="cuda")
     out = paged.paged_prefill(case.pool, 0, qt, qo, case.kv_indptr, case.kv_indices, case.seq_lens,
-                              max(q_lens), phantom=phantom, out_dtype=out_dtype)
+                              max(q_lens), phantom=phantom, out_dtype=out_dtype, workspace=workspace)
     torch.cuda.synchronize()
     return case, q, qt.float().cpu().numpy(), out.float().cpu().numpy()
 
@@ -86,3 +87,32 @@ def test_prefill_empty_chunk_rows(cuda_device):
     kv_lens, q_lens = [10, 50, 20], [0, 50, 0]
     case, q, qu, out = run_prefill(kv_lens, q_lens, 14, 2, 64, seed=3)
     check(case, q_lens, q, qu, out, 64)
+
+
+@pytest.mark.parametrize("hq,hkv,d,kv_lens,q_lens", [
+    (8, 1, 256, [8192], [512]),                      # one long chunk: every unit cut in 4
+    (2, 1, 256, [6144, 2560, 2048, 8192], [512] * 4),  # 2, 2, 4 and 4 pieces
+    (14, 2, 128, [5000, 300], [256, 300]),
+    (14, 2, 64, [9000], [200]),
+])
+def test_prefill_split_long_units(cuda_device, hq, hkv, d, kv_lens, q_lens):
+    """Few units, long contexts: pieces of kv tiles on separate CTAs, merged in
+    piece order; matches the oracle, the unsplit launch (a workspace too small
+    to split) within tolerance, and itself bit for bit on a reused workspace."""
+    from mitten_b200 import _lib as L
+    nb = L.lib().mtn_paged_prefill_workspace_bytes(len(q_lens), sum(q_lens), hq, hkv, d)
+    assert nb > 0
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    case, q, qu, out = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=d + hq, workspace=ws)
+    check(case, q_lens, q, qu, out, d)
+    _, _, _, again = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=d + hq, workspace=ws, case=case)
+    assert np.array_equal(out, again)
+    units = (sum(q_lens) // 128 + len(q_lens)) * hq
+    off = (units * 4 + 255) // 256 * 256
+    assert int(ws[:off].count_nonzero()) == 0  # arrival counters left at zero
+    assert int(ws[off:].count_nonzero()) > 0  # partials were written: the split ran
+    small = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    _, _, _, unsplit = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=d + hq, workspace=small, case=case)
+    check(case, q_lens, q, qu, unsplit, d)
+    assert float(np.abs(out - unsplit).max()) <= 1e-3
+    assert paged.device_error(0) == (0, 0)
