@@ -946,19 +946,25 @@ def run_cfg5_prefill(args, dev, stream) -> dict:
     qp = torch.randn((n_pf * chunk, hq, d), generator=gen, device=dev).to(torch.bfloat16)
     op = torch.empty((n_pf * chunk, hq, d), dtype=torch.bfloat16, device=dev)
 
-    def pre():
+    def pre():  # two query tiles per CTA (the default at these shapes)
         paged.paged_prefill(pool, 0, qp, qo, p_indptr, p_indices, p_lens, chunk, out=op)
+
+    def pre1():  # the one-tile kernel on the same inputs, for comparison
+        paged.paged_prefill(pool, 0, qp, qo, p_indptr, p_indices, p_lens, chunk, out=op, one_tile=True)
 
     for _ in range(args.warmup):
         pre()
+        pre1()
     steps = max(3, min(args.steps, 10))
     t = _graph_steps([pre] * steps, stream)
+    t1 = _graph_steps([pre1] * steps, stream)
     flops = sum(4.0 * hq * d * chunk * (int(P) + (chunk + 1) / 2) for P in pp)
     peak = load_peaks()["bf16_tflops"]
     tf = flops / (t / steps) / 1e12
     return {"workload": "16 chunks of 512 after prior U{0,512..15872} seed 14, Hq 28 / Hkv 4 / D 128, page 16",
+            "kernel": "paged_prefill_pair_kernel<128> (two query tiles per CTA)",
             "us_per_step": 1e6 * t / steps, "tflops": tf, "frac": tf / peak, "peak_tflops": peak,
-            "launches": steps}
+            "launches": steps, "one_tile_us_per_step": 1e6 * t1 / steps}
 
 
 def load_peaks() -> dict:

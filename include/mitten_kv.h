@@ -112,7 +112,11 @@ enum {
 enum {
   /* Add the reference's all-zero first K/V row (qwen model.rs:207-220) to
    * every softmax: one key with score 0 and a zero value. */
-  MTN_ATTN_PHANTOM_ZERO_SLOT = 1u << 0
+  MTN_ATTN_PHANTOM_ZERO_SLOT = 1u << 0,
+  /* mtn_paged_prefill only: run the one-query-tile kernel even where the
+   * two-tile kernel applies (head_dim <= 128 and at least two query tiles
+   * per SM); same results, for comparison. */
+  MTN_ATTN_PREFILL_ONE_TILE = 1u << 1
 };
 
 /* Per-token pool slot for a batch (Batch -> slot map; batch.rs:7-36):

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmitten_kv.so"
 MTN_OK, MTN_EINVAL, MTN_ENOMEM, MTN_ECUDA, MTN_ETIMEOUT, MTN_EDEVICE = range(6)
 MTN_DTYPE_BF16, MTN_DTYPE_F32 = 0, 1
 MTN_ATTN_PHANTOM_ZERO_SLOT = 1
+MTN_ATTN_PREFILL_ONE_TILE = 2
 MTN_SCHED_REFERENCE, MTN_SCHED_REFCOUNT = 0, 1
 MTN_REQ_WAITING, MTN_REQ_PREFILLING, MTN_REQ_DECODING, MTN_REQ_DONE, MTN_REQ_ABORTED = range(5)
 MTN_PHASE_PREFILL_ONLY, MTN_PHASE_DECODE_ONLY, MTN_PHASE_MIXED = range(3)

@@ -142,6 +142,131 @@ __device__ __forceinline__ int64_t split_piece_len(const PrefillParams& p, int b
   return max(static_cast<int64_t>(kMinPiece), (t + (p.split_target - u) - 1) / (p.split_target - u));
 }
 
+// 1 / l for a row whose softmax has max m (log2 units) and sum l, with the
+// phantom zero key (score 0, value 0) folded in when `phantom` is set; the
+// returned factor also rescales O from m to the phantom-aware max.
+__device__ __forceinline__ float row_inv_sum(int phantom, float m, float l) {
+  float a = 1.0f;
+  if (phantom) {
+    const float mf = fmaxf(m, 0.0f);
+    a = m == -INFINITY ? 0.0f : exp2f(m - mf);
+    l = l * a + exp2f(-mf);
+  }
+  return l > 0.0f ? a / l : 0.0f;
+}
+
+// Store 32 consecutive head-dim values of one output row, scaled by inv.
+__device__ __forceinline__ void store_row_chunk(const PrefillParams& p, int64_t elem0, const float* v, float inv) {
+  if (p.o_f32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + elem0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      dst[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + elem0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 w;
+      w.x = f2_to_bf2(v[8 * i + 0] * inv, v[8 * i + 1] * inv);
+      w.y = f2_to_bf2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
+      w.z = f2_to_bf2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
+      w.w = f2_to_bf2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
+      dst[i] = w;
+    }
+  }
+}
+
+// One kv tile of the online softmax over a 128-row query tile, one row per
+// thread (warp w of the four reads TMEM lanes 32 (w % 4) ..): wait for S on
+// `sfull`, mask keys after the row's position on the diagonal tile, move the
+// row's reference max only when the tile exceeds it by 2^8 (then rescale O
+// in TMEM once the previous P V is done: `odone_prev`), write P as bf16
+// pairs over the first kBN / 2 columns of the S buffer and arrive on
+// `pfull`.  Returns false (every lane of the warp) when a wait gave up.
+template <int D, int kBN>
+__device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off, uint32_t o_off, int key0, int pos0,
+                                             int row_pos, float qscale, float& m_ref, float& l_run, uint64_t* sfull,
+                                             uint32_t s_par, uint64_t* odone_prev, uint32_t o_par, uint64_t* pfull,
+                                             volatile int* abort_flag, int* err, int where) {
+  bool ok = tc::wait_bounded(sfull, s_par, abort_flag, err, where);
+  if (!__all_sync(0xffffffffu, ok)) return false;  // TMEM loads below are warp-collective
+  tc::fence_after_sync();
+  const uint32_t s_col = lane_base + s_off;
+  float sv[kBN];
+  {
+    uint32_t r[kBN / 32][32];
+#pragma unroll
+    for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, r[c]);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < kBN; ++c) sv[c] = __uint_as_float(r[c >> 5][c & 31]);
+  }
+  if (key0 + kBN - 1 > pos0) {  // diagonal tile: keys after a row's position are masked
+#pragma unroll
+    for (int c = 0; c < kBN; ++c) sv[c] = (key0 + c <= row_pos) ? sv[c] : -INFINITY;
+  }
+  // Row max of the raw scores in 8 independent chains (scale > 0 commutes with max).
+  float mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+  for (int c = 8; c < kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+  const float mt =
+      fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * qscale;
+  // Lazy rescale, per row: the reference max moves only when this tile
+  // exceeds it by 2^8.  A row's first tile always sets it when the row sees
+  // a key there; a row that sees no key yet keeps m_ref = -inf with P = 0.
+  float alpha = 1.0f;
+  bool moved = false;
+  if (m_ref == -INFINITY) {
+    m_ref = mt;
+  } else if (mt > m_ref + kRescaleLog2) {
+    alpha = exp2f(m_ref - mt);
+    m_ref = mt;
+    moved = true;
+  }
+  const float neg_m = m_ref == -INFINITY ? 0.0f : -m_ref;
+  float ps8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ps8[i] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kBN; ++c) {
+    sv[c] = tc::ex2_approx(fmaf(sv[c], qscale, neg_m));  // masked keys: 2^-inf = 0
+    ps8[c & 7] += sv[c];
+  }
+  const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+  l_run = l_run * alpha + psum;
+  // P (bf16 pairs) over the first kBN/2 columns of this tile's S buffer.
+#pragma unroll
+  for (int c = 0; c < kBN / 64; ++c) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = f2_to_bf2(sv[c * 64 + 2 * i], sv[c * 64 + 2 * i + 1]);
+    tc::tmem_st32(s_col + c * 32, r);
+  }
+  tc::tmem_st_wait();
+  if (__any_sync(0xffffffffu, moved)) {
+    // O is current once P V of the previous tile finishes (P is stored
+    // first, so the 128 exponentials are no longer live here).
+    ok = tc::wait_bounded(odone_prev, o_par, abort_flag, err, where + 1);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    tc::fence_after_sync();
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      tc::tmem_ld32(lane_base + o_off + c * 32, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+      tc::tmem_st32(lane_base + o_off + c * 32, r);
+    }
+    tc::tmem_st_wait();
+  }
+  tc::fence_before_sync();
+  tc::mbar_arrive(pfull);
+  return true;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PrefillParams p) {
@@ -351,83 +476,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {  // j counts the range's tiles
-      ok = tc::wait_bounded(&bars[kSFull0 + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 30);
-      if (!__all_sync(0xffffffffu, ok)) break;  // TMEM loads below are warp-collective
-      tc::fence_after_sync();
-      const uint32_t s_col = lane_base + C::kTmemS + (j & 1) * C::kBN;
-      float sv[C::kBN];
-      {
-        uint32_t r[C::kBN / 32][32];
-#pragma unroll
-        for (int c = 0; c < C::kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, r[c]);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < C::kBN; ++c) sv[c] = __uint_as_float(r[c >> 5][c & 31]);
-      }
-      const int key0 = (ja + j) * C::kBN;
-      if (key0 + C::kBN - 1 > pos0) {  // diagonal tile: keys after a row's position are masked
-#pragma unroll
-        for (int c = 0; c < C::kBN; ++c) sv[c] = (key0 + c <= row_pos) ? sv[c] : -INFINITY;
-      }
-      // Row max of the raw scores in 8 independent chains (scale > 0 commutes with max).
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = sv[i];
-#pragma unroll
-      for (int c = 8; c < C::kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-      const float mt =
-          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
-          p.qscale;
-      // Lazy rescale, per row: the reference max moves only when this tile
-      // exceeds it by 2^8.  Tile 0 always sets it (key 0 is visible to every
-      // row); in the second half of a cut unit a row may see no key yet, and
-      // its m_ref stays -inf with P = 0.
-      float alpha = 1.0f;
-      bool moved = false;
-      if (m_ref == -INFINITY) {
-        m_ref = mt;
-      } else if (mt > m_ref + kRescaleLog2) {
-        alpha = exp2f(m_ref - mt);
-        m_ref = mt;
-        moved = true;
-      }
-      const float neg_m = m_ref == -INFINITY ? 0.0f : -m_ref;
-      float ps8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ps8[i] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < C::kBN; ++c) {
-        sv[c] = tc::ex2_approx(fmaf(sv[c], p.qscale, neg_m));  // masked keys: 2^-inf = 0
-        ps8[c & 7] += sv[c];
-      }
-      const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-      l_run = l_run * alpha + psum;
-      if (__any_sync(0xffffffffu, moved)) {
-        // O is current once P V of tile j-1 finishes.
-        ok = tc::wait_bounded(&bars[kODone0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, abort_flag, p.err, 31);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tc::tmem_ld32(lane_base + C::kTmemO + c * 32, r);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tc::tmem_st32(lane_base + C::kTmemO + c * 32, r);
-        }
-      }
-      // P (bf16 pairs) over the first kBN/2 columns of this tile's S buffer.
-#pragma unroll
-      for (int c = 0; c < C::kBN / 64; ++c) {
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = f2_to_bf2(sv[c * 64 + 2 * i], sv[c * 64 + 2 * i + 1]);
-        tc::tmem_st32(s_col + c * 32, r);
-      }
-      tc::tmem_st_wait();
-      tc::fence_before_sync();
-      tc::mbar_arrive(&bars[kPFull0 + (j & 1)]);
+      ok = softmax_tile<D, C::kBN>(lane_base, C::kTmemS + (j & 1) * C::kBN, C::kTmemO, (ja + j) * C::kBN, pos0,
+                                   row_pos, p.qscale, m_ref, l_run, &bars[kSFull0 + (j & 1)], (j >> 1) & 1,
+                                   &bars[kODone0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, &bars[kPFull0 + (j & 1)],
+                                   abort_flag, p.err, 30);
+      if (!ok) break;
     }
     // ---- epilogue: O / l (phantom key folded in), one row per thread.
     if (ok) ok = tc::wait_bounded(&bars[kODone0 + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, abort_flag, p.err, 32);
@@ -435,35 +488,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = row < nrows;
     const int64_t orow = (static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h;
     auto store_chunk = [&](int c, const float* v, float inv) {
-      if (!valid) return;
-      if (p.o_f32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * D + c * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
-      } else {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * D + c * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 w;
-          w.x = f2_to_bf2(v[8 * i + 0] * inv, v[8 * i + 1] * inv);
-          w.y = f2_to_bf2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
-          w.z = f2_to_bf2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
-          w.w = f2_to_bf2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
-          dst[i] = w;
-        }
-      }
+      if (valid) store_row_chunk(p, orow * D + c * 32, v, inv);
     };
-    // 1 / l scaled for the phantom zero key (score 0), given the row's max m.
-    auto finish = [&](float m, float l) -> float {
-      float a = 1.0f;
-      if (p.phantom) {
-        const float mf = fmaxf(m, 0.0f);
-        a = m == -INFINITY ? 0.0f : exp2f(m - mf);
-        l = l * a + exp2f(-mf);
-      }
-      return l > 0.0f ? a / l : 0.0f;
-    };
+    auto finish = [&](float m, float l) -> float { return row_inv_sum(p.phantom, m, l); };
     // Every softmax thread takes the same branch (k is per CTA; a failed
     // wait anywhere skips the merge's barriers in all four warps).
     const bool all_ok = !tc::named_sync_or(1, kBM, !ok);
@@ -562,6 +589,270 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------ two query tiles per CTA
+// For head_dim 64 and 128 a CTA can hold two 128-row query tiles of one
+// (head, sequence): S and O of both fit the 512 TMEM columns once Q is read
+// from shared memory instead of TMEM.  Each K/V tile then serves 256 query
+// rows, halving the L2 -> SM traffic per FLOP, and the two softmax
+// warpgroups alternate with the tensor core: while one works on its S, the
+// MMA thread runs the other's P V and next S.
+//   warps 0-3  softmax of query tile A (rows 2 t .. of the pair t), warps
+//              4-7 of tile B (the next 128 rows, when the chunk has them);
+//              each first writes its Q tile to shared memory, 128B-swizzled.
+//   warp 8     producer (as in the one-tile kernel).
+//   warp 9     MMA issuer: S_A(0), S_B(0), then per kv tile j: P_A(j) V,
+//              S_A(j+1), P_B(j) V, S_B(j+1).
+// 320 threads: three warps share an SM sub-partition, so a thread gets up
+// to 168 registers.
+constexpr int kPairThreads = 320;
+
+template <int D>
+struct QCfg {
+  static constexpr int kBN = 128;                      // kv tokens per tile
+  static constexpr int kDB = D / 64;
+  static constexpr int kStages = D == 128 ? 2 : 3;     // K/V ring depth
+  static constexpr int kKVBytes = kBN * D * 2;
+  static constexpr int kQBytes = kBM * D * 2;          // [D/64 blocks][128 rows][128 B]
+  static constexpr int kGroupBytes = kDB * 1024;
+  static constexpr int kOffQ = 0;                      // [2][kQBytes]
+  static constexpr int kOffK = 2 * kQBytes;
+  static constexpr int kOffV = kOffK + kStages * kKVBytes;
+  static constexpr int kOffBar = kOffV + kStages * kKVBytes;
+  static constexpr int kOffMisc = kOffBar + 24 * 8;
+  static constexpr int kSmem = kOffMisc + 64 + 1024;
+  static constexpr int kTmemS = 0;                     // S of tile X at X * kBN
+  static constexpr int kTmemO = 2 * kBN;               // O of tile X at kTmemO + X * D
+  static constexpr int kTmemCols = 512;
+  static_assert(kTmemO + 2 * D <= kTmemCols, "TMEM budget");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+enum PairBar {
+  qQReady0 = 0,   // [2] Q of tile X in shared memory (128 threads each)
+  qKFull0 = 2,    // [3]
+  qVFull0 = 5,    // [3]
+  qKEmpty0 = 8,   // [3] S of both tiles done with the stage's K
+  qVEmpty0 = 11,  // [3] P V of both tiles done with the stage's V
+  qSFull0 = 14,   // [2] S of tile X holds kv tile j's scores
+  qPFull0 = 16,   // [2] P of tile X written (128 threads each)
+  qODone0 = 18,   // [2] P V of tile X's kv tile j done
+  qNumBars = 20
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    paged_prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PrefillParams p) {
+  using C = QCfg<D>;
+  constexpr int kS = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int q0 = p.qo_indptr[s];
+  const int q_len = p.qo_indptr[s + 1] - q0;
+  const int t0 = 2 * pair;  // query tile A; B = t0 + 1
+  if (t0 * kBM >= q_len) return;
+  const int kv_beg = p.kv_indptr[s];
+  const int npages = p.kv_indptr[s + 1] - kv_beg;
+  int kv_len = p.seq_lens[s];
+  if (kv_len < q_len || kv_len > npages * p.ps) {
+    if (pair == 0 && h == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
+    kv_len = max(q_len, min(kv_len, npages * p.ps));
+    if (kv_len > npages * p.ps) return;  // not even the chunk fits its pages
+  }
+  const bool has_b = (t0 + 1) * kBM < q_len;
+  const int pos0a = kv_len - q_len + t0 * kBM;  // position of tile A's row 0
+  const int nrows_a = min(kBM, q_len - t0 * kBM);
+  const int nrows_b = has_b ? min(kBM, q_len - (t0 + 1) * kBM) : 0;
+  const int n_a = (pos0a + nrows_a - 1) / C::kBN + 1;                   // kv tiles tile A sees
+  const int n_b = has_b ? (pos0a + kBM + nrows_b - 1) / C::kBN + 1 : 0;  // >= n_a
+  const int n = max(n_a, n_b);
+  const int g = h / (p.hq / p.hkv);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < qNumBars; ++i)
+      mbar_init(&bars[i], (i == qQReady0 || i == qQReady0 + 1 || i == qPFull0 || i == qPFull0 + 1) ? kBM : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    // As in the one-tile kernel: one 4-D box per (page, kv head), page ids
+    // fetched 32 at a time one window ahead, K refilled once S of both
+    // query tiles is done with the stage, V once both P V are.
+    const int ppt = C::kBN / p.ps;
+    const int lim = min(npages, n * ppt) - 1;
+    auto fetch = [&](int first) -> int { return p.kv_indices[kv_beg + min(first + lane, lim)]; };
+    auto to_row = [&](int page) -> int {
+      if (page < 0 || page >= p.num_pages) {
+        record_error(p.err, kDevErrBadPage, s);
+        page = 0;
+      }
+      return static_cast<int>((p.row_k + (static_cast<int64_t>(page) * p.hkv + g) * p.ps) >> 3);
+    };
+    if (lane == 0) tc::prefetch_tmap(&tm_kv);
+    const int page_bytes = p.ps * D * 2;
+    const int dv = static_cast<int>((p.row_v - p.row_k) >> 3);
+    int cur = to_row(fetch(0));
+    int nxt = fetch(32);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kS;
+      const uint32_t par = ((j / kS) - 1) & 1;
+      const int first = j * ppt;
+      if (j > 0 && (first & 31) == 0) {
+        cur = to_row(nxt);
+        nxt = fetch(first + 32);
+      }
+      bool ok = true;
+      if (lane == 0 && j >= kS) ok = tc::wait_bounded(&bars[qKEmpty0 + st], par, abort_flag, p.err, 50);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* kst = smem + C::kOffK + st * C::kKVBytes;
+      if (lane == 0) mbar_arrive_expect_tx(&bars[qKFull0 + st], C::kKVBytes);
+      for (int pi = 0; pi < ppt; ++pi) {
+        const int r = __shfl_sync(0xffffffffu, cur, (first & 31) + pi);
+        if (lane == 0) tc::tma_load_4d_w(kst + pi * page_bytes, &tm_kv, r, &bars[qKFull0 + st]);
+      }
+      if (lane == 0 && j >= kS) ok = tc::wait_bounded(&bars[qVEmpty0 + st], par, abort_flag, p.err, 51);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* vst = smem + C::kOffV + st * C::kKVBytes;
+      if (lane == 0) mbar_arrive_expect_tx(&bars[qVFull0 + st], C::kKVBytes);
+      for (int pi = 0; pi < ppt; ++pi) {
+        const int r = __shfl_sync(0xffffffffu, cur, (first & 31) + pi);
+        if (lane == 0) tc::tma_load_4d_w(vst + pi * page_bytes, &tm_kv, r + dv, &bars[qVFull0 + st]);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    // S_X = Q_X K^T with both operands in shared memory (Q block-major: 64
+    // columns x 128 rows per 16 KB block at head_dim 128); O_X += P_X V with
+    // P_X from TMEM.  One thread's tcgen05.mma execute in issue order, so
+    // S_X(j+1), issued after P_X(j) V, overwrites P_X(j) only once it is read.
+    if (lane == 0) {
+      constexpr uint32_t idS = tc::idesc_bf16(kBM, C::kBN, false);
+      constexpr uint32_t idO = tc::idesc_bf16(kBM, D, true);
+      const uint64_t dQ = tc::sdesc_sw128(smem_u32(smem + C::kOffQ), 16, 1024);
+      const uint64_t dK = tc::sdesc_sw128(smem_u32(smem + C::kOffK), 16, C::kGroupBytes);
+      const uint64_t dV = tc::sdesc_sw128(smem_u32(smem + C::kOffV), 1024, C::kGroupBytes);
+      auto issue_s = [&](int x, int j) -> bool {
+        const int st = j % kS;
+        if (!tc::wait_bounded(&bars[qKFull0 + st], (j / kS) & 1, abort_flag, p.err, 60)) return false;
+        tc::fence_after_sync();
+        const uint64_t a0 = dQ + ((x * C::kQBytes) >> 4);
+        const uint64_t b0 = dK + ((st * C::kKVBytes) >> 4);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          tc::mma_bf16(tmem + C::kTmemS + x * C::kBN, a0 + (((k >> 2) * (kBM * 128) + (k & 3) * 32) >> 4),
+                       b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
+        tc::mma_commit(&bars[qSFull0 + x]);
+        return true;
+      };
+      auto issue_pv = [&](int x, int j) -> bool {
+        const int st = j % kS;
+        if (!tc::wait_bounded(&bars[qPFull0 + x], j & 1, abort_flag, p.err, 61)) return false;
+        if (!tc::wait_bounded(&bars[qVFull0 + st], (j / kS) & 1, abort_flag, p.err, 62)) return false;
+        tc::fence_after_sync();
+        const uint64_t b0 = dV + ((st * C::kKVBytes) >> 4);
+#pragma unroll
+        for (int k = 0; k < C::kBN / 16; ++k)
+          tc::mma_bf16_ts(tmem + C::kTmemO + x * D, tmem + C::kTmemS + x * C::kBN + k * 8,
+                          b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, (j > 0 || k > 0) ? 1u : 0u);
+        tc::mma_commit(&bars[qODone0 + x]);
+        return true;
+      };
+      bool ok = tc::wait_bounded(&bars[qQReady0], 0, abort_flag, p.err, 63);
+      if (ok && has_b) ok = tc::wait_bounded(&bars[qQReady0 + 1], 0, abort_flag, p.err, 63);
+      if (ok) tc::fence_after_sync();
+      ok = ok && issue_s(0, 0) && (!has_b || issue_s(1, 0));
+      if (ok) tc::mma_commit(&bars[qKEmpty0]);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j < n_a) {
+          ok = issue_pv(0, j) && (j + 1 >= n_a || issue_s(0, j + 1));
+          if (!ok) break;
+        }
+        if (j < n_b) {
+          ok = issue_pv(1, j) && (j + 1 >= n_b || issue_s(1, j + 1));
+          if (!ok) break;
+        }
+        tc::mma_commit(&bars[qVEmpty0 + j % kS]);
+        if (j + 1 < n) tc::mma_commit(&bars[qKEmpty0 + (j + 1) % kS]);
+      }
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax
+    const int x = warp >> 2;  // query tile of this warpgroup
+    if (x == 0 || has_b) {
+      const int row = threadIdx.x & (kBM - 1);  // == TMEM lane
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+      const int nrows = x ? nrows_b : nrows_a;
+      const int pos0 = pos0a + x * kBM;
+      const int last_pos = pos0 + nrows - 1;
+      const int nx = x ? n_b : n_a;
+      const int row_pos = min(pos0 + row, last_pos);
+      const int64_t qrow0 = static_cast<int64_t>(q0) + (t0 + x) * kBM + row;
+      {
+        // Q row into shared memory: 16-byte chunk c of the row goes to block
+        // c / 8, chunk (c % 8) ^ (row % 8) of the row's 128 bytes (the
+        // 128-byte swizzle the descriptor names); rows past the chunk are zero.
+        const uint4* qrow = reinterpret_cast<const uint4*>(p.q + (qrow0 * p.hq + h) * D);
+        uint8_t* qs = smem + C::kOffQ + x * C::kQBytes + row * 128;
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b) {  // one 64-column block (8 chunks) at a time
+          uint4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = row < nrows ? qrow[b * 8 + i] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(qs + b * (kBM * 128) + ((c ^ (row & 7)) << 4)) = v[c];
+        }
+        fence_proxy_async_shared();
+        tc::mbar_arrive(&bars[qQReady0 + x]);
+      }
+      float m_ref = -INFINITY, l_run = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nx; ++j) {
+        ok = softmax_tile<D, C::kBN>(lane_base, C::kTmemS + x * C::kBN, C::kTmemO + x * D, j * C::kBN, pos0, row_pos,
+                                     p.qscale, m_ref, l_run, &bars[qSFull0 + x], j & 1, &bars[qODone0 + x],
+                                     (j - 1) & 1, &bars[qPFull0 + x], abort_flag, p.err, 70);
+        if (!ok) break;
+      }
+      if (ok) ok = tc::wait_bounded(&bars[qODone0 + x], (nx - 1) & 1, abort_flag, p.err, 72);
+      tc::fence_after_sync();
+      if (!tc::named_sync_or(1 + x, kBM, !ok)) {
+        const float inv = row_inv_sum(p.phantom, m_ref, l_run);
+        const int64_t elem0 = (qrow0 * p.hq + h) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(lane_base + C::kTmemO + x * D + c * 32, r);
+          tc::tmem_ld_wait();
+          if (row < nrows) store_row_chunk(p, elem0 + c * 32, reinterpret_cast<const float*>(r), inv);
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
 // --------------------------------------------------------------- host side
 
 template <int D>
@@ -579,6 +870,24 @@ int launch_prefill(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles
   dim3 grid(n_tiles, prm.hq, prm.split ? n_seqs * kMaxPieces : n_seqs);
   paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
   return check_launch("paged_prefill_kernel");
+}
+
+template <int D>
+int launch_prefill_pair(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
+                        cudaStream_t stream) {
+  using C = QCfg<D>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    MTN_CUDA_TRY(cudaFuncSetAttribute(paged_prefill_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::kSmem),
+                 "cudaFuncSetAttribute(prefill pair)");
+    configured[dev] = true;
+  }
+  dim3 grid((n_tiles + 1) / 2, prm.hq, n_seqs);
+  paged_prefill_pair_kernel<D><<<grid, kPairThreads, C::kSmem, stream>>>(tkv, prm);
+  return check_launch("paged_prefill_pair_kernel");
 }
 
 // Workspace of the split: counters, then (m, l) rows, then O partials.
@@ -673,6 +982,13 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
     prm.ws_o = reinterpret_cast<float*>(w + wl.off_o);
   }
   auto s = static_cast<cudaStream_t>(stream);
+  // Many query tiles (at least two per SM): two tiles per CTA at head_dim
+  // <= 128, sharing every K/V tile.
+  if (!prm.split && D <= 128 && !(flags & MTN_ATTN_PREFILL_ONE_TILE) &&
+      (total_q / mtn::kBM) * num_q_heads >= 2 * static_cast<int64_t>(mtn::sm_count())) {
+    return D == 64 ? mtn::launch_prefill_pair<64>(tkv, prm, n_tiles, n_seqs, s)
+                   : mtn::launch_prefill_pair<128>(tkv, prm, n_tiles, n_seqs, s);
+  }
   switch (D) {
     case 64: return mtn::launch_prefill<64>(tkv, prm, n_tiles, n_seqs, s);
     case 128: return mtn::launch_prefill<128>(tkv, prm, n_tiles, n_seqs, s);

@@ -176,13 +176,15 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
                   kv_indptr: torch.Tensor, kv_indices: torch.Tensor, seq_lens: torch.Tensor, max_q_len: int,
                   scale: float | None = None, phantom: bool = False, out: torch.Tensor | None = None,
                   out_dtype: torch.dtype = torch.bfloat16, workspace: torch.Tensor | None = None,
-                  stream=None) -> torch.Tensor:
+                  stream=None, one_tile: bool = False) -> torch.Tensor:
     """Chunked-prefill attention for q [total_q, num_q_heads, head_dim] (bf16) over the paged cache.
 
     Launches with few (query tile, head) units cut long ones into pieces over
     more CTAs; that needs `workspace` (mtn_paged_prefill_workspace_bytes,
     zeroed once, reusable, one stream at a time).  A fresh zeroed one is made
-    when none is given; a smaller one runs the launch unsplit.
+    when none is given; a smaller one runs the launch unsplit.  Launches with
+    many query tiles at head_dim <= 128 run two query tiles per CTA;
+    `one_tile` forces the one-tile kernel (same results).
     """
     if q.dim() != 3 or not q.is_contiguous() or q.dtype != torch.bfloat16:
         raise ValueError("q must be a contiguous bf16 [total_q, heads, head_dim] tensor")
@@ -195,7 +197,7 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
     nb = L.lib().mtn_paged_prefill_workspace_bytes(n, tq, hq, pool.num_kv_heads, d)
     if workspace is None and nb > 0:
         workspace = torch.zeros(nb, dtype=torch.uint8, device=q.device)
-    flags = L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0
+    flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_PREFILL_ONE_TILE if one_tile else 0)
     L.check(L.lib().mtn_paged_prefill(C.byref(pool.layout), layer, _ptr(q), _ptr(out), _dtype_code(out.dtype), n,
                                       tq, hq, _ptr(_i32(qo_indptr)), _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)),
                                       _ptr(_i32(seq_lens)), max_q_len, float(scale), flags, _ptr(workspace),

@@ -23,7 +23,7 @@ TOL_KERNEL = 1e-2
 
 
 def run_prefill(kv_lens, q_lens, hq, hkv, d, phantom=True, seed=0, out_dtype=torch.float32, page_size=16,
-                workspace=None, case=None):
+                workspace=None, case=None, one_tile=False):
     case = case or make_case(kv_lens, hkv, d, page_size=page_size, seed=seed)
     rng = np.random.default_rng(seed + 100)
     total_q = sum(q_lens)
@@ -31,7 +31,8 @@ def run_prefill(kv_lens, q_lens, hq, hkv, d, phantom=True, seed=0, out_dtype=tor
     qt = torch.from_numpy(q).to("cuda").to(torch.bfloat16)
     qo = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32), device="cuda")
     out = paged.paged_prefill(case.pool, 0, qt, qo, case.kv_indptr, case.kv_indices, case.seq_lens,
-                              max(q_lens), phantom=phantom, out_dtype=out_dtype, workspace=workspace)
+                              max(q_lens), phantom=phantom, out_dtype=out_dtype, workspace=workspace,
+                              one_tile=one_tile)
     torch.cuda.synchronize()
     return case, q, qt.float().cpu().numpy(), out.float().cpu().numpy()
 
@@ -115,4 +116,24 @@ def test_prefill_split_long_units(cuda_device, hq, hkv, d, kv_lens, q_lens):
     _, _, _, unsplit = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=d + hq, workspace=small, case=case)
     check(case, q_lens, q, qu, unsplit, d)
     assert float(np.abs(out - unsplit).max()) <= 1e-3
+    assert paged.device_error(0) == (0, 0)
+
+
+@pytest.mark.parametrize("hq,hkv,d,page_size", [(28, 4, 128, 16), (14, 2, 64, 16), (28, 4, 128, 64)])
+@pytest.mark.parametrize("phantom", [True, False])
+def test_prefill_two_tiles_per_cta(cuda_device, hq, hkv, d, page_size, phantom):
+    """At least two query tiles per SM at head_dim <= 128: two query tiles per
+    CTA share each K/V tile.  Ragged chunks give pairs with and without a
+    second tile and pairs whose tiles see different kv tile counts; the
+    result matches the oracle and the one-tile kernel."""
+    q_lens = [512, 300, 1, 777, 130, 1200, 128]
+    kv_lens = [512 + 1000, 300, 1, 777 + 5000, 130 + 129, 1200 + 3, 128 + 64]
+    assert (sum(q_lens) // 128) * hq >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    case, q, qu, out = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=hq + d + page_size, phantom=phantom,
+                                   page_size=page_size)
+    check(case, q_lens, q, qu, out, d, phantom=phantom)
+    _, _, _, one = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=hq + d + page_size, phantom=phantom,
+                               page_size=page_size, case=case, one_tile=True)
+    check(case, q_lens, q, qu, one, d, phantom=phantom)
+    assert float(np.abs(out - one).max()) <= 1e-3
     assert paged.device_error(0) == (0, 0)
