@@ -17,8 +17,8 @@ into the decode kernel).
          per_step_l2_flushed_us re-times the same steps one by one after an
          L2-flushing 256 MiB write.
   e2e    the same step through the C ABI with pinned HOST buffers: Q, new
-         K/V, slots and seq_lens copied host->device and the output copied
-         back inside the timed region.
+         K/V and seq_lens (packed in one staging buffer per step) copied
+         host->device and the output copied back inside the timed region.
   roofline  the decode kernel: algorithmic bytes per launch / its mean
          CUDA-event time, against MEASURED_PEAKS.json hbm_gbs.
   cpu_baseline  the reference algorithm on the host cores (oracle port of
@@ -354,8 +354,8 @@ def run_ours(args, rank, world, local, pg):
                      "algorithmic_bytes_per_launch": sum(dec_bytes) / len(dec_bytes)},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
-                "path": "per step: pinned host Q/K/V/seq_lens -> H2D -> mtn_paged_decode (C ABI) -> D2H output, "
-                        "steps back to back, batches rotating as above"},
+                "path": "per step: Q/K/V/seq_lens packed in one pinned host buffer -> one H2D copy -> "
+                        "mtn_paged_decode (C ABI) -> D2H output, steps back to back, batches rotating as above"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
         "kv_append_bulk": extras["append"],
@@ -449,27 +449,37 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
     steps = args.steps
     gen = torch.Generator()
     gen.manual_seed(5)
-    q_h = torch.randn((N_SEQS, HQ, D), generator=gen).to(torch.bfloat16).pin_memory()
-    k_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
-    v_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16).pin_memory()
+    q_h = torch.randn((N_SEQS, HQ, D), generator=gen).to(torch.bfloat16)
+    k_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16)
+    v_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16)
     o_h = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory()
-    len_h = [torch.from_numpy(step_inputs(st, i, device)[1]).pin_memory() for i in range(total_steps)]
-    q_d, k_d, v_d = (torch.empty_like(x, device=device) for x in (q_h, k_h, v_h))
+    # Each step's inputs (Q, new K, new V, seq_lens) packed in one pinned
+    # staging buffer, so a step is one host->device copy, the call and one
+    # device->host copy of O.
+    parts = [q_h.view(torch.uint8).reshape(-1), k_h.view(torch.uint8).reshape(-1), v_h.view(torch.uint8).reshape(-1)]
+    offs = np.cumsum([0] + [x.numel() for x in parts]).tolist()  # byte offsets (multiples of 16)
+    nbytes = offs[-1] + N_SEQS * 4
+    stage_h = []
+    for i in range(total_steps):
+        buf = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        for x, o in zip(parts, offs):
+            buf[o:o + x.numel()].copy_(x)
+        buf[offs[3]:].copy_(torch.from_numpy(step_inputs(st, i, device)[1]).view(torch.uint8))
+        stage_h.append(buf)
+    stage_d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    base = stage_d.data_ptr()
+    q_p, k_p, v_p, l_p = (base + o for o in offs)
     o_d = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
-    l_d = torch.empty(N_SEQS, dtype=torch.int32, device=device)
     scale = D ** -0.5
 
     def one(i):
         sp = int(torch.cuda.current_stream().cuda_stream)
         b = st["batches"][step_batch(st, i)]
-        q_d.copy_(q_h, non_blocking=True)
-        k_d.copy_(k_h, non_blocking=True)
-        v_d.copy_(v_h, non_blocking=True)
-        l_d.copy_(len_h[i], non_blocking=True)
-        _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_d.data_ptr(), _lib.MTN_DTYPE_BF16,
-                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, k_d.data_ptr(), v_d.data_ptr(),
+        stage_d.copy_(stage_h[i], non_blocking=True)
+        _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_p, _lib.MTN_DTYPE_BF16,
+                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, k_p, v_p,
                                         _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
-                                        b["indices"].data_ptr(), l_d.data_ptr(), scale, 0, ws.buf.data_ptr(),
+                                        b["indices"].data_ptr(), l_p, scale, 0, ws.buf.data_ptr(),
                                         ws.nbytes, sp))
         o_h.copy_(o_d, non_blocking=True)
 
@@ -493,7 +503,7 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
     b.synchronize()
     t = a.elapsed_time(b) * 1e-3
     del graphs
-    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, len_h[0]))
+    h2d = nbytes
     d2h = o_h.numel() * o_h.element_size()
     return {"t": t, "steps": steps, "h2d": h2d, "d2h": d2h}
 
