@@ -205,12 +205,13 @@ __device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off,
 #pragma unroll
     for (int c = 0; c < kBN; ++c) sv[c] = (key0 + c <= row_pos) ? sv[c] : -INFINITY;
   }
-  // Row max of the raw scores in 8 independent chains (scale > 0 commutes with max).
+  // Row max of the raw scores in 8 independent chains, two scores per
+  // three-input max (scale > 0 commutes with max).
   float mx[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = sv[i];
 #pragma unroll
-  for (int c = 8; c < kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+  for (int c = 8; c < kBN; c += 2) mx[(c >> 1) & 7] = tc::max3(mx[(c >> 1) & 7], sv[c], sv[c + 1]);
   const float mt =
       fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * qscale;
   // Lazy rescale, per row: the reference max moves only when this tile
@@ -229,10 +230,15 @@ __device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off,
   float ps8[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) ps8[i] = 0.0f;
+  // Pairs of scores through the packed f32x2 FMA and add: the same roundings
+  // as one fmaf / add per score, and score c still sums into chain c & 7.
 #pragma unroll
-  for (int c = 0; c < kBN; ++c) {
-    sv[c] = tc::ex2_approx(fmaf(sv[c], qscale, neg_m));  // masked keys: 2^-inf = 0
-    ps8[c & 7] += sv[c];
+  for (int c = 0; c < kBN; c += 2) {
+    float x0, x1;
+    tc::fma2(x0, x1, sv[c], sv[c + 1], qscale, neg_m);
+    sv[c] = tc::ex2_approx(x0);  // masked keys: 2^-inf = 0
+    sv[c + 1] = tc::ex2_approx(x1);
+    tc::add2(ps8[c & 7], ps8[(c & 7) + 1], sv[c], sv[c + 1]);
   }
   const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
   l_run = l_run * alpha + psum;

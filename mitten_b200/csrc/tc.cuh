@@ -176,6 +176,33 @@ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major, bool a_mn_major = f
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Three-input max (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed pair of f32 (sm_100 f32x2 arithmetic): (x0, x1) * b + c, each
+// element rounded as one fmaf.
+__device__ __forceinline__ void fma2(float& y0, float& y1, float x0, float x1, float b, float c) {
+  uint64_t x, bb, cc, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(x0), "f"(x1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b), "f"(b));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c), "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(bb), "l"(cc));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(y0), "=f"(y1) : "l"(r));
+}
+
+// (s0, s1) += (a0, a1), each element rounded as one add.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  uint64_t s, a, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(s) : "f"(s0), "f"(s1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(s), "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(s0), "=f"(s1) : "l"(r));
+}
+
 // Named barrier over `count` threads (ids 1..15; id 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
