@@ -214,8 +214,9 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
  *   long units into up to 4 pieces of kv tiles on separate CTAs and merge
  *   them; that takes mtn_paged_prefill_workspace_bytes(...) bytes (0 above
  *   296 units), 256-byte aligned, zeroed once before first use and left
- *   zeroed by every call, one stream at a time.  With no or a smaller
- *   workspace the launch runs unsplit. */
+ *   zeroed by every call, one stream at a time (after a call that reports
+ *   a device timeout, zero it again).  With no or a smaller workspace the
+ *   launch runs unsplit. */
 MTN_API size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                                          int32_t num_kv_heads, int32_t head_dim);
 MTN_API int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer,

@@ -181,7 +181,8 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
 
     Launches with few (query tile, head) units cut long ones into pieces over
     more CTAs; that needs `workspace` (mtn_paged_prefill_workspace_bytes,
-    zeroed once, reusable, one stream at a time).  A fresh zeroed one is made
+    zeroed once, reusable, one stream at a time; zero it again after a call
+    that reported a device timeout).  A fresh zeroed one is made
     when none is given; a smaller one runs the launch unsplit.  Launches with
     many query tiles at head_dim <= 128 run two query tiles per CTA;
     `one_tile` forces the one-tile kernel (same results).
