@@ -137,3 +137,31 @@ def test_prefill_two_tiles_per_cta(cuda_device, hq, hkv, d, page_size, phantom):
     check(case, q_lens, q, qu, one, d, phantom=phantom)
     assert float(np.abs(out - one).max()) <= 1e-3
     assert paged.device_error(0) == (0, 0)
+
+
+@pytest.mark.parametrize("hq,hkv,d,page_size", [(14, 2, 64, 32), (28, 4, 128, 128)])
+def test_prefill_two_tiles_page_sizes_bf16_out(cuda_device, hq, hkv, d, page_size):
+    """The two-tile kernel at other page sizes (two pages and one page per
+    128-key tile) with bf16 output."""
+    q_lens = [384, 129, 1000, 256, 64, 900, 200]
+    kv_lens = [384 + 2000, 129 + 7, 1000, 256 + 300, 64 + 4000, 900 + 128, 200 + 50]
+    assert (sum(q_lens) // 128) * hq >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    case, q, qu, out = run_prefill(kv_lens, q_lens, hq, hkv, d, seed=3 * d + page_size, page_size=page_size,
+                                   out_dtype=torch.bfloat16)
+    check(case, q_lens, q, qu, out, d)
+    assert paged.device_error(0) == (0, 0)
+
+
+def test_prefill_split_head_dim_256_one_page_per_tile(cuda_device):
+    """The split at head_dim 256 with 64-token pages (one page per 64-key kv
+    tile) and a ragged second chunk."""
+    from mitten_b200 import _lib as L
+    q_lens, kv_lens = [300, 77], [6000, 77 + 2500]
+    nb = L.lib().mtn_paged_prefill_workspace_bytes(len(q_lens), sum(q_lens), 4, 1, 256)
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    case, q, qu, out = run_prefill(kv_lens, q_lens, 4, 1, 256, seed=11, page_size=64, workspace=ws)
+    check(case, q_lens, q, qu, out, 256)
+    units = (sum(q_lens) // 128 + len(q_lens)) * 4
+    off = (units * 4 + 255) // 256 * 256
+    assert int(ws[:off].count_nonzero()) == 0 and int(ws[off:].count_nonzero()) > 0
+    assert paged.device_error(0) == (0, 0)
