@@ -67,6 +67,13 @@ MTN_API const char* mtn_version(void);
  * and the kernel-specific detail word; `clear` resets it. */
 MTN_API int mtn_device_error(int device, int clear, int32_t* code, int32_t* detail);
 
+/* Self-test of the bounded device waits (failure detection without a GPU
+ * fault): launches one block on `stream` whose mbarrier wait nothing
+ * completes.  After ~1 s the wait gives up, records device error 4
+ * (timeout) with detail 99 in the word mtn_device_error reads, and the
+ * kernel returns normally: no trap, the context stays usable. */
+MTN_API int mtn_selftest_bounded_wait(void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Device KV pool layout                                                    */
 /* ------------------------------------------------------------------------ */

@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtn_last_error": (C.c_char_p, []),
     "mtn_version": (C.c_char_p, []),
     "mtn_device_error": (C.c_int, [C.c_int, C.c_int, c_i32p, c_i32p]),
+    "mtn_selftest_bounded_wait": (C.c_int, [C.c_void_p]),
     "mtn_kv_required_bytes": (C.c_size_t, [C.c_int64] * 6),
     "mtn_kv_pool_alloc": (C.c_int, [C.c_int, C.POINTER(KvLayout)]),
     "mtn_kv_pool_free": (C.c_int, [C.POINTER(KvLayout)]),

@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace mtn {
 
@@ -62,6 +63,25 @@ int* device_error_ptr() {
   return g_dev_error_addr[dev];
 }
 
+}  // namespace mtn
+
+namespace mtn {
+namespace {
+// A wait that nothing completes: thread 0 waits on a fresh mbarrier with
+// the same bounded wait the kernels use; after ~1 s it records
+// kDevErrTimeout (detail `where`) and the kernel returns normally.
+__global__ void bounded_wait_selftest_kernel(int* err, int where) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) tc::wait_bounded(&bar, 0, &abort_flag, err, where);
+}
+}  // namespace
 }  // namespace mtn
 
 extern "C" {
@@ -127,6 +147,13 @@ int mtn_kv_pool_alloc(int device, mtn_kv_layout* out) {
   }
   out->base = p;
   return MTN_OK;
+}
+
+int mtn_selftest_bounded_wait(void* stream) {
+  int* err = mtn::device_error_ptr();
+  if (err == nullptr) return mtn::set_error(MTN_ECUDA, "mtn_selftest_bounded_wait: no device error word");
+  mtn::bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(err, 99);
+  return mtn::check_launch("bounded_wait_selftest_kernel");
 }
 
 int mtn_kv_pool_free(mtn_kv_layout* pool) {
