@@ -36,6 +36,12 @@ CASES = [
          seed=104),
     dict(name="prefill_mqa_d256", kind="prefill", hq=8, hkv=1, d=256, lens=[640], q_lens=[130], phantom=False,
          seed=106),
+    # Launches with at least two query tiles per SM (148): the two-query-tile
+    # kernel.  Every 97th output row is stored.
+    dict(name="prefill_pair_gqa7_d128", kind="prefill", hq=28, hkv=4, d=128, lens=[1412, 512, 2384],
+         q_lens=[512, 512, 384], phantom=True, seed=107, stride=97),
+    dict(name="prefill_pair_gqa7_d64", kind="prefill", hq=14, hkv=2, d=64, lens=[1324, 1024, 2268],
+         q_lens=[1024, 1024, 768], phantom=False, seed=108, stride=97),
 ]
 
 
@@ -70,9 +76,9 @@ def oracle_outputs(case: dict, q, ks, vs) -> np.ndarray:
     return np.concatenate(out)
 
 
-def kept_rows(n_rows: int) -> np.ndarray:
-    """The output rows stored (every 7th and the last), to keep the fixture small."""
-    return np.unique(np.concatenate([np.arange(0, n_rows, 7), [n_rows - 1]]))
+def kept_rows(n_rows: int, stride: int = 7) -> np.ndarray:
+    """The output rows stored (every `stride`-th and the last), to keep the fixture small."""
+    return np.unique(np.concatenate([np.arange(0, n_rows, stride), [n_rows - 1]]))
 
 
 def main() -> None:
@@ -80,7 +86,7 @@ def main() -> None:
     for case in CASES:
         q, ks, vs = inputs(case)
         out = oracle_outputs(case, q, ks, vs)
-        arrays[case["name"] + "/out"] = out[kept_rows(out.shape[0])]
+        arrays[case["name"] + "/out"] = out[kept_rows(out.shape[0], case.get("stride", 7))]
         arrays[case["name"] + "/digest"] = np.frombuffer(bytes.fromhex(digest(q, ks, vs)), dtype=np.uint8)
     np.savez_compressed(OUT, **arrays)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")
