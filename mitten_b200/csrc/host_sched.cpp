@@ -60,14 +60,27 @@ struct Sched {
     cfg.eos_token_ids = nullptr;
   }
 
+  // First failed page return since the last schedule/process call.  The
+  // reference's KvCachePool::free debug_asserts that the page is in use
+  // (kv_pool.rs:40-45), which panics in the debug builds its tests run in;
+  // here the call that hit it reports MTN_EINVAL with that message.
+  int fault = MTN_OK;
+
   bool refcount() const { return cfg.mode == MTN_SCHED_REFCOUNT; }
+
+  int take_fault() {
+    const int f = fault;
+    fault = MTN_OK;
+    return f;
+  }
 
   // --------------------------------------------------------------- pages
 
   // Return a page the request (or the tree) no longer lists.
   int drop_page(uint32_t page) {
-    if (refcount()) return pool.release(page, nullptr);
-    return pool.free(page);  // kv_pool.rs:40-47
+    const int st = refcount() ? pool.release(page, nullptr) : pool.free(page);  // kv_pool.rs:40-47
+    if (st != MTN_OK && fault == MTN_OK) fault = st;
+    return st;
   }
 
   int drop_pages(std::vector<uint32_t>& pages) {
@@ -275,6 +288,7 @@ struct Sched {
       pre.swap(kept);
     }
     batch.clear();
+    if (fault != MTN_OK) return take_fault();
     if (dec.empty() && pre.empty()) return MTN_OK;
     assemble(pre, dec);
     out->phase = pre.empty() ? MTN_PHASE_DECODE_ONLY : (dec.empty() ? MTN_PHASE_PREFILL_ONLY : MTN_PHASE_MIXED);
@@ -403,7 +417,7 @@ struct Sched {
       }
     }
     batch.clear();
-    return MTN_OK;
+    return take_fault();
   }
 };
 

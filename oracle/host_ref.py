@@ -309,6 +309,12 @@ class Batch:  # inference-backend/src/batch.rs:7-36
 
 def sample_token(logits, temperature: float) -> int:  # scheduler.rs:186-223
     if temperature <= 0.0:
+        import numpy as np
+
+        row = np.asarray(logits, dtype=np.float32)
+        if not np.isnan(row).any():
+            # Without NaNs the first strict maximum is numpy's first argmax.
+            return int(np.argmax(row)) if row.size else 0
         max_val, max_idx = -math.inf, 0
         for i, v in enumerate(logits):
             if v > max_val:
@@ -441,6 +447,14 @@ class EngineContext:
         phase = 0 if (pre and not dec) else (1 if (dec and not pre) else 2)
         return Batch(phase, reqs, input_ids, position_ids, page_table)
 
+    # engine_loop.rs:47-57: a failed forward marks every request of the batch
+    # Aborted; pages and radix locks are released later by
+    # collect_decode_requests (decode.rs:20-33) for requests in `decoding`.
+    @staticmethod
+    def abort_batch(batch: Batch):
+        for r in batch.requests:
+            r.state = ABORTED
+
     # scheduler.rs:79-184
     def process_and_transition(self, batch: Batch, logits_rows):
         row = 0
@@ -472,3 +486,22 @@ class EngineContext:
                     if r in self.decoding:
                         self.decoding.remove(r)
                 row += 1
+
+
+# ---------------------------------------------------------------- stub.rs
+def stub_logits(requests, vocab_size: int, eos_token_ids, forced_tokens=(), rng_seed: int = 42):
+    """StubBackend::forward (inference-backend/src/stub.rs:32-67): one row per
+    request, all zeros except 10.0 at the token it forces -- forced_tokens
+    indexed by the request's output length (EOS past their end), or, with no
+    forced tokens, (rng_seed ^ low 64 bits of the id ^ step) % vocab_size."""
+    import numpy as np
+
+    data = np.zeros((len(requests), vocab_size), dtype=np.float32)
+    for i, r in enumerate(requests):
+        idx = len(r.output_ids)
+        if forced_tokens:
+            tok = forced_tokens[idx] if idx < len(forced_tokens) else eos_token_ids[0]
+        else:
+            tok = (rng_seed ^ (int(r.id) & 0xFFFFFFFFFFFFFFFF) ^ idx) % vocab_size
+        data[i, int(tok) % vocab_size] = 10.0
+    return data
