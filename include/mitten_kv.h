@@ -373,6 +373,19 @@ MTN_API int mtn_sched_request_info(const mtn_sched* s, uint64_t req_id, int32_t*
                            int64_t* n_output);
 MTN_API int mtn_sched_request_pages(const mtn_sched* s, uint64_t req_id, uint32_t* pages, int64_t* n_pages);
 MTN_API int mtn_sched_request_output(const mtn_sched* s, uint64_t req_id, uint32_t* out, int64_t* n_out);
+/* Prefix fork (refcount mode; no counterpart in the reference, whose pages
+ * carry no reference counts): queue child_id with the prompt
+ * parent prompt + suffix (n_suffix >= 1), sharing the parent's pages of its
+ * whole prompt -- the partially filled last page too -- with cached_len set
+ * to the parent's prompt length.  The first write into a shared partial
+ * page is preceded by a copy-on-write pair in the batch (cow_src/cow_dst).
+ * The parent must have finished its prompt and still hold its pages. */
+MTN_API int mtn_sched_fork(mtn_sched* s, uint64_t parent_id, uint64_t child_id, const uint32_t* suffix,
+                           int64_t n_suffix, float temperature, int32_t max_new_tokens);
+/* Inspection for tests: a page's reference count (0 = free, -1 = out of
+ * range) and every page the radix cache lists (capacity/count in *n_pages). */
+MTN_API int32_t mtn_sched_page_refcount(const mtn_sched* s, uint32_t page);
+MTN_API int mtn_sched_tree_pages(const mtn_sched* s, uint32_t* pages, int64_t* n_pages);
 MTN_API int64_t mtn_sched_free_pages(const mtn_sched* s);
 MTN_API int64_t mtn_sched_cached_pages(const mtn_sched* s);
 MTN_API int32_t mtn_sched_num_active(const mtn_sched* s);

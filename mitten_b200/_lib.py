@@ -134,6 +134,9 @@ SIGNATURES: dict[str, tuple] = {
     "mtn_sched_request_info": (C.c_int, [C.c_void_p, C.c_uint64, c_i32p, c_i64p, c_i64p, c_i64p, c_i64p]),
     "mtn_sched_request_pages": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, c_i64p]),
     "mtn_sched_request_output": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, c_i64p]),
+    "mtn_sched_fork": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, c_u32p, C.c_int64, C.c_float, C.c_int32]),
+    "mtn_sched_page_refcount": (C.c_int32, [C.c_void_p, C.c_uint32]),
+    "mtn_sched_tree_pages": (C.c_int, [C.c_void_p, c_u32p, c_i64p]),
     "mtn_sched_free_pages": (C.c_int64, [C.c_void_p]),
     "mtn_sched_cached_pages": (C.c_int64, [C.c_void_p]),
     "mtn_sched_num_active": (C.c_int32, [C.c_void_p]),

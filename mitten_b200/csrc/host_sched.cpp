@@ -34,6 +34,7 @@ struct Req {
   float temperature = 1.0f;
   int32_t max_new_tokens = 512;
   std::vector<uint64_t> locked_nodes;
+  bool forked = false;  // holds its parent's prompt pages from mtn_sched_fork
 };
 
 }  // namespace
@@ -192,7 +193,12 @@ struct Sched {
     while (used < budget && !waiting.empty()) {
       Req* r = waiting.front();
       const int64_t input_len = static_cast<int64_t>(r->input_ids.size());
-      const int64_t pages_needed = (input_len + ps - 1) / ps;
+      // A fork already holds its parent's prompt pages: it needs the rest of
+      // its prompt's pages plus one for the copy of a shared partial page.
+      const int64_t pages_needed =
+          r->forked ? (input_len + ps - 1) / ps - static_cast<int64_t>(r->kv_pages.size()) +
+                          ((r->cached_len % ps) != 0 ? 1 : 0)
+                    : (input_len + ps - 1) / ps;
       if (pool.free_pages() < pages_needed) {
         std::vector<uint32_t> freed;
         if (refcount()) {
@@ -209,20 +215,23 @@ struct Sched {
         if (pool.free_pages() < pages_needed) break;  // cannot admit yet
       }
       waiting.pop_front();
-      int64_t cached = 0;
-      std::vector<uint32_t> pages;
-      std::vector<uint64_t> nodes;
-      // A fully cached prompt would leave nothing to compute and no logits
-      // to sample from; the refcount engine always recomputes the last token.
-      const int64_t match_n = refcount() ? std::max<int64_t>(0, input_len - 1) : input_len;
-      radix.match_prefix(r->input_ids.data(), match_n, &cached, &pages, &nodes);
-      r->cached_len = cached;
-      r->device_len = cached;
-      r->locked_nodes = nodes;
-      r->kv_pages = pages;
-      if (refcount())
-        for (uint32_t p : r->kv_pages) pool.retain(p);
-      while (static_cast<int64_t>(r->kv_pages.size()) < pages_needed) {
+      if (!r->forked) {
+        int64_t cached = 0;
+        std::vector<uint32_t> pages;
+        std::vector<uint64_t> nodes;
+        // A fully cached prompt would leave nothing to compute and no logits
+        // to sample from; the refcount engine always recomputes the last token.
+        const int64_t match_n = refcount() ? std::max<int64_t>(0, input_len - 1) : input_len;
+        radix.match_prefix(r->input_ids.data(), match_n, &cached, &pages, &nodes);
+        r->cached_len = cached;
+        r->device_len = cached;
+        r->locked_nodes = nodes;
+        r->kv_pages = pages;
+        if (refcount())
+          for (uint32_t p : r->kv_pages) pool.retain(p);
+      }
+      const int64_t prompt_pages = (input_len + ps - 1) / ps;
+      while (static_cast<int64_t>(r->kv_pages.size()) < prompt_pages) {
         uint32_t p = 0;
         if (!pool.allocate(r->id >> 32, r->id, &p)) break;  // unreachable after the check above
         r->kv_pages.push_back(p);
@@ -254,6 +263,42 @@ struct Sched {
       pool.release(old, nullptr);
     }
     return true;
+  }
+
+  // A new request whose prompt is the parent's whole prompt plus `suffix`,
+  // holding (one more reference each) the parent's pages of that prompt,
+  // its partially filled last page included; its first write into that
+  // page makes it a private copy (prepare_write).  Refcount mode only.
+  int fork(uint64_t parent_id, uint64_t child_id, const uint32_t* suffix, int64_t n_suffix, float temperature,
+           int32_t max_new_tokens) {
+    MTN_CHECK_ARG(refcount(), "mtn_sched_fork: needs MTN_SCHED_REFCOUNT (the reference frees shared pages)");
+    auto it = reqs.find(parent_id);
+    MTN_CHECK_ARG(it != reqs.end(), "mtn_sched_fork: unknown parent %llu", (unsigned long long)parent_id);
+    MTN_CHECK_ARG(reqs.find(child_id) == reqs.end(), "mtn_sched_fork: duplicate request id %llu",
+                  (unsigned long long)child_id);
+    Req* par = it->second.get();
+    const int64_t n_prompt = static_cast<int64_t>(par->input_ids.size());
+    const int64_t ps = cfg.page_size;
+    MTN_CHECK_ARG((par->state == MTN_REQ_DECODING || par->state == MTN_REQ_PREFILLING) && par->device_len >= n_prompt &&
+                      static_cast<int64_t>(par->kv_pages.size()) >= (n_prompt + ps - 1) / ps,
+                  "mtn_sched_fork: parent %llu has not finished its prompt or no longer holds its pages",
+                  (unsigned long long)parent_id);
+    MTN_CHECK_ARG(suffix != nullptr && n_suffix > 0 && n_prompt + n_suffix < (int64_t(1) << 31),
+                  "mtn_sched_fork: the suffix must hold at least one token");
+    auto r = std::make_unique<Req>();
+    r->id = child_id;
+    r->input_ids = par->input_ids;
+    r->input_ids.insert(r->input_ids.end(), suffix, suffix + n_suffix);
+    r->temperature = temperature;
+    r->max_new_tokens = max_new_tokens;
+    r->cached_len = n_prompt;
+    r->device_len = n_prompt;
+    r->forked = true;
+    r->kv_pages.assign(par->kv_pages.begin(), par->kv_pages.begin() + (n_prompt + ps - 1) / ps);
+    for (uint32_t p : r->kv_pages) pool.retain(p);
+    waiting.push_back(r.get());
+    reqs.emplace(child_id, std::move(r));
+    return MTN_OK;
   }
 
   int schedule(mtn_batch_view* out, int32_t* has_batch) {
@@ -525,6 +570,30 @@ int mtn_sched_request_output(const mtn_sched* s, uint64_t req_id, uint32_t* out,
                 "mtn_sched_request_output: buffer too small (%zu tokens)", v.size());
   std::copy(v.begin(), v.end(), out);
   *n_out = static_cast<int64_t>(v.size());
+  return MTN_OK;
+}
+
+int mtn_sched_fork(mtn_sched* s, uint64_t parent_id, uint64_t child_id, const uint32_t* suffix, int64_t n_suffix,
+                   float temperature, int32_t max_new_tokens) {
+  MTN_CHECK_ARG(s, "mtn_sched_fork: null scheduler");
+  return s->impl.fork(parent_id, child_id, suffix, n_suffix, temperature, max_new_tokens);
+}
+
+int32_t mtn_sched_page_refcount(const mtn_sched* s, uint32_t page) {
+  if (!s || page >= static_cast<uint64_t>(s->impl.pool.num_pages)) return -1;
+  return s->impl.pool.in_use[page] ? s->impl.pool.refcnt[page] : 0;
+}
+
+int mtn_sched_tree_pages(const mtn_sched* s, uint32_t* pages, int64_t* n_pages) {
+  MTN_CHECK_ARG(s && n_pages, "mtn_sched_tree_pages: null argument");
+  const mtn::RadixTree& t = s->impl.radix;
+  std::vector<uint32_t> all;
+  for (size_t i = 0; i < t.entries.size(); ++i)
+    if (t.occupied[i]) all.insert(all.end(), t.entries[i].kv_pages.begin(), t.entries[i].kv_pages.end());
+  MTN_CHECK_ARG(static_cast<int64_t>(all.size()) <= *n_pages && (pages || all.empty()),
+                "mtn_sched_tree_pages: buffer too small (%zu pages)", all.size());
+  std::copy(all.begin(), all.end(), pages);
+  *n_pages = static_cast<int64_t>(all.size());
   return MTN_OK;
 }
 

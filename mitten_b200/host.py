@@ -249,6 +249,22 @@ class Scheduler:
         L.check(L.lib().mtn_sched_request_output(self._h, req_id, buf, C.byref(cnt)))
         return list(buf[:cnt.value])
 
+    def fork(self, parent_id: int, child_id: int, suffix, temperature: float = 0.0, max_new_tokens: int = 512) -> None:
+        """Queue child_id = parent's prompt + suffix, sharing the parent's prompt pages (refcount mode)."""
+        a, p = _u32(suffix)
+        L.check(L.lib().mtn_sched_fork(self._h, parent_id, child_id, p, len(a), temperature, max_new_tokens))
+
+    def page_refcount(self, page: int) -> int:
+        return int(L.lib().mtn_sched_page_refcount(self._h, page))
+
+    def tree_pages(self) -> list[int]:
+        # the tree lists exactly cached_pages() pages
+        cap = max(1, self.cached_pages())
+        buf = (C.c_uint32 * cap)()
+        cnt = C.c_int64(cap)
+        L.check(L.lib().mtn_sched_tree_pages(self._h, buf, C.byref(cnt)))
+        return list(buf[:cnt.value])
+
     def free_pages(self) -> int:
         return int(L.lib().mtn_sched_free_pages(self._h))
 
