@@ -292,12 +292,13 @@ def run_ours(args, rank, world, local, pg):
     for i in range(args.warmup):  # also configures the kernel before capture
         step(i)
     torch.cuda.synchronize()
-    graphs = []
-    for j in range(args.steps):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+    # All K timed steps in one CUDA graph: consecutive decode launches keep
+    # their programmatic-dependent-launch edges (the next step's CTAs start
+    # their prologue on SMs the previous step frees, then wait for it).
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for j in range(args.steps):
             step(args.warmup + j)
-        graphs.append(g)
     torch.cuda.synchronize()
     barrier(pg)
     stream = torch.cuda.current_stream()
@@ -305,14 +306,20 @@ def run_ours(args, rank, world, local, pg):
     with ClockSampler(local) as clk:
         barrier(pg)
         ev0.record(stream)
-        for j in range(args.steps):
-            graphs[j].replay()
+        graph.replay()
         ev1.record(stream)
         torch.cuda.synchronize()
     barrier(pg)
     t_step = ev0.elapsed_time(ev1) * 1e-3
+    del graph
     # The same steps again, one at a time after an L2-flushing write, for
     # comparison (their appends rewrite the same rows with the same values).
+    graphs = []
+    for j in range(args.steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(args.warmup + j)
+        graphs.append(g)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     for j in range(args.steps):
         flush.zero_()
@@ -342,9 +349,9 @@ def run_ours(args, rank, world, local, pg):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q/K/V)",
-        "config": workload_config({"parallelism": f"replicas{world}",
-                                   "step": "one fused append+decode launch per step, CUDA graphs replayed "
-                                           "back to back between two events"}),
+        "config": workload_config(),
+        "execution": {"replicas": world, "step": "one fused append+decode launch per step; the K timed steps "
+                                                  "captured in one CUDA graph, replayed between two events"},
         "kv_read_gbs": sum_over_ranks(pg, kv_bytes) / t_max / 1e9,
         "decode_us_per_step": 1e6 * t_step / args.steps,
         "per_step_l2_flushed_us": 1e6 * t_flushed / args.steps,
@@ -355,7 +362,9 @@ def run_ours(args, rank, world, local, pg):
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
                 "path": "per step: Q/K/V/seq_lens packed in one pinned host buffer -> one H2D copy -> "
-                        "mtn_paged_decode (C ABI) -> D2H output, steps back to back, batches rotating as above"},
+                        "mtn_paged_decode (C ABI) -> D2H output; step i+1's H2D and step i-1's D2H overlap "
+                        "step i's kernel (upload/download streams, double-buffered staging), batches rotating "
+                        "as above"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
         "kv_append_bulk": extras["append"],
@@ -438,7 +447,14 @@ def run_append_and_copy(st, pool, device, stream) -> dict:
 
 
 def run_e2e(args, st, pool, ws, device, stream, total_steps):
-    """Append + decode through the C ABI with host inputs/outputs copied inside the timed region."""
+    """Append + decode through the C ABI with host inputs/outputs copied inside the timed region.
+
+    Each step's Q, new K/V and seq_lens are packed in one pinned host buffer and copied in with one
+    H2D copy; O comes back with one D2H copy.  The copies of neighbouring steps overlap the kernel:
+    step i+1's H2D (on an upload stream) and step i-1's D2H (on a download stream) run while step
+    i's kernel runs, through two device staging buffers and two output buffers, ordered by events.
+    All K steps (copies and kernels) are captured in one CUDA graph and replayed between two events.
+    """
     import ctypes as C
 
     import torch
@@ -452,10 +468,6 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
     q_h = torch.randn((N_SEQS, HQ, D), generator=gen).to(torch.bfloat16)
     k_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16)
     v_h = torch.randn((N_SEQS, HKV, D), generator=gen).to(torch.bfloat16)
-    o_h = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory()
-    # Each step's inputs (Q, new K, new V, seq_lens) packed in one pinned
-    # staging buffer, so a step is one host->device copy, the call and one
-    # device->host copy of O.
     parts = [q_h.view(torch.uint8).reshape(-1), k_h.view(torch.uint8).reshape(-1), v_h.view(torch.uint8).reshape(-1)]
     offs = np.cumsum([0] + [x.numel() for x in parts]).tolist()  # byte offsets (multiples of 16)
     nbytes = offs[-1] + N_SEQS * 4
@@ -466,45 +478,78 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
             buf[o:o + x.numel()].copy_(x)
         buf[offs[3]:].copy_(torch.from_numpy(step_inputs(st, i, device)[1]).view(torch.uint8))
         stage_h.append(buf)
-    stage_d = torch.empty(nbytes, dtype=torch.uint8, device=device)
-    base = stage_d.data_ptr()
-    q_p, k_p, v_p, l_p = (base + o for o in offs)
-    o_d = torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device)
+    o_h = [torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory() for _ in range(total_steps)]
+    stage_d = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(2)]
+    o_d = [torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16, device=device) for _ in range(2)]
     scale = D ** -0.5
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
-    def one(i):
+    def call(i, buf):
         sp = int(torch.cuda.current_stream().cuda_stream)
         b = st["batches"][step_batch(st, i)]
-        stage_d.copy_(stage_h[i], non_blocking=True)
+        base = stage_d[buf].data_ptr()
+        q_p, k_p, v_p, l_p = (base + o for o in offs)
         _lib.check(lib.mtn_paged_decode(C.byref(pool.layout), 0, q_p, _lib.MTN_DTYPE_BF16,
-                                        o_d.data_ptr(), _lib.MTN_DTYPE_BF16, k_p, v_p,
+                                        o_d[buf].data_ptr(), _lib.MTN_DTYPE_BF16, k_p, v_p,
                                         _lib.MTN_DTYPE_BF16, N_SEQS, HQ, st["indptr"].data_ptr(),
                                         b["indices"].data_ptr(), l_p, scale, 0, ws.buf.data_ptr(),
                                         ws.nbytes, sp))
-        o_h.copy_(o_d, non_blocking=True)
+
+    def pipeline(first, n):
+        """Steps first .. first+n-1 on the current (compute) stream with overlapped copies."""
+        comp = torch.cuda.current_stream()
+        ev_in = [torch.cuda.Event() for _ in range(n)]
+        ev_k = [torch.cuda.Event() for _ in range(n)]
+        ev_out = [torch.cuda.Event() for _ in range(n)]
+        up.wait_stream(comp)
+        down.wait_stream(comp)
+
+        def upload(j):
+            with torch.cuda.stream(up):
+                if j >= 2:
+                    up.wait_event(ev_k[j - 2])  # kernel j-2 has read staging buffer j % 2
+                stage_d[j % 2].copy_(stage_h[first + j], non_blocking=True)
+                ev_in[j].record(up)
+
+        upload(0)
+        if n > 1:
+            upload(1)
+        for j in range(n):
+            comp.wait_event(ev_in[j])
+            if j >= 2:
+                comp.wait_event(ev_out[j - 2])  # output buffer j % 2 has been downloaded
+            call(first + j, j % 2)
+            ev_k[j].record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(ev_k[j])
+                o_h[first + j].copy_(o_d[j % 2], non_blocking=True)
+                ev_out[j].record(down)
+            if j + 2 < n:
+                upload(j + 2)
+        comp.wait_stream(up)
+        comp.wait_stream(down)
 
     # the pool already holds the device arm's appends: these steps rewrite the same positions
     first = total_steps - steps
-    for i in range(min(3, steps)):
-        one(first + i)
+    pipeline(first, min(3, steps))
     torch.cuda.synchronize()
-    graphs = []
-    for j in range(steps):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            one(first + j)
-        graphs.append(g)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        pipeline(first, steps)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for j in range(steps):
-        graphs[j].replay()
+    g.replay()
     b.record(stream)
     b.synchronize()
     t = a.elapsed_time(b) * 1e-3
-    del graphs
+    del g
+    # the last step's output reached the host
+    ref_out = o_d[(steps - 1) % 2].cpu()
+    if not torch.equal(o_h[first + steps - 1], ref_out):
+        raise SystemExit("e2e: the downloaded output differs from the device output")
     h2d = nbytes
-    d2h = o_h.numel() * o_h.element_size()
+    d2h = o_h[0].numel() * o_h[0].element_size()
     return {"t": t, "steps": steps, "h2d": h2d, "d2h": d2h}
 
 
@@ -563,7 +608,7 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": done,
         "warmup": args.warmup, "ms_per_step": 1e3 * t / max(done, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V)",
-        "config": workload_config({"parallelism": "host cores"}), "impl": "reference",
+        "config": workload_config(), "execution": {"host_cores": cores}, "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{done} of {args.steps} requested steps of the full config-2 batch "
                                    f"(cap {args.ref_seconds:.0f} s); the Rust reference cannot be built here"},

@@ -123,7 +123,16 @@ enum {
   /* mtn_paged_prefill only: run the one-query-tile kernel even where the
    * two-tile kernel applies (head_dim <= 128 and at least two query tiles
    * per SM); same results, for comparison. */
-  MTN_ATTN_PREFILL_ONE_TILE = 1u << 1
+  MTN_ATTN_PREFILL_ONE_TILE = 1u << 1,
+  /* Split the tensor-core operands Q and P into bf16 hi + lo pairs
+   * (hi = bf16(x), lo = bf16(x - hi)) and accumulate both products in f32,
+   * so f32 queries and the softmax weights keep about 16 significant bits
+   * (the reference computes q.k and P.v in f32, model.rs:413-416).  K and
+   * V are the pool's bf16 values either way.  Decode: no extra tensor-core
+   * work (the lo rows fill the padding of the 16-wide query-head operand).
+   * Prefill: twice the tensor-core work; head_dim <= 128; always the
+   * one-query-tile kernel. */
+  MTN_ATTN_SPLIT_BF16 = 1u << 2
 };
 
 /* Per-token pool slot for a batch (Batch -> slot map; batch.rs:7-36):
@@ -172,7 +181,14 @@ MTN_API int mtn_kv_gather(const mtn_kv_layout* pool, int32_t layer,
  *   q head h uses kv head h / (num_q_heads / num_kv_heads) (model.rs:398-408),
  *   at most 8 query heads per kv head.  scale multiplies q.k (model.rs:298, 413).
  *   workspace: mtn_paged_decode_workspace_bytes(...) bytes, zeroed once before
- *   first use (calls leave it reusable); concurrent calls must not share one.
+ *   first use (calls leave it reusable; after a call that reports a device
+ *   timeout, mtn_device_error code 4, zero it again); concurrent calls must
+ *   not share one.
+ *   Programmatic dependent launch: a decode launch lets the next kernel of
+ *   its stream start early, and itself may start while the previous kernel
+ *   of the stream finishes; before waiting for that kernel it reads only
+ *   kv_indptr and seq_lens, which therefore must not be written by a kernel
+ *   that itself allows early launch (no kernel of this library writes them).
  *   The pool memory must have been zero-initialised (mtn_kv_pool_alloc does). */
 MTN_API size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                                         int32_t head_dim);
@@ -193,9 +209,11 @@ MTN_API int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer,
  * without the workspace: the scratch is a static 8 MiB device array inside
  * this library, present on every GPU that loads it until the process exits.
  * Batches needing more scratch than that (mtn_paged_decode_workspace_bytes
- * > 8 MiB: on a 148-SM B200, more than about 1.4 million sequence x kv-head
- * pairs at head_dim 64, or 0.7 million at head_dim 256) are rejected with
- * MTN_EINVAL.  The first call on a device looks up the array's device
+ * > 8 MiB) are rejected with MTN_EINVAL: the fixed part is
+ * ctas x 32 x (head_dim + 2) x 4 bytes (ctas = SMs x 2 at head_dim 64, SMs
+ * otherwise) and each sequence x kv-head pair adds 4 bytes, so a 148-SM B200
+ * takes up to about 1.47 million pairs at head_dim 64 or 128 and 0.87
+ * million at head_dim 256.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress with that device current), so make that
  * first call before any stream capture.  Every call on a device shares the
  * one array and it keeps the previous call's contents; the part that must
@@ -210,7 +228,9 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
                      float scale, uint32_t flags, void* stream);
 
 /* Chunked-prefill attention over paged KV (tcgen05 / TMEM tensor cores).
- *   q: [total_q][num_q_heads][head_dim] bf16; o: same shape (o_dtype).
+ *   q: [total_q][num_q_heads][head_dim] (q_dtype: bf16, or f32 rounded to
+ *   bf16 -- or split into bf16 hi + lo with MTN_ATTN_SPLIT_BF16 -- on
+ *   load); o: same shape (o_dtype).
  *   Sequence r owns query rows qo_indptr[r] .. qo_indptr[r+1]; those are its
  *   LAST q_len = qo_indptr[r+1]-qo_indptr[r] tokens out of seq_lens[r]
  *   (their K/V already appended), so query i sits at position
@@ -227,7 +247,7 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
 MTN_API size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                                          int32_t num_kv_heads, int32_t head_dim);
 MTN_API int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer,
-                      const void* q, void* o, int32_t o_dtype,
+                      const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
                       int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                       const int32_t* qo_indptr, const int32_t* kv_indptr,
                       const int32_t* kv_indices, const int32_t* seq_lens,
@@ -237,6 +257,17 @@ MTN_API int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer,
 /* Greedy sampling on the device (scheduler.rs:186-199 temperature <= 0):
  * out[r] = index of the first strict maximum of logits row r. */
 MTN_API int mtn_argmax_rows(const float* logits, int64_t n_rows, int64_t vocab, int32_t* out, void* stream);
+
+/* sample_token (scheduler.rs:186-223) for every row on the device, with
+ * row r's temperature temperatures[r] (device array): greedy first strict
+ * maximum when <= 0; otherwise the reference's pick -- hash of the first
+ * 100 logits' bit patterns -> rand in [0, 1), exp(logit / t) in f32, their
+ * sum and running sum in index order, first index reaching rand -- with the
+ * same f32 operations in the same order.  workspace: device memory of
+ * mtn_sample_rows_workspace_bytes(n_rows, vocab) bytes (any contents). */
+MTN_API size_t mtn_sample_rows_workspace_bytes(int64_t n_rows, int64_t vocab);
+MTN_API int mtn_sample_rows(const float* logits, const float* temperatures, int64_t n_rows, int64_t vocab,
+                            int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Host mirror: page allocator (kv_pool.rs:4-69) + refcount extension       */
@@ -351,6 +382,7 @@ typedef struct {
   int64_t n_cow;               /* copy-on-write page pairs to run first   */
   const int32_t* cow_src;
   const int32_t* cow_dst;
+  const float* temperatures;   /* [n_reqs] SamplingParams::temperature     */
 } mtn_batch_view;
 
 MTN_API int mtn_sched_create(const mtn_sched_config* cfg, mtn_sched** out);

@@ -16,6 +16,7 @@ MTN_OK, MTN_EINVAL, MTN_ENOMEM, MTN_ECUDA, MTN_ETIMEOUT, MTN_EDEVICE = range(6)
 MTN_DTYPE_BF16, MTN_DTYPE_F32 = 0, 1
 MTN_ATTN_PHANTOM_ZERO_SLOT = 1
 MTN_ATTN_PREFILL_ONE_TILE = 2
+MTN_ATTN_SPLIT_BF16 = 4
 MTN_SCHED_REFERENCE, MTN_SCHED_REFCOUNT = 0, 1
 MTN_REQ_WAITING, MTN_REQ_PREFILLING, MTN_REQ_DECODING, MTN_REQ_DONE, MTN_REQ_ABORTED = range(5)
 MTN_PHASE_PREFILL_ONLY, MTN_PHASE_DECODE_ONLY, MTN_PHASE_MIXED = range(3)
@@ -67,6 +68,7 @@ class BatchView(C.Structure):
         ("n_cow", C.c_int64),
         ("cow_src", c_i32p),
         ("cow_dst", c_i32p),
+        ("temperatures", c_f32p),
     ]
 
 
@@ -97,10 +99,14 @@ SIGNATURES: dict[str, tuple] = {
                                            C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p]),
     "mtn_paged_prefill_workspace_bytes": (C.c_size_t, [C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int32]),
-    "mtn_paged_prefill": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+    "mtn_paged_prefill": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
+                                    C.c_int32,
                                     C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_int32, C.c_float, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p]),
     "mtn_argmax_rows": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),
+    "mtn_sample_rows_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int64]),
+    "mtn_sample_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_size_t,
+                                  C.c_void_p]),
     # host mirror: page pool
     "mtn_page_pool_create": (C.c_int, [C.c_int64, C.c_int32, C.POINTER(C.c_void_p)]),
     "mtn_page_pool_destroy": (None, [C.c_void_p]),

@@ -144,6 +144,14 @@ __device__ __forceinline__ uint32_t f2_to_bf2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// bf16x2 of the rounding remainders (a - hi.lo, b - hi.hi) of two f32 values
+// whose bf16 pair (round to nearest even) is `hi`: hi + lo carries about 16
+// significant bits of each value.
+__device__ __forceinline__ uint32_t bf2_residual(uint32_t hi, float a, float b) {
+  const float2 h = bf2_to_f2(hi);
+  return f2_to_bf2(a - h.x, b - h.y);
+}
+
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -231,7 +231,13 @@ __device__ __forceinline__ int64_t cta_of(int64_t x, int64_t U, int64_t C) {
   return min(C - 1, ((x + 1) * C - 1) / U);
 }
 
-template <int D, int NREP>
+// PREC (MTN_ATTN_SPLIT_BF16): Q and P enter the tensor cores as bf16 hi +
+// lo pairs, hi = bf16(x) and lo = bf16(x - hi), so each product carries
+// about 16 mantissa bits of its f32 operand instead of 8.  N = 16 holds at
+// most 8 query heads, so the lo rows ride in rows 8..15 of the same Q^T and
+// P^T operands: S^T columns h and h + 8 (and O^T columns h and h + 8) are
+// the hi and lo products of head h, summed in f32 -- no extra MMA.
+template <int D, int NREP, bool PREC>
 __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ DecodeParams p) {
@@ -258,6 +264,12 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int tid = threadIdx.x;
   const int64_t cta = blockIdx.x;
 
+  // Programmatic dependent launch: the next kernel of the stream (the next
+  // decode launch, the next layer's or step's) may start its own prologue on
+  // SMs this launch frees; it waits for this grid to finish (griddepcontrol
+  // .wait below) before it reads or writes anything this grid touches.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   // TMEM first.  Measured with %globaltimer on B200: the second CTA of an SM
   // started only once the first had allocated TMEM and given up its
   // allocation permit (2.5 us late when that came after the metadata scan,
@@ -280,11 +292,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     const int T = (len + kTile - 1) / kTile;
     if (s == sb) len_first = len;
     mine += T;
-    if (T == 0 && s % static_cast<int64_t>(gridDim.x) == cta) {
-      // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
-      const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
-      for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
-    }
   }
   int64_t incl = mine;
 #pragma unroll
@@ -332,6 +339,22 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_base_s;
+  // Up to here the CTA read only the batch metadata (seq_lens, kv_indptr),
+  // which no decode launch writes; it may have started while the previous
+  // kernel of the stream was still running (see launch_dependents above).
+  // Wait for that kernel before reading q, k_new/v_new, K/V pages or writing
+  // o, the pool or the workspace.  (A kernel that does not allow early
+  // launch has finished before this grid starts: then this returns at once.)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int s = sb; s < se; ++s) {
+    if (s % static_cast<int64_t>(gridDim.x) != cta) continue;
+    const int len = seq_len_of(p, s);
+    if ((len + kTile - 1) / kTile == 0) {
+      // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
+      const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
+      for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
+    }
+  }
   // Uniform over the CTA.  The bad start cannot happen for consistent metadata.
   const bool bad_start = n_local > 0 && (*start_s < 0 || *start_s >= p.n_seqs);
   if (n_local == 0 || bad_start) {
@@ -448,8 +471,16 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
               const float* src = static_cast<const float*>(p.q) + (static_cast<int64_t>(qrow) + r) * D + c * 8;
               const float4 a = *reinterpret_cast<const float4*>(src);
               const float4 b2 = *reinterpret_cast<const float4*>(src + 4);
-              *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+              const uint4 hi =
                   make_uint4(f2_to_bf2(a.x, a.y), f2_to_bf2(a.z, a.w), f2_to_bf2(b2.x, b2.y), f2_to_bf2(b2.z, b2.w));
+              *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = hi;
+              if constexpr (PREC) {
+                // row r + 8: the bf16 remainders (r + 8 has the same swizzle phase as r)
+                const uint4 lo = make_uint4(bf2_residual(hi.x, a.x, a.y), bf2_residual(hi.y, a.z, a.w),
+                                            bf2_residual(hi.z, b2.x, b2.y), bf2_residual(hi.w, b2.z, b2.w));
+                *reinterpret_cast<uint4*>(q_s + (c >> 3) * (kN * 128) + (r + 8) * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+                    lo;
+              }
             }
             fence_proxy_async_shared();
             __syncwarp();
@@ -727,6 +758,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       tc::fence_after_sync();
       float sv[16];
       tmem_ld16(lane_addr + C::kTmemS + (i & 1) * kN, sv);
+      if (PREC && p.q_f32) {
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) sv[h] += sv[h + 8];  // K.Q_hi + K.Q_lo
+      }
       const bool valid = w.j * kTile + t < w.len;
       bool need = false;
 #pragma unroll
@@ -776,7 +811,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             float ov[16];
             tmem_ld16(lane_addr + o_col + mb * kN, ov);
 #pragma unroll
-            for (int h = 0; h < NREP; ++h) ov[h] *= alpha[h];
+            for (int h = 0; h < NREP; ++h) {
+              ov[h] *= alpha[h];
+              if constexpr (PREC) ov[h + 8] *= alpha[h];
+            }
             tmem_st16(lane_addr + o_col + mb * kN, ov);
           }
           tc::tmem_st_wait();
@@ -793,7 +831,11 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
 #pragma unroll
         for (int h = 0; h < NREP; ++h) {
           const int off = sub * (kN * 128) + h * 128 + ((((col >> 3) ^ (h & 7))) << 4) + (col & 7) * 2;
-          *reinterpret_cast<__nv_bfloat16*>(p_s + (i & 1) * C::kPBytes + off) = __float2bfloat16_rn(sv[h]);
+          const __nv_bfloat16 hi = __float2bfloat16_rn(sv[h]);
+          *reinterpret_cast<__nv_bfloat16*>(p_s + (i & 1) * C::kPBytes + off) = hi;
+          if constexpr (PREC)  // row h + 8: the remainder (same swizzle phase)
+            *reinterpret_cast<__nv_bfloat16*>(p_s + (i & 1) * C::kPBytes + off + 8 * 128) =
+                __float2bfloat16_rn(sv[h] - __bfloat162float(hi));
         }
       }
       fence_proxy_async_shared();
@@ -807,7 +849,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform for tcgen05.ld
         float ov[D / C::kMO][16];
 #pragma unroll
-        for (int mb = 0; mb < D / C::kMO; ++mb) tmem_ld16(lane_addr + o_col + mb * kN, ov[mb]);
+        for (int mb = 0; mb < D / C::kMO; ++mb) {
+          tmem_ld16(lane_addr + o_col + mb * kN, ov[mb]);
+          if constexpr (PREC) {
+#pragma unroll
+            for (int h = 0; h < NREP; ++h) ov[mb][h] += ov[mb][h + 8];  // V.P_hi + V.P_lo
+          }
+        }
         tc::fence_before_sync();
         tc::mbar_arrive(&bars[kOFree0 + (seg & 1)]);  // O^T buffer reusable two segments on
 #pragma unroll
@@ -985,10 +1033,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
 }
 
-template <int D, int NREP>
+template <int D, int NREP, bool PREC>
 int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm, cudaStream_t stream) {
   using C = DCfg<D>;
-  auto kern = paged_decode_kernel<D, NREP>;
+  auto kern = paged_decode_kernel<D, NREP, PREC>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -997,25 +1045,43 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
                  "cudaFuncSetAttribute(decode)");
     configured[dev] = true;
   }
-  const int grid = sm_count() * C::kCtasPerSm;
-  kern<<<grid, kThreads, C::kSmem, stream>>>(tkv, tq, prm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count() * C::kCtasPerSm);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  // Programmatic dependent launch: this grid may begin while the previous
+  // kernel of the stream finishes, if that kernel allows it (decode launches
+  // do); the kernel waits for it before touching its data.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MTN_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tkv, tq, prm), "cudaLaunchKernelEx(paged_decode_kernel)");
   return check_launch("paged_decode_kernel");
 }
 
-template <int D>
+template <int D, bool PREC>
 int dispatch_nrep(int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm,
                   cudaStream_t stream) {
   switch (nrep) {
-    case 1: return launch_decode<D, 1>(tkv, tq, prm, stream);
-    case 2: return launch_decode<D, 2>(tkv, tq, prm, stream);
-    case 3: return launch_decode<D, 3>(tkv, tq, prm, stream);
-    case 4: return launch_decode<D, 4>(tkv, tq, prm, stream);
-    case 5: return launch_decode<D, 5>(tkv, tq, prm, stream);
-    case 6: return launch_decode<D, 6>(tkv, tq, prm, stream);
-    case 7: return launch_decode<D, 7>(tkv, tq, prm, stream);
-    case 8: return launch_decode<D, 8>(tkv, tq, prm, stream);
+    case 1: return launch_decode<D, 1, PREC>(tkv, tq, prm, stream);
+    case 2: return launch_decode<D, 2, PREC>(tkv, tq, prm, stream);
+    case 3: return launch_decode<D, 3, PREC>(tkv, tq, prm, stream);
+    case 4: return launch_decode<D, 4, PREC>(tkv, tq, prm, stream);
+    case 5: return launch_decode<D, 5, PREC>(tkv, tq, prm, stream);
+    case 6: return launch_decode<D, 6, PREC>(tkv, tq, prm, stream);
+    case 7: return launch_decode<D, 7, PREC>(tkv, tq, prm, stream);
+    case 8: return launch_decode<D, 8, PREC>(tkv, tq, prm, stream);
     default: return set_error(MTN_EINVAL, "paged decode: query heads per kv head %d not in [1,8]", nrep);
   }
+}
+
+template <int D>
+int dispatch_prec(bool prec, int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm,
+                  cudaStream_t stream) {
+  return prec ? dispatch_nrep<D, true>(nrep, tkv, tq, prm, stream) : dispatch_nrep<D, false>(nrep, tkv, tq, prm, stream);
 }
 
 int decode_ctas(int head_dim) {
@@ -1110,10 +1176,11 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   prm.err = mtn::device_error_ptr();
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
+  const bool prec = (flags & MTN_ATTN_SPLIT_BF16) != 0;
   switch (D) {
-    case 64: return mtn::dispatch_nrep<64>(nrep, tkv, tq, prm, s);
-    case 128: return mtn::dispatch_nrep<128>(nrep, tkv, tq, prm, s);
-    default: return mtn::dispatch_nrep<256>(nrep, tkv, tq, prm, s);
+    case 64: return mtn::dispatch_prec<64>(prec, nrep, tkv, tq, prm, s);
+    case 128: return mtn::dispatch_prec<128>(prec, nrep, tkv, tq, prm, s);
+    default: return mtn::dispatch_prec<256>(prec, nrep, tkv, tq, prm, s);
   }
 }
 

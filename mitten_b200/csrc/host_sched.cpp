@@ -54,6 +54,7 @@ struct Sched {
   std::vector<uint64_t> v_ids;
   std::vector<uint32_t> v_input;
   std::vector<int32_t> v_pos, v_qo, v_kvp, v_kvi, v_len, v_cow_src, v_cow_dst;
+  std::vector<float> v_temp;
 
   Sched(const mtn_sched_config& c)
       : cfg(c), pool(c.num_pages, c.page_size), radix(c.page_size, c.radix_max_pages) {
@@ -350,6 +351,7 @@ struct Sched {
     out->n_cow = static_cast<int64_t>(v_cow_src.size());
     out->cow_src = v_cow_src.data();
     out->cow_dst = v_cow_dst.data();
+    out->temperatures = v_temp.data();
     *has_batch = 1;
     return MTN_OK;
   }
@@ -363,6 +365,7 @@ struct Sched {
     v_kvp.assign(1, 0);
     v_kvi.clear();
     v_len.clear();
+    v_temp.clear();
     for (Req* r : pre) {
       const int64_t start = r->device_len, end = r->device_len + r->extend_len;
       for (int64_t i = start; i < end; ++i) {
@@ -386,6 +389,7 @@ struct Sched {
     for (uint32_t p : r->kv_pages) v_kvi.push_back(static_cast<int32_t>(p));
     v_kvp.push_back(static_cast<int32_t>(v_kvi.size()));
     v_len.push_back(static_cast<int32_t>(kv_len));
+    v_temp.push_back(r->temperature);
   }
 
   // ------------------------------------------------------------ transition

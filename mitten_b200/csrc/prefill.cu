@@ -41,7 +41,8 @@ constexpr int kBM = 128;   // query rows per CTA (TMEM lanes)
 constexpr int kThreads = 192;
 
 struct PrefillParams {
-  const __nv_bfloat16* q;  // [total_q][hq][head_dim]
+  const void* q;  // [total_q][hq][head_dim], bf16 or (q_f32) f32
+  int q_f32;
   const int32_t* qo_indptr;
   const int32_t* kv_indptr;
   const int32_t* kv_indices;
@@ -93,11 +94,15 @@ struct PCfg {
   static constexpr int kOffMisc = kOffBar + 24 * 8;     // tmem base, abort flag
   static constexpr int kSmem = kOffMisc + 64 + 1024;    // + slack for 1024-byte alignment
   // TMEM columns: S[2] (P of a tile overwrites the first kBN/2 columns of its
-  // S buffer as bf16 pairs), the O accumulator, and Q as bf16 pairs.
+  // S buffer as bf16 pairs; with split operands the remainder of P takes the
+  // other kBN/2), the O accumulator, Q as bf16 pairs and, with split
+  // operands, the remainder of Q after it (head_dim <= 128 only).
   static constexpr int kTmemS = 0;
   static constexpr int kTmemO = 2 * kBN;
   static constexpr int kTmemQ = 2 * kBN + D;
+  static constexpr int kTmemQlo = kTmemQ + D / 2;
   static constexpr int kTmemCols = 512;
+  static constexpr bool kSplitFits = kTmemQlo + D / 2 <= kTmemCols;
   static_assert(kTmemQ + D / 2 <= kTmemCols, "TMEM budget");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
@@ -183,7 +188,7 @@ __device__ __forceinline__ void store_row_chunk(const PrefillParams& p, int64_t 
 // in TMEM once the previous P V is done: `odone_prev`), write P as bf16
 // pairs over the first kBN / 2 columns of the S buffer and arrive on
 // `pfull`.  Returns false (every lane of the warp) when a wait gave up.
-template <int D, int kBN>
+template <int D, int kBN, bool PREC = false>
 __device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off, uint32_t o_off, int key0, int pos0,
                                              int row_pos, float qscale, float& m_ref, float& l_run, uint64_t* sfull,
                                              uint32_t s_par, uint64_t* odone_prev, uint32_t o_par, uint64_t* pfull,
@@ -242,13 +247,19 @@ __device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off,
   }
   const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
   l_run = l_run * alpha + psum;
-  // P (bf16 pairs) over the first kBN/2 columns of this tile's S buffer.
+  // P (bf16 pairs) over the first kBN/2 columns of this tile's S buffer;
+  // with split operands its remainders over the other kBN/2.
 #pragma unroll
   for (int c = 0; c < kBN / 64; ++c) {
     uint32_t r[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) r[i] = f2_to_bf2(sv[c * 64 + 2 * i], sv[c * 64 + 2 * i + 1]);
     tc::tmem_st32(s_col + c * 32, r);
+    if constexpr (PREC) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = bf2_residual(r[i], sv[c * 64 + 2 * i], sv[c * 64 + 2 * i + 1]);
+      tc::tmem_st32(s_col + kBN / 2 + c * 32, r);
+    }
   }
   tc::tmem_st_wait();
   if (__any_sync(0xffffffffu, moved)) {
@@ -273,10 +284,14 @@ __device__ __forceinline__ bool softmax_tile(uint32_t lane_base, uint32_t s_off,
   return true;
 }
 
-template <int D>
+// PREC (MTN_ATTN_SPLIT_BF16): Q and P as bf16 hi + lo pairs, hi = bf16(x)
+// and lo = bf16(x - hi); S = Q_hi K^T + Q_lo K^T and O += P_hi V + P_lo V,
+// all accumulated in the same f32 TMEM columns (twice the MMAs).
+template <int D, bool PREC>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
+  static_assert(!PREC || C::kSplitFits, "split operands need head_dim <= 128");
   constexpr int kS = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -426,6 +441,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < D / 16; ++k)
           tc::mma_bf16_ts(tmem + C::kTmemS + (j & 1) * C::kBN, tmem + C::kTmemQ + k * 8,
                           b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, k > 0 ? 1u : 0u);
+        if constexpr (PREC) {
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k)
+            tc::mma_bf16_ts(tmem + C::kTmemS + (j & 1) * C::kBN, tmem + C::kTmemQlo + k * 8,
+                            b0 + (((k >> 2) * 1024 + (k & 3) * 32) >> 4), idS, 1u);
+        }
         tc::mma_commit(&bars[kSFull0 + (j & 1)]);
         tc::mma_commit(&bars[kKEmpty0 + st]);
         return true;
@@ -446,6 +467,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < C::kBN / 16; ++k)
           tc::mma_bf16_ts(tmem + C::kTmemO, tmem + C::kTmemS + (j & 1) * C::kBN + k * 8,
                           b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, (j > 0 || k > 0) ? 1u : 0u);
+        if constexpr (PREC) {
+#pragma unroll
+          for (int k = 0; k < C::kBN / 16; ++k)
+            tc::mma_bf16_ts(tmem + C::kTmemO, tmem + C::kTmemS + (j & 1) * C::kBN + C::kBN / 2 + k * 8,
+                            b0 + ((k * 2 * C::kGroupBytes) >> 4), idO, 1u);
+        }
         tc::mma_commit(&bars[kODone0 + (j & 1)]);
         tc::mma_commit(&bars[kVEmpty0 + st]);
       }
@@ -456,13 +483,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int row_pos = min(pos0 + row, last_pos);
     // Q row (bf16 pairs) into TMEM, every load in flight at once; rows past
-    // the chunk are zero.
+    // the chunk are zero.  f32 queries are rounded to bf16 here (and with
+    // split operands their remainders go to the second Q region).
     {
-      const uint4* qrow = reinterpret_cast<const uint4*>(
-          p.q + ((static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h) * D);
+      const int64_t qoff = ((static_cast<int64_t>(q0) + tile * kBM + row) * p.hq + h) * D;
       uint4 v[D / 8];
+      if (p.q_f32) {
+        const float4* qrow = reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + qoff);
+        float4 f[D / 4];
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) v[i] = row < nrows ? qrow[i] : make_uint4(0u, 0u, 0u, 0u);
+        for (int i = 0; i < D / 4; ++i) f[i] = row < nrows ? qrow[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i)
+          v[i] = make_uint4(f2_to_bf2(f[2 * i].x, f[2 * i].y), f2_to_bf2(f[2 * i].z, f[2 * i].w),
+                            f2_to_bf2(f[2 * i + 1].x, f[2 * i + 1].y), f2_to_bf2(f[2 * i + 1].z, f[2 * i + 1].w));
+        if constexpr (PREC) {
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t r[32];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int e = c * 8 + i;
+              r[4 * i] = bf2_residual(v[e].x, f[2 * e].x, f[2 * e].y);
+              r[4 * i + 1] = bf2_residual(v[e].y, f[2 * e].z, f[2 * e].w);
+              r[4 * i + 2] = bf2_residual(v[e].z, f[2 * e + 1].x, f[2 * e + 1].y);
+              r[4 * i + 3] = bf2_residual(v[e].w, f[2 * e + 1].z, f[2 * e + 1].w);
+            }
+            tc::tmem_st32(lane_base + C::kTmemQlo + c * 32, r);
+          }
+        }
+      } else {
+        const uint4* qrow = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + qoff);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) v[i] = row < nrows ? qrow[i] : make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (PREC) {  // bf16 queries: no remainder
+          uint32_t z[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) z[i] = 0u;
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) tc::tmem_st32(lane_base + C::kTmemQlo + c * 32, z);
+        }
+      }
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         uint32_t r[32];
@@ -482,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {  // j counts the range's tiles
-      ok = softmax_tile<D, C::kBN>(lane_base, C::kTmemS + (j & 1) * C::kBN, C::kTmemO, (ja + j) * C::kBN, pos0,
+      ok = softmax_tile<D, C::kBN, PREC>(lane_base, C::kTmemS + (j & 1) * C::kBN, C::kTmemO, (ja + j) * C::kBN, pos0,
                                    row_pos, p.qscale, m_ref, l_run, &bars[kSFull0 + (j & 1)], (j >> 1) & 1,
                                    &bars[kODone0 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, &bars[kPFull0 + (j & 1)],
                                    abort_flag, p.err, 30);
@@ -813,7 +874,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // Q row into shared memory: 16-byte chunk c of the row goes to block
         // c / 8, chunk (c % 8) ^ (row % 8) of the row's 128 bytes (the
         // 128-byte swizzle the descriptor names); rows past the chunk are zero.
-        const uint4* qrow = reinterpret_cast<const uint4*>(p.q + (qrow0 * p.hq + h) * D);
+        const uint4* qrow =
+            reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + (qrow0 * p.hq + h) * D);
         uint8_t* qs = smem + C::kOffQ + x * C::kQBytes + row * 128;
 #pragma unroll
         for (int b = 0; b < D / 64; ++b) {  // one 64-column block (8 chunks) at a time
@@ -830,7 +892,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       float m_ref = -INFINITY, l_run = 0.0f;
       bool ok = true;
       for (int j = 0; j < nx; ++j) {
-        ok = softmax_tile<D, C::kBN>(lane_base, C::kTmemS + x * C::kBN, C::kTmemO + x * D, j * C::kBN, pos0, row_pos,
+        ok = softmax_tile<D, C::kBN, false>(lane_base, C::kTmemS + x * C::kBN, C::kTmemO + x * D, j * C::kBN, pos0, row_pos,
                                      p.qscale, m_ref, l_run, &bars[qSFull0 + x], j & 1, &bars[qODone0 + x],
                                      (j - 1) & 1, &bars[qPFull0 + x], abort_flag, p.err, 70);
         if (!ok) break;
@@ -861,7 +923,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
 // --------------------------------------------------------------- host side
 
-template <int D>
+template <int D, bool PREC = false>
 int launch_prefill(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles, int n_seqs,
                    cudaStream_t stream) {
   using C = PCfg<D>;
@@ -869,12 +931,13 @@ int launch_prefill(const CUtensorMap& tkv, const PrefillParams& prm, int n_tiles
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    MTN_CUDA_TRY(cudaFuncSetAttribute(paged_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem),
+    MTN_CUDA_TRY(cudaFuncSetAttribute(paged_prefill_kernel<D, PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::kSmem),
                  "cudaFuncSetAttribute(prefill)");
     configured[dev] = true;
   }
   dim3 grid(n_tiles, prm.hq, prm.split ? n_seqs * kMaxPieces : n_seqs);
-  paged_prefill_kernel<D><<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
+  paged_prefill_kernel<D, PREC><<<grid, kThreads, C::kSmem, stream>>>(tkv, prm);
   return check_launch("paged_prefill_kernel");
 }
 
@@ -929,7 +992,8 @@ size_t mtn_paged_prefill_workspace_bytes(int32_t n_seqs, int64_t total_q, int32_
   return mtn::split_layout(n_seqs, total_q, num_q_heads, head_dim).bytes;
 }
 
-int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, void* o, int32_t o_dtype,
+int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                      int32_t o_dtype,
                       int32_t n_seqs, int64_t total_q, int32_t num_q_heads, const int32_t* qo_indptr,
                       const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens, int32_t max_q_len,
                       float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
@@ -939,6 +1003,7 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
   MTN_CHECK_ARG(total_q >= 0 && total_q < (int64_t(1) << 31), "mtn_paged_prefill: bad total_q");
   if (n_seqs == 0 || total_q == 0) return MTN_OK;
   MTN_CHECK_ARG(q && o && qo_indptr && kv_indptr && kv_indices && seq_lens, "mtn_paged_prefill: null pointer");
+  MTN_CHECK_ARG(q_dtype == MTN_DTYPE_BF16 || q_dtype == MTN_DTYPE_F32, "mtn_paged_prefill: bad q dtype");
   MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_prefill: bad o dtype");
   MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads <= 65535 && num_q_heads % pool->num_kv_heads == 0,
                 "mtn_paged_prefill: %d query heads not a multiple of %d kv heads", num_q_heads, pool->num_kv_heads);
@@ -949,11 +1014,14 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
                 "mtn_paged_prefill: page_size %d must be a multiple of 8 dividing %d", pool->page_size, bn);
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0,
                 "mtn_paged_prefill: q/o must be 16-byte aligned");
+  const bool prec = (flags & MTN_ATTN_SPLIT_BF16) != 0;
+  MTN_CHECK_ARG(!prec || D <= 128, "mtn_paged_prefill: MTN_ATTN_SPLIT_BF16 needs head_dim <= 128 (got %d)", D);
   CUtensorMap tkv;
   st = mtn::pool_tensor_map_paged(pool, &tkv);
   if (st != MTN_OK) return st;
   mtn::PrefillParams prm{};
-  prm.q = static_cast<const __nv_bfloat16*>(q);
+  prm.q = q;
+  prm.q_f32 = q_dtype == MTN_DTYPE_F32;
   prm.qo_indptr = qo_indptr;
   prm.kv_indptr = kv_indptr;
   prm.kv_indices = kv_indices;
@@ -988,9 +1056,13 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, v
     prm.ws_o = reinterpret_cast<float*>(w + wl.off_o);
   }
   auto s = static_cast<cudaStream_t>(stream);
+  if (prec) {
+    return D == 64 ? mtn::launch_prefill<64, true>(tkv, prm, n_tiles, n_seqs, s)
+                   : mtn::launch_prefill<128, true>(tkv, prm, n_tiles, n_seqs, s);
+  }
   // Many query tiles (at least two per SM): two tiles per CTA at head_dim
-  // <= 128, sharing every K/V tile.
-  if (!prm.split && D <= 128 && !(flags & MTN_ATTN_PREFILL_ONE_TILE) &&
+  // <= 128, sharing every K/V tile (bf16 queries).
+  if (!prm.split && D <= 128 && !prm.q_f32 && !(flags & MTN_ATTN_PREFILL_ONE_TILE) &&
       (total_q / mtn::kBM) * num_q_heads >= 2 * static_cast<int64_t>(mtn::sm_count())) {
     return D == 64 ? mtn::launch_prefill_pair<64>(tkv, prm, n_tiles, n_seqs, s)
                    : mtn::launch_prefill_pair<128>(tkv, prm, n_tiles, n_seqs, s);

@@ -160,6 +160,7 @@ class Batch:
     seq_lens: np.ndarray
     cow_src: np.ndarray
     cow_dst: np.ndarray
+    temperatures: np.ndarray  # per row, SamplingParams::temperature
 
     @property
     def n_reqs(self) -> int:
@@ -214,7 +215,7 @@ class Scheduler:
                      _arr(v.position_ids, v.n_tokens, np.int32), _arr(v.qo_indptr, n + 1, np.int32),
                      _arr(v.kv_indptr, n + 1, np.int32), _arr(v.kv_indices, nkv, np.int32),
                      _arr(v.seq_lens, n, np.int32), _arr(v.cow_src, v.n_cow, np.int32),
-                     _arr(v.cow_dst, v.n_cow, np.int32))
+                     _arr(v.cow_dst, v.n_cow, np.int32), _arr(v.temperatures, n, np.float32))
 
     def process_logits(self, logits: np.ndarray) -> None:
         lg = np.ascontiguousarray(logits, dtype=np.float32)

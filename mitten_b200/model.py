@@ -72,8 +72,14 @@ class QwenPagedModel:
     """Qwen3_5Model (all layers full attention) over a PagedKVPool."""
 
     def __init__(self, shape: DecoderShape, weights: dict, num_pages: int, page_size: int = 16,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", split_bf16: bool = True):
         self.s = shape
+        # The dense path is f32, like the reference's (model.rs:413-416
+        # multiplies in f32): q and the softmax weights reach the tensor cores
+        # as bf16 hi + lo pairs (MTN_ATTN_SPLIT_BF16) unless split_bf16=False;
+        # prefill can split only at head_dim <= 128.
+        self.split_dec = split_bf16
+        self.split_pre = split_bf16 and shape.head_dim <= 128
         self.dev = torch.device(device)
         self.w = {k: torch.as_tensor(v).to(self.dev, torch.float32) for k, v in weights.items()}
         # RMSNorm scales (1 + w), formed once
@@ -117,6 +123,14 @@ class QwenPagedModel:
             self._pws = torch.zeros(nb, dtype=torch.uint8, device=self.dev)
         return self._pws
 
+    def reset_workspaces(self) -> None:
+        """Zero every attention workspace (after a launch that gave up on a bounded wait)."""
+        for ws in [self._ws] + [g.meta["ws"] for g in self._graphs.values()]:
+            if ws is not None:
+                ws.reset()
+        if self._pws is not None:
+            self._pws.zero_()
+
     def _decode_ws(self, n: int) -> paged.DecodeWorkspace:
         if self._ws is None or n > self._ws_seqs:
             self._ws = paged.DecodeWorkspace.for_shape(self.pool, n, self.s.hq)
@@ -150,13 +164,13 @@ class QwenPagedModel:
         tp = meta["tp"]
         if tp:
             self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
-            paged.paged_prefill(self.pool, li, q[:tp].to(torch.bfloat16).contiguous(), meta["qo_p"], meta["kv_p"],
+            paged.paged_prefill(self.pool, li, q[:tp].contiguous(), meta["qo_p"], meta["kv_p"],
                                 meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=s.phantom,
-                                out=attn[:tp], workspace=meta["pws"])
+                                out=attn[:tp], workspace=meta["pws"], split_bf16=self.split_pre)
         if T > tp:
             paged.paged_decode(self.pool, li, q[tp:].contiguous(), meta["kv_d"], meta["kv_indices"], meta["len_d"],
                                scale=self.scale, phantom=s.phantom, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
-                               out=attn[tp:], workspace=meta["ws"])
+                               out=attn[tp:], workspace=meta["ws"], split_bf16=self.split_dec)
         o = attn.view(T, s.hq * s.head_dim)
         if gate is not None:
             o = torch.sigmoid(gate) * o
@@ -284,15 +298,18 @@ class Engine:
     """engine_loop.rs:28-107 over the scheduler mirror and a paged model.
 
     Each iteration: schedule a batch, run its copy-on-write page copies and
-    the model forward, sample greedily on the device (first strict max,
-    scheduler.rs:186-199) and hand the tokens back to the scheduler.  A
-    backend error aborts every request of the batch (engine_loop.rs:47-57).
+    the model forward, sample every row on the device with its request's
+    temperature (sample_token, scheduler.rs:186-223: greedy first strict max
+    or the reference's hash-of-logits pick) and hand the tokens back to the
+    scheduler.  A backend error aborts every request of the batch
+    (engine_loop.rs:47-57).
     """
 
     def __init__(self, model: QwenPagedModel, sched, cuda_graphs: bool = True):
         self.model, self.sched = model, sched
         self.cuda_graphs = cuda_graphs
         self.iterations = 0
+        self._sample_ws = None
 
     def step(self) -> bool:
         b = self.sched.schedule()
@@ -300,7 +317,21 @@ class Engine:
             return False
         try:
             logits = self.model.decode_step(b) if self.cuda_graphs else self.model.forward(b)
-            tokens = paged.argmax_rows(logits).cpu().numpy().astype(np.uint32)
+            if np.any(b.temperatures > 0):
+                nb = L.lib().mtn_sample_rows_workspace_bytes(*logits.shape)
+                if self._sample_ws is None or self._sample_ws.numel() < nb:
+                    self._sample_ws = torch.empty(nb, dtype=torch.uint8, device=logits.device)
+                temps = torch.from_numpy(b.temperatures).to(logits.device)
+                tokens = paged.sample_rows(logits, temps, workspace=self._sample_ws).cpu().numpy().astype(np.uint32)
+            else:
+                tokens = paged.argmax_rows(logits).cpu().numpy().astype(np.uint32)
+            code, detail = paged.device_error(self.model.dev.index or 0)
+            if code:
+                timeout = code == paged.DEV_ERR_TIMEOUT
+                if timeout:
+                    self.model.reset_workspaces()
+                raise L.MittenError(L.MTN_ETIMEOUT if timeout else L.MTN_EDEVICE,
+                                    f"device error {code} (detail {detail}) in the step's kernels")
         except (L.MittenError, RuntimeError):
             self.sched.abort_batch()
             raise

@@ -124,11 +124,17 @@ def build_slot_mapping(qo_indptr, positions, kv_indptr, kv_indices, page_size: i
 
 
 class DecodeWorkspace:
-    """Partials + arrival counters for mtn_paged_decode (zeroed once, reusable)."""
+    """Partials + arrival counters for mtn_paged_decode (zeroed once, reusable).
+
+    A launch that gives up on a bounded wait (device error code 4) can leave
+    arrival counters non-zero: call reset() before the next launch."""
 
     def __init__(self, nbytes: int, device):
         self.nbytes = max(int(nbytes), 256)
         self.buf = torch.zeros(self.nbytes, dtype=torch.uint8, device=device)
+
+    def reset(self) -> None:
+        self.buf.zero_()
 
     @classmethod
     def for_shape(cls, pool: PagedKVPool, n_seqs: int, num_q_heads: int):
@@ -140,11 +146,13 @@ def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torc
                  kv_indices: torch.Tensor, seq_lens: torch.Tensor, scale: float | None = None,
                  phantom: bool = False, k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-                 workspace: DecodeWorkspace | None = None, stream=None) -> torch.Tensor:
+                 workspace: DecodeWorkspace | None = None, stream=None, split_bf16: bool = False) -> torch.Tensor:
     """Decode attention for q [n_seqs, num_q_heads, head_dim] over the paged cache.
 
     With k_new/v_new [n_seqs, kv_heads, head_dim] the step's token is first
     stored at position seq_lens[r]-1 of each sequence (fused KV append).
+    `split_bf16` passes Q and P to the tensor cores as bf16 hi + lo pairs
+    (MTN_ATTN_SPLIT_BF16): f32-level products at no extra tensor-core work.
     """
     if q.dim() != 3 or not q.is_contiguous():
         raise ValueError("q must be a contiguous [n_seqs, heads, head_dim] tensor")
@@ -164,7 +172,7 @@ def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torc
         if k_new.dtype != v_new.dtype or k_new.numel() != n * pool.num_kv_heads * d:
             raise ValueError("k_new/v_new shape or dtype mismatch")
         new_code = _dtype_code(k_new.dtype)
-    flags = L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0
+    flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_SPLIT_BF16 if split_bf16 else 0)
     L.check(L.lib().mtn_paged_decode(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype), _ptr(out),
                                      _dtype_code(out.dtype), _ptr(k_new), _ptr(v_new), new_code, n, hq,
                                      _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)), _ptr(_i32(seq_lens)),
@@ -176,8 +184,12 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
                   kv_indptr: torch.Tensor, kv_indices: torch.Tensor, seq_lens: torch.Tensor, max_q_len: int,
                   scale: float | None = None, phantom: bool = False, out: torch.Tensor | None = None,
                   out_dtype: torch.dtype = torch.bfloat16, workspace: torch.Tensor | None = None,
-                  stream=None, one_tile: bool = False) -> torch.Tensor:
-    """Chunked-prefill attention for q [total_q, num_q_heads, head_dim] (bf16) over the paged cache.
+                  stream=None, one_tile: bool = False, split_bf16: bool = False) -> torch.Tensor:
+    """Chunked-prefill attention for q [total_q, num_q_heads, head_dim] (bf16 or f32) over the paged cache.
+
+    f32 queries are rounded to bf16 as they are loaded; `split_bf16`
+    (MTN_ATTN_SPLIT_BF16, head_dim <= 128) instead passes Q and P to the
+    tensor cores as bf16 hi + lo pairs, twice the tensor-core work.
 
     Launches with few (query tile, head) units cut long ones into pieces over
     more CTAs; that needs `workspace` (mtn_paged_prefill_workspace_bytes,
@@ -187,8 +199,8 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
     many query tiles at head_dim <= 128 run two query tiles per CTA;
     `one_tile` forces the one-tile kernel (same results).
     """
-    if q.dim() != 3 or not q.is_contiguous() or q.dtype != torch.bfloat16:
-        raise ValueError("q must be a contiguous bf16 [total_q, heads, head_dim] tensor")
+    if q.dim() != 3 or not q.is_contiguous() or q.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("q must be a contiguous bf16 or f32 [total_q, heads, head_dim] tensor")
     tq, hq, d = q.shape
     if scale is None:
         scale = d ** -0.5
@@ -198,8 +210,10 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
     nb = L.lib().mtn_paged_prefill_workspace_bytes(n, tq, hq, pool.num_kv_heads, d)
     if workspace is None and nb > 0:
         workspace = torch.zeros(nb, dtype=torch.uint8, device=q.device)
-    flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_PREFILL_ONE_TILE if one_tile else 0)
-    L.check(L.lib().mtn_paged_prefill(C.byref(pool.layout), layer, _ptr(q), _ptr(out), _dtype_code(out.dtype), n,
+    flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_PREFILL_ONE_TILE if one_tile else 0) \
+        | (L.MTN_ATTN_SPLIT_BF16 if split_bf16 else 0)
+    L.check(L.lib().mtn_paged_prefill(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype), _ptr(out),
+                                      _dtype_code(out.dtype), n,
                                       tq, hq, _ptr(_i32(qo_indptr)), _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)),
                                       _ptr(_i32(seq_lens)), max_q_len, float(scale), flags, _ptr(workspace),
                                       0 if workspace is None else workspace.numel(), _stream(stream)))
@@ -216,8 +230,33 @@ def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None, stream=No
     return out
 
 
+def sample_rows(logits: torch.Tensor, temperatures: torch.Tensor, out: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """sample_token (scheduler.rs:186-223) on the device: greedy rows (temperature <= 0) take the
+    first strict max, the others the reference's hash-of-logits pick, bit-exact with its f32 order."""
+    if logits.dtype != torch.float32 or not logits.is_contiguous() or logits.dim() != 2:
+        raise ValueError("logits must be a contiguous f32 [rows, vocab] tensor")
+    n, vocab = logits.shape
+    t = temperatures.to(device=logits.device, dtype=torch.float32).contiguous()
+    if t.numel() != n:
+        raise ValueError("one temperature per row")
+    if out is None:
+        out = torch.empty(n, dtype=torch.int32, device=logits.device)
+    nb = L.lib().mtn_sample_rows_workspace_bytes(n, vocab)
+    if workspace is None or workspace.numel() < nb:
+        workspace = torch.empty(max(nb, 4), dtype=torch.uint8, device=logits.device)
+    L.check(L.lib().mtn_sample_rows(_ptr(logits), _ptr(t), n, vocab, _ptr(out), _ptr(workspace), workspace.numel(),
+                                    _stream(stream)))
+    return out
+
+
+DEV_ERR_TIMEOUT = 4  # a bounded device wait ran out
+
+
 def device_error(device: int = 0, clear: bool = True) -> tuple[int, int]:
-    """(code, detail) of the first metadata error a kernel recorded; (0, 0) if none."""
+    """(code, detail) of the first metadata error a kernel recorded; (0, 0) if none.
+    After DEV_ERR_TIMEOUT, reset() every DecodeWorkspace (and zero every prefill split
+    workspace) the failed launches used."""
     code, detail = C.c_int32(0), C.c_int32(0)
     L.check(L.lib().mtn_device_error(device, int(clear), C.byref(code), C.byref(detail)))
     return code.value, detail.value

@@ -2,19 +2,16 @@
 against the numpy restatement of Qwen3_5Model (oracle/model_ref.py).
 
 Pass criteria: greedy tokens equal to the oracle's for
-32 steps, and the logits every token is chosen from within a stated
-tolerance.  The oracle stores its cache rows rounded to bf16 (the pool's
-storage precision; the reference f32 path with bf16 K/V), so the remaining
-differences are BLAS summation order and the bf16 Q and P operands of the
-tensor-core attention (measured: with those two roundings emulated in the
-oracle the logit error falls from ~3e-2 to ~5e-3 at config 1).
+all 32 steps of every request, and the logits every token is chosen from
+within a stated tolerance.  The oracle stores its cache rows rounded to
+bf16 (the pool's storage precision; the reference f32 path with bf16 K/V).
+The model's attention runs with MTN_ATTN_SPLIT_BF16 (Q and P reach the
+tensor cores as bf16 hi + lo pairs), so what remains is f32 summation order
+(BLAS vs numpy, tensor-core accumulation) and the occasional K/V element
+whose f32 value rounds to a different bf16 neighbour on the two sides.
 
-The oracle is also run teacher-forced on the kernel path's own tokens, so a
-free-running divergence is checked where it happens: it passes only at a
-near-tie, where the oracle's logit for the kernel path's token is within
-2 x the logit tolerance of the oracle's maximum.  At config 1 (seeds 0 and
-1) 3 of 4 requests match for all 32 steps; request 3 matches for 20 steps
-and then takes a token whose oracle logit is 0.0073 below the maximum.
+The oracle is also run teacher-forced on the kernel path's own tokens; the
+largest logit error over every sampled step is printed and bounded.
 """
 from __future__ import annotations
 
@@ -28,8 +25,8 @@ from oracle import model_ref as R
 pytestmark = pytest.mark.gpu
 
 # max |logit_gpu - logit_oracle| over every sampled step (teacher-forced)
-LOGIT_TOL_SMALL = 1e-2   # 3 layers: measured 4.1e-3
-LOGIT_TOL_CONFIG1 = 5e-2  # 24 layers of N(0, 0.02) weights: measured 3.3e-2
+LOGIT_TOL_SMALL = 1e-2
+LOGIT_TOL_CONFIG1 = 1e-2  # 24 layers of N(0, 0.02) weights
 
 
 def shape_of(cfg: R.QwenShape) -> M.DecoderShape:
@@ -66,35 +63,30 @@ def run_engine(cfg, weights, prompts, steps, num_pages=256, budget=512, max_deco
 
 
 def compare(cfg, weights, prompts, steps, tol, **kw):
-    """Free-running greedy tokens must equal the oracle's; the oracle is then also run teacher-forced on
-    the kernel path's tokens so a divergence can be told apart: it is accepted only at a near-tie,
-    where the oracle's logit for the kernel path's token is within 2 * tol of its maximum."""
+    """Free-running greedy tokens must equal the oracle's, every request, every step.  The oracle is
+    also run teacher-forced on the kernel path's tokens to measure the logit error of every sampled
+    step (the first-strict-max choice is compared with the oracle's at each step too)."""
     outs, lg_gpu, model, sched = run_engine(cfg, weights, prompts, steps, **kw)
     ref = R.RefModel(cfg, weights, kv_round=True)
-    lg_ref = []
-    want = R.generate(ref, prompts, steps, logits_out=lg_ref)
-    # teacher-forced oracle: the same prompts followed by the kernel path's tokens
+    want = R.generate(ref, prompts, steps)
     forced = R.RefModel(cfg, weights, kv_round=True)
-    err, report = 0.0, []
+    err, gaps = 0.0, []
     for rid, prompt in enumerate(prompts):
         assert len(outs[rid]) == steps
         lg = forced.forward(rid, prompt, np.arange(len(prompt)))
         for s in range(steps):
             err = max(err, float(np.abs(lg_gpu[rid][s] - lg).max()))
-            tok = outs[rid][s]
             best = R.greedy_first_max(lg)
-            gap = float(lg[best] - lg[tok])
-            if tok != best:
-                report.append((rid, s, tok, best, gap))
-                assert gap <= 2 * tol, (rid, s, tok, best, gap)
+            top2 = np.partition(lg, -2)[-2:]
+            gaps.append(float(top2[1] - top2[0]))
+            assert outs[rid][s] == best, (rid, s, outs[rid][s], best)
             if s + 1 < steps:
-                lg = forced.forward(rid, np.array([tok]), np.array([len(prompt) + s]))
-    print(f"max |logit error| (teacher forced) {err:.3e}; near-tie divergences {report}")
+                lg = forced.forward(rid, np.array([outs[rid][s]]), np.array([len(prompt) + s]))
+    print(f"max |logit error| (teacher forced) {err:.3e}; smallest top-2 logit gap {min(gaps):.3e}")
+    assert outs == want
     assert err <= tol, err
-    if not report:
-        assert outs == want
     assert sched.num_active() == 0
-    return err, report
+    return err
 
 
 def test_small_model_chunked_prefill_and_mixed_batches(cuda_device):
@@ -124,8 +116,7 @@ def test_config1_greedy_32_steps(cuda_device):
     w = R.random_weights(cfg, seed=0)
     rng = np.random.default_rng(1)
     prompts = [rng.integers(0, cfg.vocab, 128).astype(np.int64) for _ in range(4)]
-    err, report = compare(cfg, w, prompts, 32, LOGIT_TOL_CONFIG1, num_pages=512)
-    assert len(report) <= 1  # near-ties, each a free-running divergence
+    compare(cfg, w, prompts, 32, LOGIT_TOL_CONFIG1, num_pages=512)
 
 
 def test_engine_cuda_graph_decode_matches_eager(cuda_device):
