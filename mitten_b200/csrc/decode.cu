@@ -136,6 +136,17 @@ enum Bar {
   kNumBars = 24
 };
 
+// A segment's arrival ticket: one atomic add at gpu scope with acquire and
+// release semantics.  Release: the partials this CTA's threads wrote before
+// the named barrier that precedes the call are visible to whoever acquires
+// a later ticket; acquire: this CTA's reads after the next barrier see every
+// partial released by earlier tickets (the merge reads them with ld.cg).
+__device__ __forceinline__ unsigned int ticket_add(unsigned int* cnt) {
+  unsigned int r;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(r) : "l"(cnt) : "memory");
+  return r;
+}
+
 // Final normalisation of one output element: o/l with the phantom key folded in.
 __device__ __forceinline__ float finalize(float o, float l, float m, int phantom) {
   if (phantom) {
@@ -248,7 +259,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffMisc + 4);
   int* start_s = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 12);
   int64_t* start_pre = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 16);
-  int64_t* total_u = reinterpret_cast<int64_t*>(smem_raw + C::kOffMisc + 24);
   int* start_len = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 32);
   int* start_pbeg = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 36);
   float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
@@ -335,29 +345,35 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       pre += T;
     }
   }
-  if (tid == 0) *total_u = U;
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_base_s;
   // Up to here the CTA read only the batch metadata (seq_lens, kv_indptr),
   // which no decode launch writes; it may have started while the previous
   // kernel of the stream was still running (see launch_dependents above).
-  // Wait for that kernel before reading q, k_new/v_new, K/V pages or writing
-  // o, the pool or the workspace.  (A kernel that does not allow early
-  // launch has finished before this grid starts: then this returns at once.)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int s = sb; s < se; ++s) {
-    if (s % static_cast<int64_t>(gridDim.x) != cta) continue;
-    const int len = seq_len_of(p, s);
-    if ((len + kTile - 1) / kTile == 0) {
-      // No tiles: nobody else writes this sequence's output (phantom-only or empty softmax).
-      const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
-      for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
+  // Each role waits for that kernel (griddepcontrol.wait) before it reads
+  // q, k_new/v_new or K/V pages, or writes o, the pool or the workspace:
+  // the producer only after fetching its first tiles' page ids, which are
+  // metadata too.  (A kernel that does not allow early launch has finished
+  // before this grid starts: then the wait returns at once.)
+  auto grid_wait = [] { asm volatile("griddepcontrol.wait;" ::: "memory"); };
+  // Sequences without tiles: nobody else writes their output (phantom-only
+  // or empty softmax).  Run by every thread after its wait.
+  auto empty_outputs = [&] {
+    for (int s = sb; s < se; ++s) {
+      if (s % static_cast<int64_t>(gridDim.x) != cta) continue;
+      const int len = seq_len_of(p, s);
+      if ((len + kTile - 1) / kTile == 0) {
+        const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
+        for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
+      }
     }
-  }
+  };
   // Uniform over the CTA.  The bad start cannot happen for consistent metadata.
   const bool bad_start = n_local > 0 && (*start_s < 0 || *start_s >= p.n_seqs);
   if (n_local == 0 || bad_start) {
+    grid_wait();
+    empty_outputs();
     if (bad_start && tid == 0) record_error(p.err, kDevErrBadSeqLen, -1);
     if (warp == 0) tc::tmem_dealloc(tmem, C::kTmemCols);
     return;
@@ -370,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     const int tid160 = warp == 5 ? 128 + lane : tid;
     uint4* pz = reinterpret_cast<uint4*>(p_s);
     for (int e = tid160; e < 2 * C::kPBytes / 16; e += 160) pz[e] = make_uint4(0u, 0u, 0u, 0u);
+    grid_wait();
+    empty_outputs();
     fence_proxy_async_shared();
     tc::named_sync(2, 160);
   }
@@ -395,8 +413,27 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     // overlap the wait for a free stage; the ids are checked only when used,
     // so no fetch waits for its own load.
     int pg[C::kStages], apg[C::kStages], apos[C::kStages];
+    int64_t asrc[C::kStages];  // element offset of the appended row in k_new / v_new
     uint4 ak[C::kStages], av[C::kStages];
-    auto fetch = [&](int& pg_o, int& apg_o, int& apos_o, uint4& ak_o, uint4& av_o) {
+    auto load_rows = [&](int64_t src, uint4& ak_o, uint4& av_o) {
+      if (lane >= D / 8) return;
+      src += lane * 8;
+      if (p.new_f32) {
+        const float* kf = static_cast<const float*>(p.k_new) + src;
+        const float* vf = static_cast<const float*>(p.v_new) + src;
+        const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
+        const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
+        ak_o = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y), f2_to_bf2(k1.z, k1.w));
+        av_o = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y), f2_to_bf2(v1.z, v1.w));
+      } else {
+        ak_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
+        av_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
+      }
+    };
+    // Page ids of wp's tile and, when that tile ends its segment, the page
+    // and offset of this step's row; the row itself (k_new / v_new, which the
+    // previous kernel may have written) only when `rows` is set.
+    auto fetch = [&](int& pg_o, int& apg_o, int& apos_o, int64_t& asrc_o, uint4& ak_o, uint4& av_o, bool rows) {
       const int npg = (wp.len + p.ps - 1) / p.ps;
       pg_o = 0;
       if (lane < tile_pages) pg_o = p.kv_indices[wp.pbeg + min(wp.j * tile_pages + lane, npg - 1)];
@@ -408,29 +445,20 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         const int pos = wp.len - 1;
         apos_o = pos % p.ps;
         apg_o = p.kv_indices[wp.pbeg + pos / p.ps];
-        if (lane < D / 8) {
-          const int64_t src = (static_cast<int64_t>(wp.s) * p.hkv + wp.g) * D + lane * 8;
-          if (p.new_f32) {
-            const float* kf = static_cast<const float*>(p.k_new) + src;
-            const float* vf = static_cast<const float*>(p.v_new) + src;
-            const float4 k0 = *reinterpret_cast<const float4*>(kf), k1 = *reinterpret_cast<const float4*>(kf + 4);
-            const float4 v0 = *reinterpret_cast<const float4*>(vf), v1 = *reinterpret_cast<const float4*>(vf + 4);
-            ak_o = make_uint4(f2_to_bf2(k0.x, k0.y), f2_to_bf2(k0.z, k0.w), f2_to_bf2(k1.x, k1.y),
-                              f2_to_bf2(k1.z, k1.w));
-            av_o = make_uint4(f2_to_bf2(v0.x, v0.y), f2_to_bf2(v0.z, v0.w), f2_to_bf2(v1.x, v1.y),
-                              f2_to_bf2(v1.z, v1.w));
-          } else {
-            ak_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.k_new) + src);
-            av_o = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.v_new) + src);
-          }
-        }
+        asrc_o = (static_cast<int64_t>(wp.s) * p.hkv + wp.g) * D;
+        if (rows) load_rows(asrc_o, ak_o, av_o);
       }
     };
 #pragma unroll
     for (int k = 0; k < C::kStages; ++k) {
-      if (k < n_local) fetch(pg[k], apg[k], apos[k], ak[k], av[k]);
+      if (k < n_local) fetch(pg[k], apg[k], apos[k], asrc[k], ak[k], av[k], false);
       if (k + 1 < n_local) wp.next(p);
     }
+    grid_wait();
+    empty_outputs();
+#pragma unroll
+    for (int k = 0; k < C::kStages; ++k)
+      if (k < n_local && apos[k] >= 0) load_rows(asrc[k], ak[k], av[k]);
     bool run = true;
     // Stage slot st of round i0 is tile i0 + st: unrolled so the ring
     // registers are indexed with constants.
@@ -565,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         }
         }
         if (i + C::kStages < n_local) {
-          fetch(pg[st], apg[st], apos[st], ak[st], av[st]);  // wp is at tile i + kStages
+          fetch(pg[st], apg[st], apos[st], asrc[st], ak[st], av[st], true);  // wp is at tile i + kStages
           if (i + C::kStages + 1 < n_local) wp.next(p);
         }
         if (i + 1 < n_local) w.next(p);
@@ -870,7 +898,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           l_cta[h] = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] + red_sum[3 * kN + h];
         tc::named_sync(1, 128);  // red_sum is reused by the next segment
         const int64_t head0 = static_cast<int64_t>(w.s) * p.hq + w.g * NREP;
-        const int64_t U = *total_u;
         const int64_t s_start = w.seg_start(p);
         const int64_t ca = cta_of(s_start, U, ctas), cb = cta_of(s_start + w.T - 1, U, ctas);
         if (ca == cb) {
@@ -910,10 +937,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             // one merge is left for the end.  Only thread 0 waits on the fence;
             // the ticket value is first needed after the last tile.
             tc::named_sync(1, 128);  // every thread's partial is written
-            if (t == 0) {
-              __threadfence();
-              early_ticket = atomicAdd(&p.ws_cnt[seg_id], 1u);
-            }
+            if (t == 0) early_ticket = ticket_add(&p.ws_cnt[seg_id]);
             early = true;
           }
           ++n_pend;
@@ -933,13 +957,9 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (t == 0 && early) {
           ticket = early_ticket;
         } else {
-          // One cumulative fence per ticket after the barrier publishes
-          // every thread's partials.
-          __threadfence();
-          ticket = atomicAdd(&p.ws_cnt[pd.x], 1u);
+          ticket = ticket_add(&p.ws_cnt[pd.x]);
         }
         last_flag[t] = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
-        __threadfence();
       }
       tc::named_sync(1, 128);
     }
@@ -1040,15 +1060,17 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  const int grid = sm_count() * C::kCtasPerSm;
+  const int smem = C::kSmem;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    MTN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem),
+    MTN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "cudaFuncSetAttribute(decode)");
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count() * C::kCtasPerSm);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   // Programmatic dependent launch: this grid may begin while the previous
   // kernel of the stream finishes, if that kernel allows it (decode launches

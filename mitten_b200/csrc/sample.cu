@@ -15,14 +15,15 @@
 // f32::exp calls libm's expf (glibc: at most 0.502 ulp), which is correctly
 // rounded except for results within about 0.002 ulp of a rounding midpoint;
 // only there can an e_i differ, by one ulp.  The two sums are sequential
-// chains, as in the reference: one thread runs them while the block has
-// computed every e_i in parallel beforehand.
+// chains, as in the reference: one thread runs them over shared-memory
+// chunks that the rest of the block computes and stages ahead of it.
 #include "common.cuh"
 
 namespace mtn {
 namespace {
 
 constexpr int kSampleThreads = 512;
+constexpr int kChunk = 4096;  // floats per shared-memory stage of the two sequential sums
 
 __device__ __forceinline__ float exp_f32(float x) { return __double2float_rn(exp(static_cast<double>(x))); }
 
@@ -80,46 +81,91 @@ __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const float
   float* e = ws + r * vocab;
   for (int64_t i = tid; i < vocab; i += kSampleThreads) e[i] = exp_f32(__fdiv_rn(row[i], t));
   __syncthreads();
-  if (tid != 0) return;
+  __shared__ float buf[2][kChunk];
+  __shared__ float sum_s;
+  __shared__ int done_s;
   uint64_t hash = 0;
-  const int64_t nh = vocab < 100 ? vocab : 100;
-  for (int64_t i = 0; i < nh; ++i) hash = hash * 31u + static_cast<uint64_t>(__float_as_uint(row[i]));
-  const float rand_val = __fdiv_rn(static_cast<float>(hash % 1000u), 1000.0f);
-  // Sequential sum in index order; loads run ahead of the add chain.
-  float sum = 0.0f;
-  int64_t i = 0;
-  for (; i + 8 <= vocab; i += 8) {
-    float v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = e[i + k];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, v[k]);
+  float rand_val = 0.0f;
+  if (tid == 0) {
+    const int64_t nh = vocab < 100 ? vocab : 100;
+    for (int64_t i = 0; i < nh; ++i) hash = hash * 31u + static_cast<uint64_t>(__float_as_uint(row[i]));
+    rand_val = __fdiv_rn(static_cast<float>(hash % 1000u), 1000.0f);
+    done_s = 0;
   }
-  for (; i < vocab; ++i) sum = __fadd_rn(sum, e[i]);
-  // First index whose running sum of e_j / sum reaches rand_val.
-  float cum = 0.0f;
+  const int64_t nc = (vocab + kChunk - 1) / kChunk;
+  // Both chains run in thread 0 over shared-memory chunks, while the other
+  // threads stage the next chunk: pass 0 stages e_i and sums them in index
+  // order; pass 1 stages e_i / sum and accumulates the running sum until it
+  // reaches rand_val.
+  float sum = 0.0f, cum = 0.0f;
   int64_t pick = vocab - 1;
-  bool found = false;
-  for (i = 0; !found && i + 8 <= vocab; i += 8) {
-    float pv[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) pv[k] = __fdiv_rn(e[i + k], sum);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      cum = __fadd_rn(cum, pv[k]);
-      if (!found && rand_val <= cum) {
-        pick = i + k;
-        found = true;
+  for (int pass = 0; pass < 2; ++pass) {
+    const float div = pass ? sum_s : 1.0f;
+    auto stage = [&](int64_t c) {
+      const int64_t base = c * kChunk;
+      for (int k = tid; k < kChunk; k += kSampleThreads) {
+        const int64_t i = base + k;
+        float x = 0.0f;
+        if (i < vocab) x = pass ? __fdiv_rn(e[i], div) : e[i];
+        buf[c & 1][k] = x;
       }
+    };
+    stage(0);
+    __syncthreads();
+    for (int64_t c = 0; c < nc; ++c) {
+      if (c + 1 < nc) stage(c + 1);
+      if (tid == 0 && !(pass == 1 && done_s)) {
+        const float* b = buf[c & 1];
+        const int n = static_cast<int>(min(static_cast<int64_t>(kChunk), vocab - c * kChunk));
+        if (pass == 0) {
+          int k = 0;
+          for (; k + 8 <= n; k += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = b[k + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v[j]);
+          }
+          for (; k < n; ++k) sum = __fadd_rn(sum, b[k]);
+        } else {
+          int k = 0;
+          for (; k + 8 <= n; k += 8) {
+            float v[8], run[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = b[k + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              cum = __fadd_rn(cum, v[j]);
+              run[j] = cum;
+            }
+            int hit = -1;
+#pragma unroll
+            for (int j = 7; j >= 0; --j)
+              if (rand_val <= run[j]) hit = j;  // the first crossing of the eight
+            if (hit >= 0) {
+              pick = c * kChunk + k + hit;
+              done_s = 1;
+              break;
+            }
+          }
+          for (; !done_s && k < n; ++k) {
+            cum = __fadd_rn(cum, b[k]);
+            if (rand_val <= cum) {
+              pick = c * kChunk + k;
+              done_s = 1;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (pass == 1 && done_s) break;  // every thread reads the flag after the barrier
+    }
+    if (pass == 0) {
+      if (tid == 0) sum_s = sum;
+      __syncthreads();
     }
   }
-  for (; !found && i < vocab; ++i) {
-    cum = __fadd_rn(cum, __fdiv_rn(e[i], sum));
-    if (rand_val <= cum) {
-      pick = i;
-      found = true;
-    }
-  }
+  if (tid != 0) return;
   out[r] = static_cast<int32_t>(pick);
 }
 

@@ -5,8 +5,9 @@ this package, and only as the checker (or the timed CPU baseline); the
 product path in mitten_b200/ never imports it.
 
   attention_ref.c  f32 restatement of the reference attention core
-                   (inference-model-qwen/src/model.rs:394-416) and of the
-                   reference's cat-grown CPU decode step (the timed baseline).
+                   (inference-model-qwen/src/model.rs:394-416), of the
+                   reference's cat-grown CPU decode step (the timed baseline)
+                   and of sample_token (scheduler.rs:186-223).
   host_ref.py      pure-Python restatement of kv_pool.rs / radix_cache.rs /
                    prefill.rs / decode.rs / scheduler.rs.
   model_ref.py     numpy f32 restatement of Qwen3_5Model::forward with
@@ -58,6 +59,8 @@ def lib():
         h.ref_catgrown_step.restype = None
         h.ref_rne_bf16.argtypes = [f32p, C.c_int64, C.POINTER(C.c_uint16)]
         h.ref_rne_bf16.restype = None
+        h.ref_sample_token.argtypes = [f32p, C.c_int64, C.c_float, f32p]
+        h.ref_sample_token.restype = C.c_int64
         h.ref_num_threads.argtypes = []
         h.ref_num_threads.restype = C.c_int
         _lib = h
@@ -95,6 +98,13 @@ def rne_bf16_bits(x) -> np.ndarray:
 
 def bf16_bits_to_f32(b) -> np.ndarray:
     return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def sample_token(row, temperature: float) -> int:
+    """sample_token (scheduler.rs:186-223) of one logits row, in C with libm expf (ref_sample_token)."""
+    r, rp = _f32(np.asarray(row).reshape(-1))
+    scratch = np.empty(max(r.size, 1), np.float32)
+    return int(lib().ref_sample_token(rp, r.size, float(temperature), scratch.ctypes.data_as(C.POINTER(C.c_float))))
 
 
 def round_bf16(x) -> np.ndarray:

@@ -26,6 +26,7 @@
  *                      (model.rs:398-408), a materialised -1e10 mask
  *                      (model.rs:410-411), q.k^T*scale, softmax, P.V
  *                      (model.rs:413-416).  Used as the timed CPU baseline.
+ *   ref_sample_token   sample_token (scheduler.rs:186-223) of one logits row.
  *   ref_rne_bf16       f32 -> bf16 round-to-nearest-even (IEEE), the rounding
  *                      the device path applies when K/V are stored as bf16.
  */
@@ -171,4 +172,43 @@ int ref_num_threads(void) {
 #else
   return 1;
 #endif
+}
+
+/* sample_token (inference-engine/src/scheduler.rs:186-223) on one logits row,
+ * in the reference's f32 operations and order.  temperature <= 0: index of
+ * the first strict maximum (val > max_val; NaN never wins).  Otherwise:
+ * hash = fold over the first 100 logits of hash * 31 + bits (wrapping u64),
+ * rand = (hash % 1000) / 1000 in f32, e_i = expf(l_i / t) (libm's expf, which
+ * Rust's f32::exp calls), sum = e_0 + e_1 + ... left to right, then the first
+ * i whose running sum of e_i / sum reaches rand, else the last index.
+ * scratch: vocab floats.  Built without -ffast-math, so no sum is
+ * reassociated. */
+int64_t ref_sample_token(const float* row, int64_t vocab, float temperature, float* scratch) {
+  if (temperature <= 0.0f) {
+    float max_val = -INFINITY;
+    int64_t max_idx = 0;
+    for (int64_t i = 0; i < vocab; ++i) {
+      if (row[i] > max_val) {
+        max_val = row[i];
+        max_idx = i;
+      }
+    }
+    return max_idx;
+  }
+  uint64_t hash = 0;
+  for (int64_t i = 0; i < vocab && i < 100; ++i) {
+    uint32_t bits;
+    memcpy(&bits, &row[i], 4);
+    hash = hash * 31u + (uint64_t)bits;
+  }
+  const float rand_val = (float)(hash % 1000u) / 1000.0f;
+  for (int64_t i = 0; i < vocab; ++i) scratch[i] = expf(row[i] / temperature);
+  float sum = 0.0f;
+  for (int64_t i = 0; i < vocab; ++i) sum += scratch[i];
+  float cum = 0.0f;
+  for (int64_t i = 0; i < vocab; ++i) {
+    cum += scratch[i] / sum;
+    if (rand_val <= cum) return i;
+  }
+  return vocab - 1;
 }
