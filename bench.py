@@ -476,7 +476,8 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
         buf = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
         for x, o in zip(parts, offs):
             buf[o:o + x.numel()].copy_(x)
-        buf[offs[3]:].copy_(torch.from_numpy(step_inputs(st, i, device)[1]).view(torch.uint8))
+        lens_i = np.ascontiguousarray(step_inputs(st, i, device)[1], np.int32)
+        buf[offs[3]:].copy_(torch.from_numpy(lens_i).view(torch.uint8))
         stage_h.append(buf)
     o_h = [torch.empty((N_SEQS, HQ, D), dtype=torch.bfloat16).pin_memory() for _ in range(total_steps)]
     stage_d = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(2)]
@@ -1041,6 +1042,81 @@ def traffic_from_profile():
     return None
 
 
+QWEN7B = dict(hidden=3584, layers=28, hq=28, hkv=4, head_dim=128, inter=18944, vocab=152064, theta=1e6)
+
+
+def run_box_engine(args, rank, world, local, pg) -> dict:
+    """Whole-box decode through the engine (trimmed): every rank is an independent
+    replica with its own scheduler, KV pool and Qwen2.5-7B-shaped model (random bf16 weights, the
+    reference's gated-q / qk-norm attention), serving its round-robin share of config 5's requests
+    (request r goes to rank r % world).  Trimmed so a run fits in seconds: 64 requests per rank,
+    prompts U[1024, 16384] (seed 9) capped at 4096 tokens, 48 greedy tokens each.  The decode phase
+    (every request prefilled, then every decode step through the engine: schedule, forward replayed
+    from a CUDA graph, device sampling, transition) is timed with CUDA events on each rank; value =
+    decode tokens of all ranks / the slowest rank's decode time."""
+    import torch
+
+    from mitten_b200 import host, model as M
+
+    dev = torch.device("cuda", local)
+    per_rank, cap, out_tokens, timed_steps = 64, 4096, 48, 24
+    rng = np.random.default_rng(9)
+    lens = np.minimum(rng.integers(1024, 16385, size=per_rank * world), cap)
+    toks = np.random.default_rng(10)
+    mine = [r for r in range(per_rank * world) if r % world == rank]
+    prompts = {r: toks.integers(0, QWEN7B["vocab"], int(lens[r])).astype(np.uint32) for r in range(per_rank * world)}
+    shape = M.DecoderShape(**QWEN7B)
+    w = model_weights(shape, dev, seed=0)
+    page_bytes = 2 * shape.layers * 16 * shape.hkv * shape.head_dim * 2
+    num_pages = int(sum((int(lens[r]) + out_tokens + 15) // 16 for r in mine) * 1.1) + 64
+    model = M.QwenPagedModel(shape, w, num_pages, 16, device=dev, split_bf16=False, dtype=torch.bfloat16)
+    del w
+    torch.cuda.empty_cache()
+    sched = host.Scheduler(num_pages, 16, max_prefill_tokens_per_iter=32768, max_decode_batch_size=per_rank,
+                           eos_token_ids=(shape.vocab,))
+    for r in mine:
+        sched.add_request(r, prompts[r], temperature=0.0, max_new_tokens=out_tokens)
+    eng = M.Engine(model, sched, cuda_graphs=True)
+    t0 = time.perf_counter()
+    while any(sched.request_info(r)["state"] != 2 for r in mine):  # until every request is decoding
+        eng.step()
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
+    eng.step()  # first decode-only batch: eager run + capture of the batch's CUDA graph
+    torch.cuda.synchronize(dev)
+    done0 = sum(len(sched.request_output(r)) for r in mine)
+    # Every request has at most 1 + (prefill iterations) tokens here and asks
+    # for 48, so all 64 stay in the batch for the timed steps: one graph size.
+    assert all(len(sched.request_output(r)) + timed_steps < out_tokens for r in mine)
+    barrier(pg)
+    stream = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(timed_steps):
+        eng.step()
+    b.record(stream)
+    b.synchronize()
+    steps = timed_steps
+    t = a.elapsed_time(b) * 1e-3
+    tokens = sum(len(sched.request_output(r)) for r in mine) - done0
+    assert tokens == len(mine) * timed_steps
+    value, t_max = job_throughput(pg, float(tokens), t)
+    code, detail = M.paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail}) in the engine run")
+    res = {"metric": "decode tokens/s (whole box, engine, replicas)", "value": value, "unit": "tokens/s",
+           "n_gpus": world, "decode_steps": steps, "decode_ms_per_step_max": 1e3 * t_max / max(steps, 1),
+           "tokens_per_rank": tokens, "prefill_s_rank0": prefill_s, "kv_pool_gb": num_pages * page_bytes / 1e9,
+           "config": {"workload": "BASELINE config 5 (trimmed): Qwen2.5-7B shape, random bf16 weights, requests "
+                                  "round-robin over replicas", "requests_per_rank": per_rank,
+                      "prompt_tokens": "U[1024, 16384] (seed 9) capped at 4096", "output_tokens": out_tokens,
+                      "timed": f"{timed_steps} decode-only engine steps at a constant batch of {per_rank} per rank",
+                      "trimmed_from": "1024 requests, prompts up to 16384, 256 output tokens, 16 x 32k long-context"}}
+    del model, eng, sched
+    torch.cuda.empty_cache()
+    return res
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1050,6 +1126,7 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-engine", action="store_true", help="skip the whole-box config-5 engine leg")
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
                     help="cfg2 (default) is the headline; cfg3 / cfg4 / cfg5 time those configs' attention "
                          "layers; cfg1 runs config 1's model through the engine")
@@ -1073,6 +1150,11 @@ def main(argv=None) -> int:
         return 0
     try:
         res = run_ours(args, rank, world, local, pg)
+        if not args.no_engine:
+            import torch
+
+            torch.cuda.empty_cache()
+            res["box_engine"] = run_box_engine(args, rank, world, local, pg)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

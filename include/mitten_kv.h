@@ -64,7 +64,10 @@ MTN_API const char* mtn_version(void);
  * (page id >= num_pages, seq_len beyond its pages, ...).  Kernels never trap:
  * they clamp, finish, and record the first error here.  Reading it
  * synchronises `device`.  Returns MTN_OK and stores the code (0 = none)
- * and the kernel-specific detail word; `clear` resets it. */
+ * and the kernel-specific detail word; `clear` resets it.  Codes: 1 page id
+ * outside the pool, 2 seq_len negative or beyond its pages, 3 slot outside
+ * the pool, 4 a bounded wait ran out, 5 position beyond a sequence's pages,
+ * 6 a decode plan made for another grid or not a plan. */
 MTN_API int mtn_device_error(int device, int clear, int32_t* code, int32_t* detail);
 
 /* Self-test of the bounded device waits (failure detection without a GPU
@@ -159,6 +162,42 @@ MTN_API int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer,
 MTN_API int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages,
                   const int32_t* dst_pages, int64_t n_pages, void* stream);
 
+/* KV offload and prefill -> decode handoff (the reference designs these
+ * without code: KvOffloadManager's host KV buffers, design/phase1-
+ * deliverable.md:253-337, and the disaggregation KvHandoff of request id,
+ * pages and cached length, design/phase2b-deliverable.md:272-354): the
+ * listed pages (device array of page ids) of every layer, K and V, to or
+ * from a flat buffer laid out [n_pages][num_layers][2][num_kv_heads]
+ * [page_size][head_dim] bf16, mtn_kv_pages_bytes(pool, n_pages) bytes,
+ * 16-byte aligned: device memory, pinned host memory the device can reach
+ * (offload), or another GPU's memory under peer access (handoff between
+ * replicas).  Page ids outside the pool are skipped and flagged (device
+ * error 1). */
+MTN_API size_t mtn_kv_pages_bytes(const mtn_kv_layout* pool, int64_t n_pages);
+MTN_API int mtn_kv_pages_pack(const mtn_kv_layout* pool, const int32_t* pages, int64_t n_pages, void* dst,
+                              void* stream);
+MTN_API int mtn_kv_pages_unpack(const mtn_kv_layout* pool, const void* src, const int32_t* pages,
+                                int64_t n_pages, void* stream);
+
+/* Fused attention prologue (the per-head work of qwen model.rs:372-392
+ * between the projection GEMMs and attention), one launch for every token
+ * row of a batch: q = RoPE(RMSNorm_(1+w)(q head)) written to q_out
+ * [n_tokens][num_q_heads][head_dim] f32; k = RoPE(RMSNorm_(1+w)(k head)) and
+ * v stored as bf16 (round to nearest even) into the pool at slots[t]
+ * (page * page_size + offset; < 0 skips the token's K/V).  q / k / v:
+ * src_dtype rows q_stride / k_stride / v_stride elements apart (a slice of a
+ * fused projection is fine); q rows are [num_q_heads][1 + q_gated][head_dim]
+ * (q then its gate per head, model.rs:372-375; the gate is left for the
+ * caller).  q_norm_w1 / k_norm_w1: (1 + w) per element, or NULL for no
+ * norm (Gemma).  RoPE: rotate-half over the first rotary_dim elements
+ * (a multiple of 64), angle = positions[t] * inv_freq[i] in f32.  With
+ * the step's rows stored here, mtn_paged_decode runs without k_new / v_new. */
+MTN_API int mtn_qkv_prologue(const mtn_kv_layout* pool, int32_t layer, const void* q, const void* k, const void* v,
+                             int32_t src_dtype, int64_t q_stride, int64_t k_stride, int64_t v_stride,
+                             int32_t q_gated, int32_t num_q_heads, const float* q_norm_w1, const float* k_norm_w1,
+                             float eps, const float* inv_freq, int32_t rotary_dim, const int32_t* positions,
+                             const int64_t* slots, int64_t n_tokens, float* q_out, void* stream);
+
 /* Gather sequences back into the reference's contiguous cache layout
  * KVCacheState::Attention [num_kv_heads][seq_len][head_dim] (bf16):
  * sequence r lands at out + out_offsets[r]*num_kv_heads*head_dim, where
@@ -198,6 +237,32 @@ MTN_API int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer,
                      int32_t n_seqs, int32_t num_q_heads,
                      const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
                      float scale, uint32_t flags,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Work plan for mtn_paged_decode_with_plan (no counterpart in the reference,
+ * whose decode runs per request on the CPU).  Made on the host from the
+ * batch's host-side CSR metadata (the scheduler builds it there every step;
+ * every layer of a step shares one plan): the launch's (sequence, kv head)
+ * segments are cut into 128-token tiles laid end to end, and each CTA of the
+ * persistent grid gets a contiguous range of equal cost -- a tile costs 8, a
+ * segment start 16 more -- plus its start sequence, so the kernel's first
+ * loads need one read of the plan instead of a scan of seq_lens.  plan:
+ * host memory of mtn_paged_decode_plan_bytes(head_dim) bytes; copy it to the
+ * device (16-byte aligned) before the launch that uses it.  The plan holds
+ * the device's SM count: a plan made on another GPU model is rejected by the
+ * kernel (device error 6, nothing computed). */
+MTN_API size_t mtn_paged_decode_plan_bytes(int32_t head_dim);
+MTN_API int mtn_paged_decode_plan(const int32_t* kv_indptr, const int32_t* seq_lens, int32_t n_seqs,
+                                  int32_t page_size, int32_t num_kv_heads, int32_t head_dim, void* plan,
+                                  size_t plan_bytes);
+/* mtn_paged_decode with a device copy of a plan made for these kv_indptr /
+ * seq_lens (NULL: the kernel splits the tiles evenly itself). */
+MTN_API int mtn_paged_decode_with_plan(const mtn_kv_layout* pool, int32_t layer,
+                     const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
+                     const void* k_new, const void* v_new, int32_t new_dtype,
+                     int32_t n_seqs, int32_t num_q_heads,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
+                     float scale, uint32_t flags, const void* plan,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of mtn_paged_decode (no counterpart in the
@@ -414,6 +479,26 @@ MTN_API int mtn_sched_request_output(const mtn_sched* s, uint64_t req_id, uint32
  * The parent must have finished its prompt and still hold its pages. */
 MTN_API int mtn_sched_fork(mtn_sched* s, uint64_t parent_id, uint64_t child_id, const uint32_t* suffix,
                            int64_t n_suffix, float temperature, int32_t max_new_tokens);
+/* Prefill -> decode handoff on the host side (KvHandoff, phase2b-deliverable
+ * .md:272-354).  Export: a Decoding request (its prompt done) leaves this
+ * scheduler -- its pages (capacity/count in *n_pages), device_len (tokens of
+ * KV they hold) and generated tokens (capacity/count in *n_output) are
+ * reported, its page references returned and it ends Done here.  Pack the
+ * pages (mtn_kv_pages_pack, on the stream this scheduler's kernels use)
+ * before this scheduler's next launch, which may reuse them.
+ * Import: admit a handed-over request straight into Decoding on this
+ * scheduler -- prompt, generated tokens (at least one), device_len with
+ * n_input <= device_len < n_input + n_output -- on ceil(device_len /
+ * page_size) freshly allocated pages returned in pages (evicting radix
+ * pages when needed; MTN_ENOMEM when the pool cannot hold them).  Unpack
+ * the KV there (mtn_kv_pages_unpack) before its next decode batch.  The id
+ * may be one this scheduler exported (or saw finish) earlier: swapping a
+ * request out to host memory and back in. */
+MTN_API int mtn_sched_export(mtn_sched* s, uint64_t req_id, uint32_t* pages, int64_t* n_pages, int64_t* device_len,
+                             uint32_t* output_ids, int64_t* n_output);
+MTN_API int mtn_sched_import(mtn_sched* s, uint64_t req_id, const uint32_t* input_ids, int64_t n_input,
+                             const uint32_t* output_ids, int64_t n_output, int64_t device_len, float temperature,
+                             int32_t max_new_tokens, uint32_t* pages, int64_t* n_pages);
 /* Inspection for tests: a page's reference count (0 = free, -1 = out of
  * range) and every page the radix cache lists (capacity/count in *n_pages). */
 MTN_API int32_t mtn_sched_page_refcount(const mtn_sched* s, uint32_t page);

@@ -95,6 +95,13 @@ SIGNATURES: dict[str, tuple] = {
                                    C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                    C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p, C.c_size_t,
                                    C.c_void_p]),
+    "mtn_paged_decode_plan_bytes": (C.c_size_t, [C.c_int32]),
+    "mtn_paged_decode_plan": (C.c_int, [c_i32p, c_i32p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                        C.c_size_t]),
+    "mtn_paged_decode_with_plan": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
+                                             C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
+                                             C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p,
+                                             C.c_void_p, C.c_size_t, C.c_void_p]),
     "mtn_paged_decode_noalloc": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
                                            C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p]),
@@ -103,6 +110,13 @@ SIGNATURES: dict[str, tuple] = {
                                     C.c_int32,
                                     C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_int32, C.c_float, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "mtn_qkv_prologue": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                   C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                   C.c_float, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                   C.c_void_p]),
+    "mtn_kv_pages_bytes": (C.c_size_t, [C.POINTER(KvLayout), C.c_int64]),
+    "mtn_kv_pages_pack": (C.c_int, [C.POINTER(KvLayout), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
+    "mtn_kv_pages_unpack": (C.c_int, [C.POINTER(KvLayout), C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
     "mtn_argmax_rows": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),
     "mtn_sample_rows_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int64]),
     "mtn_sample_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_size_t,
@@ -140,6 +154,9 @@ SIGNATURES: dict[str, tuple] = {
     "mtn_sched_request_info": (C.c_int, [C.c_void_p, C.c_uint64, c_i32p, c_i64p, c_i64p, c_i64p, c_i64p]),
     "mtn_sched_request_pages": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, c_i64p]),
     "mtn_sched_request_output": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, c_i64p]),
+    "mtn_sched_export": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, c_i64p, c_i64p, c_u32p, c_i64p]),
+    "mtn_sched_import": (C.c_int, [C.c_void_p, C.c_uint64, c_u32p, C.c_int64, c_u32p, C.c_int64, C.c_int64, C.c_float,
+                                   C.c_int32, c_u32p, c_i64p]),
     "mtn_sched_fork": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, c_u32p, C.c_int64, C.c_float, C.c_int32]),
     "mtn_sched_page_refcount": (C.c_int32, [C.c_void_p, C.c_uint32]),
     "mtn_sched_tree_pages": (C.c_int, [C.c_void_p, c_u32p, c_i64p]),

@@ -31,6 +31,35 @@ int cuda_status(cudaError_t e, const char* what);
 // Launch-result check after a <<<>>> launch.
 int check_launch(const char* what);
 
+// Launch with programmatic dependent launch allowed: the kernel may begin
+// while the previous kernel of the stream finishes, if that kernel lets it
+// (griddepcontrol.launch_dependents); kernels launched this way execute
+// griddepcontrol.wait before touching memory another kernel may write.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+  if (e != cudaSuccess) return cuda_status(e, what);
+  return check_launch(what);
+}
+
+// First statements of a kernel launched with launch_pdl: wait for the
+// previous grid's memory, then let the next grid start its CTAs.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Device error word: [0] = first error code, [1] = detail.
 int* device_error_ptr();  // device address for the current device
 
@@ -47,7 +76,8 @@ enum DevErr : int {
   kDevErrBadSeqLen = 2,     // seq_len negative or beyond its pages
   kDevErrBadSlot = 3,       // slot outside the pool
   kDevErrTimeout = 4,       // bounded wait ran out
-  kDevErrBadPosition = 5    // position beyond a sequence's pages
+  kDevErrBadPosition = 5,   // position beyond a sequence's pages
+  kDevErrBadPlan = 6        // decode plan made for another grid (detail: its grid) or not a plan (-1)
 };
 
 // ---------------------------------------------------------------- device side

@@ -42,6 +42,7 @@
 #include <cfloat>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -55,6 +56,13 @@ namespace mtn {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+// Work plan of a decode launch, made on the host (int32 words):
+//   [0] kPlanMagic  [1] participating CTAs  [2] grid it was made for  [3] tiles U
+//   [4 + 8 c + k] CTA c: t0, n_local, start sequence, tiles (one kv head's) of
+//                 the sequences before it, its valid length, its first page index
+//   [4 + 8 grid + c] CTA boundaries, c = 0 .. grid (participating CTAs .. grid: U)
+constexpr int32_t kPlanMagic = 0x504e544d;  // "MTNP"
+constexpr int kPlanEntry = 8;
 constexpr int kTile = 128;    // tokens per tile = MMA1 M = TMEM lanes
 constexpr int kThreads = 192;
 constexpr int kN = 16;        // query heads per KV head, padded (MMA N)
@@ -87,6 +95,7 @@ struct DecodeParams {
   float* ws_ml;          // [ctas][2][16][2]   partial (m, l)
   unsigned int* ws_cnt;  // [n_seqs][hkv]      arrival tickets (left at zero)
   int* err;
+  const int32_t* plan;   // host-made work plan (mtn_paged_decode_plan) or null
 };
 
 template <int D>
@@ -236,10 +245,21 @@ struct Walker {
   __device__ int64_t seg_start(const DecodeParams& p) const { return pre * p.hkv + static_cast<int64_t>(g) * T; }
 };
 
-__device__ __forceinline__ int64_t tile_begin(int64_t c, int64_t U, int64_t C) { return c * U / C; }
-// The CTA whose tile range holds global tile x.
-__device__ __forceinline__ int64_t cta_of(int64_t x, int64_t U, int64_t C) {
-  return min(C - 1, ((x + 1) * C - 1) / U);
+// CTA c's first tile and the CTA whose range holds global tile x: from the
+// plan's boundary table (bnd, in shared memory) when there is one, else the
+// equal split c * U / C.
+__device__ __forceinline__ int64_t tile_begin(const int32_t* bnd, int64_t c, int64_t U, int64_t C) {
+  return bnd ? bnd[c] : c * U / C;
+}
+__device__ __forceinline__ int64_t cta_of(const int32_t* bnd, int64_t x, int64_t U, int64_t C) {
+  if (!bnd) return min(C - 1, ((x + 1) * C - 1) / U);
+  int64_t lo = 0, hi = C - 1;  // the last c with bnd[c] <= x
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (bnd[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
 }
 
 // PREC (MTN_ATTN_SPLIT_BF16): Q and P enter the tensor cores as bf16 hi +
@@ -291,24 +311,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
 
   // ------------------------------------------------------------ work split
-  // Tiles per sequence (for one kv head), prefix-summed over the CTA; each
-  // thread owns a contiguous chunk of sequences.
+  // Each thread owns a contiguous chunk of sequences (the scan below, and the
+  // outputs of sequences without tiles).
   const int chunk = (p.n_seqs + kThreads - 1) / kThreads;
   const int sb = min(p.n_seqs, tid * chunk), se = min(p.n_seqs, sb + chunk);
-  int64_t mine = 0;
-  int len_first = 0;  // metadata of this thread's first sequence, kept for the start search
-  for (int s = sb; s < se; ++s) {
-    const int len = seq_len_of(p, s);
-    const int T = (len + kTile - 1) / kTile;
-    if (s == sb) len_first = len;
-    mine += T;
-  }
-  int64_t incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
       mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1 || i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
@@ -316,33 +322,78 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     *start_s = -1;
     fence_barrier_init();
   }
-  if (lane == 31) scan[warp] = incl;
-  __syncthreads();
-  int64_t before = incl - mine;
-  for (int w = 0; w < warp; ++w) before += scan[w];
-  int64_t total_seq_tiles = 0;
-  for (int w = 0; w < kThreads / 32; ++w) total_seq_tiles += scan[w];
-  const int64_t U = total_seq_tiles * p.hkv;
-  // With fewer tiles than CTAs only the first U CTAs take part, so every
-  // participating CTA owns at least one tile and a segment's pieces are
-  // exactly the CTAs cta_of(first tile) .. cta_of(last tile).
-  const int64_t ctas = min(static_cast<int64_t>(gridDim.x), U);
-  const int64_t t0 = cta < ctas ? tile_begin(cta, U, ctas) : 0;
-  const int64_t t1 = cta < ctas ? tile_begin(cta + 1, U, ctas) : 0;
-  const int n_local = static_cast<int>(t1 - t0);
-  if (n_local > 0 && t0 >= before * p.hkv && t0 < (before + mine) * p.hkv) {
-    int64_t pre = before;
-    for (int s = sb; s < se; ++s) {
-      const int len = (s == sb) ? len_first : seq_len_of(p, s);
-      const int T = (len + kTile - 1) / kTile;
-      if (t0 < (pre + T) * p.hkv) {
-        *start_s = s;
-        *start_pre = pre;
-        *start_len = len;
-        *start_pbeg = p.kv_indptr[s];
-        break;
+  int64_t U = 0, ctas = 0, t0 = 0;
+  int n_local = 0;
+  const int32_t* bnd = nullptr;  // the plan's CTA boundaries (shared memory) when there is a plan
+  if (p.plan != nullptr) {
+    // Host-made plan: this CTA's range and start, and every CTA's first
+    // tile, in one round of independent loads.
+    const int32_t* pl = p.plan;
+    int32_t* bnd_s = reinterpret_cast<int32_t*>(big + C::kBigBytes);
+    for (int i = tid; i <= static_cast<int>(gridDim.x); i += kThreads) bnd_s[i] = pl[4 + kPlanEntry * gridDim.x + i];
+    const int32_t* e = pl + 4 + kPlanEntry * cta;
+    const bool plan_ok = pl[0] == kPlanMagic && pl[2] == static_cast<int32_t>(gridDim.x) && pl[1] >= 0 &&
+                         pl[1] <= static_cast<int32_t>(gridDim.x);
+    if (plan_ok) {
+      ctas = pl[1];
+      U = pl[3];
+      if (cta < ctas) {
+        t0 = e[0];
+        n_local = e[1];
+        if (tid == 0) {
+          *start_s = e[2];
+          *start_pre = e[3];
+          *start_len = e[4];
+          *start_pbeg = e[5];
+        }
       }
-      pre += T;
+    } else if (tid == 0 && cta == 0) {
+      record_error(p.err, kDevErrBadPlan, pl[0] == kPlanMagic ? pl[2] : -1);
+    }
+    bnd = bnd_s;
+  } else {
+    // Tiles per sequence (for one kv head), prefix-summed over the CTA.
+    int64_t mine = 0;
+    int len_first = 0;  // metadata of this thread's first sequence, kept for the start search
+    for (int s = sb; s < se; ++s) {
+      const int len = seq_len_of(p, s);
+      const int T = (len + kTile - 1) / kTile;
+      if (s == sb) len_first = len;
+      mine += T;
+    }
+    int64_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) scan[warp] = incl;
+    __syncthreads();
+    int64_t before = incl - mine;
+    for (int w = 0; w < warp; ++w) before += scan[w];
+    int64_t total_seq_tiles = 0;
+    for (int w = 0; w < kThreads / 32; ++w) total_seq_tiles += scan[w];
+    U = total_seq_tiles * p.hkv;
+    // With fewer tiles than CTAs only the first U CTAs take part, so every
+    // participating CTA owns at least one tile and a segment's pieces are
+    // exactly the CTAs cta_of(first tile) .. cta_of(last tile).
+    ctas = min(static_cast<int64_t>(gridDim.x), U);
+    t0 = cta < ctas ? tile_begin(nullptr, cta, U, ctas) : 0;
+    n_local = static_cast<int>(cta < ctas ? tile_begin(nullptr, cta + 1, U, ctas) - t0 : 0);
+    if (n_local > 0 && t0 >= before * p.hkv && t0 < (before + mine) * p.hkv) {
+      int64_t pre = before;
+      for (int s = sb; s < se; ++s) {
+        const int len = (s == sb) ? len_first : seq_len_of(p, s);
+        const int T = (len + kTile - 1) / kTile;
+        if (t0 < (pre + T) * p.hkv) {
+          *start_s = s;
+          *start_pre = pre;
+          *start_len = len;
+          *start_pbeg = p.kv_indptr[s];
+          break;
+        }
+        pre += T;
+      }
     }
   }
   __syncthreads();
@@ -455,7 +506,6 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (k + 1 < n_local) wp.next(p);
     }
     grid_wait();
-    empty_outputs();
 #pragma unroll
     for (int k = 0; k < C::kStages; ++k)
       if (k < n_local && apos[k] >= 0) load_rows(asrc[k], ak[k], av[k]);
@@ -599,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (i + 1 < n_local) w.next(p);
       }
     }
+    empty_outputs();  // off the first loads' path
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -899,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         tc::named_sync(1, 128);  // red_sum is reused by the next segment
         const int64_t head0 = static_cast<int64_t>(w.s) * p.hq + w.g * NREP;
         const int64_t s_start = w.seg_start(p);
-        const int64_t ca = cta_of(s_start, U, ctas), cb = cta_of(s_start + w.T - 1, U, ctas);
+        const int64_t ca = cta_of(bnd, s_start, U, ctas), cb = cta_of(bnd, s_start + w.T - 1, U, ctas);
         if (ca == cb) {
           if (holds) {
 #pragma unroll
@@ -928,7 +979,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
           const int seg_id = static_cast<int>(static_cast<int64_t>(w.s) * p.hkv + w.g);
           if (t == 0) {
-            const int wa = (tile_begin(ca, U, ctas) != s_start) ? 1 : 0;
+            const int wa = (tile_begin(bnd, ca, U, ctas) != s_start) ? 1 : 0;
             pend[n_pend] = make_int4(seg_id, static_cast<int>(ca), static_cast<int>(cb), wa);
           }
           if (cta == cb && i + 1 < n_local) {
@@ -1061,7 +1112,7 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
   int dev = 0;
   cudaGetDevice(&dev);
   const int grid = sm_count() * C::kCtasPerSm;
-  const int smem = C::kSmem;
+  const int smem = C::kSmem + (grid + 1) * 4;  // + the plan's CTA boundary table
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     MTN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "cudaFuncSetAttribute(decode)");
@@ -1117,7 +1168,109 @@ int decode_ctas(int head_dim) {
 
 using mtn::set_error;
 
+namespace mtn {
+namespace {
+
+size_t plan_words(int grid) { return 4 + static_cast<size_t>(kPlanEntry) * grid + grid + 1; }
+
+// Cost-balanced split of the tiles (laid end to end: sequence by sequence,
+// kv head by kv head) into the CTAs' contiguous ranges.  A tile costs 8 and
+// a segment start ((sequence, kv head) first tile) 16 more: a CTA whose range
+// spans two segments pays a second epilogue, measured with %globaltimer at
+// about two tiles of streaming.  The segment cost is used only with at least
+// 25/8 tiles per CTA; then boundary targets are at least 25 cost units apart
+// while tile starts are at most 24 apart, so boundaries strictly increase.
+void split_tiles(const std::vector<int64_t>& T, int hkv, int64_t U, int64_t ctas, int32_t* bnd) {
+  if (U <= ctas) {
+    for (int64_t c = 0; c <= ctas; ++c) bnd[c] = static_cast<int32_t>(c);
+    return;
+  }
+  const int64_t w8 = 8 * U >= 25 * ctas ? 16 : 0;
+  int64_t ne = 0, tiles = 0;
+  for (int64_t t : T) {
+    ne += t > 0;
+    tiles += t;
+  }
+  const int64_t ctot = (8 * tiles + w8 * ne) * hkv;
+  size_t s = 0;
+  int64_t acc = 0, pre = 0;
+  for (int64_t c = 0; c < ctas; ++c) {
+    const int64_t y = c * ctot / ctas;
+    int64_t seg = 0;
+    for (;;) {  // y < ctot: stops at a sequence with tiles
+      seg = 8 * T[s] + (T[s] > 0 ? w8 : 0);
+      if (y < acc + seg * hkv) break;
+      acc += seg * hkv;
+      pre += T[s];
+      ++s;
+    }
+    const int64_t local = y - acc, g = local / seg, r = local - g * seg;
+    // tile j of a segment starts at cost 0 (j = 0) or w8 + 8 j (j >= 1)
+    const int64_t j = r == 0 ? 0 : std::max<int64_t>(1, (r - w8 + 7) / 8);
+    bnd[c] = static_cast<int32_t>(pre * hkv + g * T[s] + std::min(j, T[s]));
+  }
+  bnd[ctas] = static_cast<int32_t>(U);
+}
+
+}  // namespace
+}  // namespace mtn
+
 extern "C" {
+
+size_t mtn_paged_decode_plan_bytes(int32_t head_dim) {
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return 0;
+  return (mtn::plan_words(mtn::decode_ctas(head_dim)) * 4 + 255) & ~static_cast<size_t>(255);
+}
+
+int mtn_paged_decode_plan(const int32_t* kv_indptr, const int32_t* seq_lens, int32_t n_seqs, int32_t page_size,
+                          int32_t num_kv_heads, int32_t head_dim, void* plan, size_t plan_bytes) {
+  MTN_CHECK_ARG(n_seqs >= 0 && page_size > 0 && num_kv_heads > 0, "mtn_paged_decode_plan: bad sizes");
+  MTN_CHECK_ARG(n_seqs == 0 || (kv_indptr && seq_lens), "mtn_paged_decode_plan: null metadata");
+  const size_t need = mtn_paged_decode_plan_bytes(head_dim);
+  MTN_CHECK_ARG(need > 0, "mtn_paged_decode_plan: head_dim %d not in {64,128,256}", head_dim);
+  MTN_CHECK_ARG(plan != nullptr && plan_bytes >= need, "mtn_paged_decode_plan: plan buffer of %zu bytes < %zu",
+                plan_bytes, need);
+  const int grid = mtn::decode_ctas(head_dim);
+  // Valid lengths clamped to each block table, as the kernel clamps them.
+  std::vector<int64_t> T(static_cast<size_t>(n_seqs)), len(static_cast<size_t>(n_seqs));
+  int64_t tiles = 0;
+  for (int32_t s = 0; s < n_seqs; ++s) {
+    const int64_t cap = static_cast<int64_t>(kv_indptr[s + 1] - kv_indptr[s]) * page_size;
+    len[s] = std::min<int64_t>(std::max<int64_t>(seq_lens[s], 0), std::max<int64_t>(cap, 0));
+    T[s] = (len[s] + mtn::kTile - 1) / mtn::kTile;
+    tiles += T[s];
+  }
+  const int64_t U = tiles * num_kv_heads;
+  MTN_CHECK_ARG(U < (int64_t(1) << 31), "mtn_paged_decode_plan: %lld tiles exceed the plan's int32 range",
+                static_cast<long long>(U));
+  const int64_t ctas = std::min<int64_t>(grid, U);
+  int32_t* w = static_cast<int32_t*>(plan);
+  std::memset(w, 0, need);
+  w[0] = mtn::kPlanMagic;
+  w[1] = static_cast<int32_t>(ctas);
+  w[2] = grid;
+  w[3] = static_cast<int32_t>(U);
+  int32_t* bnd = w + 4 + mtn::kPlanEntry * grid;
+  if (ctas > 0) mtn::split_tiles(T, num_kv_heads, U, ctas, bnd);
+  for (int64_t c = ctas + 1; c <= grid; ++c) bnd[c] = static_cast<int32_t>(U);
+  int32_t s = 0;
+  int64_t pre = 0;
+  for (int64_t c = 0; c < ctas; ++c) {
+    const int64_t t0 = bnd[c];
+    while ((pre + T[s]) * num_kv_heads <= t0) {  // the sequence holding tile t0
+      pre += T[s];
+      ++s;
+    }
+    int32_t* e = w + 4 + mtn::kPlanEntry * c;
+    e[0] = static_cast<int32_t>(t0);
+    e[1] = bnd[c + 1] - bnd[c];
+    e[2] = s;
+    e[3] = static_cast<int32_t>(pre);
+    e[4] = static_cast<int32_t>(len[s]);
+    e[5] = kv_indptr[s];
+  }
+  return MTN_OK;
+}
 
 size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                                         int32_t head_dim) {
@@ -1130,11 +1283,11 @@ size_t mtn_paged_decode_workspace_bytes(int32_t n_seqs, int32_t num_q_heads, int
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
-int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
-                     int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
-                     int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,
-                     const int32_t* seq_lens, float scale, uint32_t flags, void* workspace, size_t workspace_bytes,
-                     void* stream) {
+int mtn_paged_decode_with_plan(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                               int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype,
+                               int32_t n_seqs, int32_t num_q_heads, const int32_t* kv_indptr,
+                               const int32_t* kv_indices, const int32_t* seq_lens, float scale, uint32_t flags,
+                               const void* plan, void* workspace, size_t workspace_bytes, void* stream) {
   int st = mtn::validate_layout(pool, layer, "mtn_paged_decode");
   if (st != MTN_OK) return st;
   MTN_CHECK_ARG(n_seqs >= 0, "mtn_paged_decode: n_seqs < 0");
@@ -1196,6 +1349,8 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
   prm.ws_ml = prm.ws_o + slots * D;
   prm.ws_cnt = reinterpret_cast<unsigned int*>(prm.ws_ml + slots * 2);
   prm.err = mtn::device_error_ptr();
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(plan) & 15) == 0, "mtn_paged_decode: plan must be 16-byte aligned");
+  prm.plan = static_cast<const int32_t*>(plan);
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
   const bool prec = (flags & MTN_ATTN_SPLIT_BF16) != 0;
@@ -1204,6 +1359,16 @@ int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, in
     case 128: return mtn::dispatch_prec<128>(prec, nrep, tkv, tq, prm, s);
     default: return mtn::dispatch_prec<256>(prec, nrep, tkv, tq, prm, s);
   }
+}
+
+int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                     int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
+                     int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,
+                     const int32_t* seq_lens, float scale, uint32_t flags, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return mtn_paged_decode_with_plan(pool, layer, q, q_dtype, o, o_dtype, k_new, v_new, new_dtype, n_seqs, num_q_heads,
+                                    kv_indptr, kv_indices, seq_lens, scale, flags, nullptr, workspace,
+                                    workspace_bytes, stream);
 }
 
 }  // extern "C"

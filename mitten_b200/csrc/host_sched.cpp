@@ -302,6 +302,72 @@ struct Sched {
     return MTN_OK;
   }
 
+  // Prefill -> decode handoff (the reference's KvHandoff: request id, its
+  // pages, the tokens they hold).  Export: a Decoding request leaves this
+  // scheduler; the caller gets its pages (pack them before this scheduler's
+  // next launch) and its state, and the request's page references are
+  // returned (it ends Done here).
+  int export_request(uint64_t id, std::vector<uint32_t>* pages, int64_t* device_len,
+                     std::vector<uint32_t>* outputs) {
+    auto it = reqs.find(id);
+    MTN_CHECK_ARG(it != reqs.end(), "mtn_sched_export: unknown request %llu", (unsigned long long)id);
+    Req* r = it->second.get();
+    MTN_CHECK_ARG(r->state == MTN_REQ_DECODING, "mtn_sched_export: request %llu is not decoding",
+                  (unsigned long long)id);
+    *pages = r->kv_pages;
+    *device_len = r->device_len;
+    *outputs = r->output_ids;
+    r->state = MTN_REQ_DONE;
+    release_request(r);
+    erase_from(decoding, r);
+    return take_fault();
+  }
+
+  // Import: admit a handed-over request straight into Decoding with
+  // device_len tokens of KV on pages allocated here (returned: unpack the KV
+  // into them before its next decode batch).
+  int import_request(uint64_t id, const uint32_t* input_ids, int64_t n_input, const uint32_t* outputs,
+                     int64_t n_output, int64_t device_len, float temperature, int32_t max_new_tokens,
+                     std::vector<uint32_t>* pages) {
+    // A finished request (Done or Aborted, no pages) may come back under its
+    // id: a request swapped out to host memory by export and swapped in again.
+    auto prev = reqs.find(id);
+    MTN_CHECK_ARG(prev == reqs.end() || ((prev->second->state == MTN_REQ_DONE || prev->second->state == MTN_REQ_ABORTED) &&
+                                         prev->second->kv_pages.empty()),
+                  "mtn_sched_import: request id %llu is still live here", (unsigned long long)id);
+    MTN_CHECK_ARG(input_ids && n_input > 0 && n_output >= 1 && outputs && device_len >= n_input &&
+                      device_len < n_input + n_output,
+                  "mtn_sched_import: inconsistent request (prompt %lld, outputs %lld, device_len %lld)",
+                  (long long)n_input, (long long)n_output, (long long)device_len);
+    const int64_t ps = cfg.page_size;
+    const int64_t need = (device_len + ps - 1) / ps;
+    auto r = std::make_unique<Req>();
+    r->id = id;
+    r->input_ids.assign(input_ids, input_ids + n_input);
+    r->output_ids.assign(outputs, outputs + n_output);
+    r->temperature = temperature;
+    r->max_new_tokens = max_new_tokens;
+    r->device_len = device_len;
+    while (static_cast<int64_t>(r->kv_pages.size()) < need) {
+      uint32_t p = 0;
+      if (!alloc_page(r.get(), &p)) {
+        drop_pages(r->kv_pages);
+        return set_error(MTN_ENOMEM, "mtn_sched_import: %lld pages needed, the pool is exhausted", (long long)need);
+      }
+      r->kv_pages.push_back(p);
+    }
+    r->state = MTN_REQ_DECODING;
+    *pages = r->kv_pages;
+    decoding.push_back(r.get());
+    if (prev != reqs.end()) {
+      std::replace(batch.begin(), batch.end(), prev->second.get(), r.get());
+      prev->second = std::move(r);
+    } else {
+      reqs.emplace(id, std::move(r));
+    }
+    return MTN_OK;
+  }
+
   int schedule(mtn_batch_view* out, int32_t* has_batch) {
     // scheduler.rs:8-27.
     *has_batch = 0;
@@ -574,6 +640,43 @@ int mtn_sched_request_output(const mtn_sched* s, uint64_t req_id, uint32_t* out,
                 "mtn_sched_request_output: buffer too small (%zu tokens)", v.size());
   std::copy(v.begin(), v.end(), out);
   *n_out = static_cast<int64_t>(v.size());
+  return MTN_OK;
+}
+
+int mtn_sched_export(mtn_sched* s, uint64_t req_id, uint32_t* pages, int64_t* n_pages, int64_t* device_len,
+                     uint32_t* output_ids, int64_t* n_output) {
+  MTN_CHECK_ARG(s && n_pages && device_len && n_output, "mtn_sched_export: null argument");
+  auto it = s->impl.reqs.find(req_id);
+  MTN_CHECK_ARG(it != s->impl.reqs.end(), "mtn_sched_export: unknown request %llu", (unsigned long long)req_id);
+  const mtn::Req& r = *it->second;
+  MTN_CHECK_ARG(static_cast<int64_t>(r.kv_pages.size()) <= *n_pages && (pages || r.kv_pages.empty()) &&
+                    static_cast<int64_t>(r.output_ids.size()) <= *n_output && (output_ids || r.output_ids.empty()),
+                "mtn_sched_export: buffers too small (%zu pages, %zu tokens)", r.kv_pages.size(), r.output_ids.size());
+  std::vector<uint32_t> pg, out;
+  int64_t dl = 0;
+  const int st = s->impl.export_request(req_id, &pg, &dl, &out);
+  if (st != MTN_OK) return st;
+  std::copy(pg.begin(), pg.end(), pages);
+  std::copy(out.begin(), out.end(), output_ids);
+  *n_pages = static_cast<int64_t>(pg.size());
+  *n_output = static_cast<int64_t>(out.size());
+  *device_len = dl;
+  return MTN_OK;
+}
+
+int mtn_sched_import(mtn_sched* s, uint64_t req_id, const uint32_t* input_ids, int64_t n_input,
+                     const uint32_t* output_ids, int64_t n_output, int64_t device_len, float temperature,
+                     int32_t max_new_tokens, uint32_t* pages, int64_t* n_pages) {
+  MTN_CHECK_ARG(s && n_pages, "mtn_sched_import: null argument");
+  const int64_t need = (device_len + s->impl.cfg.page_size - 1) / s->impl.cfg.page_size;
+  MTN_CHECK_ARG(device_len >= 0 && need <= *n_pages && (pages || need == 0),
+                "mtn_sched_import: page buffer too small (%lld pages)", (long long)need);
+  std::vector<uint32_t> pg;
+  const int st = s->impl.import_request(req_id, input_ids, n_input, output_ids, n_output, device_len, temperature,
+                                        max_new_tokens, &pg);
+  if (st != MTN_OK) return st;
+  std::copy(pg.begin(), pg.end(), pages);
+  *n_pages = static_cast<int64_t>(pg.size());
   return MTN_OK;
 }
 

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kThreads) kv_append_kernel(
     __nv_bfloat16* __restrict__ kdst, __nv_bfloat16* __restrict__ vdst, int64_t num_pages, int hkv, int ps,
     int d, const SrcT* __restrict__ k, const SrcT* __restrict__ v, int64_t src_stride,
     const int64_t* __restrict__ slots, int64_t n_tokens, int* err, int lg_chunks, int lg_per_tok) {
+  pdl_enter();
   const int chunks = d >> 3;
   const Idx per_tok = static_cast<Idx>(hkv) * chunks;
   const Idx total = static_cast<Idx>(n_tokens) * per_tok;
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kThreads) page_copy_kernel(__nv_bfloat16* __re
                                                              const int32_t* __restrict__ src,
                                                              const int32_t* __restrict__ dst, int64_t n_pairs,
                                                              int* err) {
+  pdl_enter();
   uint4* p4 = reinterpret_cast<uint4*>(pool);
   const Idx pv = static_cast<Idx>(page_vecs);
   const Idx units = static_cast<Idx>(n_pairs) * num_layers * 2;
@@ -174,6 +176,50 @@ __global__ void __launch_bounds__(kThreads) page_copy_kernel(__nv_bfloat16* __re
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       if (to[u] >= 0) p4[to[u]] = val[u];
+    }
+  }
+}
+
+// Pages between the pool and a flat buffer [n_pages][layers][2 (K, V)]
+// [page_vecs x 16 bytes] (KV offload and prefill -> decode handoff):
+// kUnpack false copies pool -> buffer, true buffer -> pool.  The buffer may
+// be device memory, pinned host memory or a peer GPU's memory.
+template <typename Idx, bool kUnpack>
+__global__ void __launch_bounds__(kThreads) page_xfer_kernel(__nv_bfloat16* __restrict__ pool, int64_t num_pages,
+                                                             int num_layers, int64_t page_vecs,
+                                                             const int32_t* __restrict__ pages, int64_t n_pages,
+                                                             uint4* __restrict__ buf, int* err) {
+  uint4* p4 = reinterpret_cast<uint4*>(pool);
+  const Idx pv = static_cast<Idx>(page_vecs);
+  const Idx total = static_cast<Idx>(n_pages) * num_layers * 2 * pv;
+  const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
+  for (Idx base = blockIdx.x * static_cast<Idx>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * kUnroll) {
+    uint4 val[kUnroll];
+    int64_t at[kUnroll];  // pool vector of element u, -1 = skip
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const Idx i = base + u * stride;
+      at[u] = -1;
+      if (i < total) {
+        const Idx unit = i / pv;
+        const int64_t w = i - unit * pv;
+        const Idx pair = unit / static_cast<Idx>(num_layers * 2);
+        const int64_t lk = unit - pair * static_cast<Idx>(num_layers * 2);  // layer * 2 + kv
+        const int64_t pg = pages[pair];
+        if (pg < 0 || pg >= num_pages) {
+          record_error(err, kDevErrBadPage, static_cast<int>(pair));
+        } else {
+          at[u] = (lk * num_pages + pg) * page_vecs + w;
+          val[u] = kUnpack ? buf[i] : p4[at[u]];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (at[u] < 0) continue;
+      if (kUnpack) p4[at[u]] = val[u];
+      else buf[base + u * stride] = val[u];
     }
   }
 }
@@ -269,6 +315,37 @@ int validate_layout(const mtn_kv_layout* pool, int layer, const char* who) { ret
 
 using mtn::set_error;
 
+namespace mtn {
+namespace {
+
+template <bool kUnpack>
+int pages_xfer(const mtn_kv_layout* pool, const int32_t* pages, int64_t n_pages, void* buf, void* stream,
+               const char* who) {
+  int st = check_layout(pool, 0, who);
+  if (st != MTN_OK) return st;
+  MTN_CHECK_ARG(n_pages >= 0, "%s: n_pages < 0", who);
+  if (n_pages == 0) return MTN_OK;
+  MTN_CHECK_ARG(pages && buf, "%s: null pointer", who);
+  MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(buf) & 15) == 0, "%s: buffer must be 16-byte aligned", who);
+  const int64_t page_vecs = static_cast<int64_t>(pool->num_kv_heads) * pool->page_size * pool->head_dim / 8;
+  const int64_t work = n_pages * pool->num_layers * 2 * page_vecs;
+  const int grid = grid_for(work, kThreads * kUnroll);
+  const bool narrow = work + static_cast<int64_t>(grid) * kThreads * kUnroll < (int64_t(1) << 31);
+  auto* base = static_cast<__nv_bfloat16*>(pool->base);
+  auto* b4 = static_cast<uint4*>(buf);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (narrow)
+    page_xfer_kernel<uint32_t, kUnpack><<<grid, kThreads, 0, s>>>(
+        base, pool->num_pages, pool->num_layers, page_vecs, pages, n_pages, b4, device_error_ptr());
+  else
+    page_xfer_kernel<int64_t, kUnpack><<<grid, kThreads, 0, s>>>(
+        base, pool->num_pages, pool->num_layers, page_vecs, pages, n_pages, b4, device_error_ptr());
+  return check_launch("page_xfer_kernel");
+}
+
+}  // namespace
+}  // namespace mtn
+
 extern "C" {
 
 int mtn_build_slot_mapping(const int32_t* qo_indptr, const int32_t* positions, const int32_t* kv_indptr,
@@ -313,10 +390,10 @@ int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer, const void* k, const
   const bool p2 = (chunks & (chunks - 1)) == 0 && (per_tok & (per_tok - 1)) == 0;
   const int lg_c = p2 ? __builtin_ctz(static_cast<unsigned>(chunks)) : 0;
   const int lg_t = p2 ? __builtin_ctz(static_cast<unsigned>(per_tok)) : 0;
-#define MTN_APPEND_LAUNCH(SRC, IDX, P2F, KP, VP)                                                              \
-  mtn::kv_append_kernel<SRC, IDX, P2F><<<grid, mtn::kThreads, 0, s>>>(                                       \
-      kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size, pool->head_dim, KP, VP, src_stride, slots, \
-      n_tokens, mtn::device_error_ptr(), lg_c, lg_t)
+#define MTN_APPEND_LAUNCH(SRC, IDX, P2F, KP, VP)                                                               \
+  return mtn::launch_pdl(mtn::kv_append_kernel<SRC, IDX, P2F>, dim3(grid), dim3(mtn::kThreads), 0, s,           \
+                         "kv_append_kernel", kd, vd, pool->num_pages, pool->num_kv_heads, pool->page_size,       \
+                         pool->head_dim, KP, VP, src_stride, slots, n_tokens, mtn::device_error_ptr(), lg_c, lg_t)
   if (src_dtype == MTN_DTYPE_BF16) {
     auto kb = static_cast<const __nv_bfloat16*>(k);
     auto vb = static_cast<const __nv_bfloat16*>(v);
@@ -345,15 +422,29 @@ int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages, const int
   const int64_t work = n_pages * pool->num_layers * 2 * page_vecs;
   const int grid = mtn::grid_for(work, mtn::kThreads * mtn::kUnroll);
   const bool narrow = work + static_cast<int64_t>(grid) * mtn::kThreads * mtn::kUnroll < (int64_t(1) << 31);
+  auto* base = static_cast<__nv_bfloat16*>(pool->base);
+  auto s = static_cast<cudaStream_t>(stream);
   if (narrow)
-    mtn::page_copy_kernel<uint32_t><<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
-        n_pages, mtn::device_error_ptr());
-  else
-    mtn::page_copy_kernel<int64_t><<<grid, mtn::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__nv_bfloat16*>(pool->base), pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages,
-        n_pages, mtn::device_error_ptr());
-  return mtn::check_launch("page_copy_kernel");
+    return mtn::launch_pdl(mtn::page_copy_kernel<uint32_t>, dim3(grid), dim3(mtn::kThreads), 0, s, "page_copy_kernel",
+                           base, pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages, n_pages,
+                           mtn::device_error_ptr());
+  return mtn::launch_pdl(mtn::page_copy_kernel<int64_t>, dim3(grid), dim3(mtn::kThreads), 0, s, "page_copy_kernel",
+                         base, pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages, n_pages,
+                         mtn::device_error_ptr());
+}
+
+size_t mtn_kv_pages_bytes(const mtn_kv_layout* pool, int64_t n_pages) {
+  if (pool == nullptr || n_pages <= 0) return 0;
+  return static_cast<size_t>(n_pages) * pool->num_layers * 2 * pool->num_kv_heads * pool->page_size * pool->head_dim * 2;
+}
+
+int mtn_kv_pages_pack(const mtn_kv_layout* pool, const int32_t* pages, int64_t n_pages, void* dst, void* stream) {
+  return mtn::pages_xfer<false>(pool, pages, n_pages, dst, stream, "mtn_kv_pages_pack");
+}
+
+int mtn_kv_pages_unpack(const mtn_kv_layout* pool, const void* src, const int32_t* pages, int64_t n_pages,
+                        void* stream) {
+  return mtn::pages_xfer<true>(pool, pages, n_pages, const_cast<void*>(src), stream, "mtn_kv_pages_unpack");
 }
 
 int mtn_kv_gather(const mtn_kv_layout* pool, int32_t layer, const int32_t* kv_indptr, const int32_t* kv_indices,

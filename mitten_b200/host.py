@@ -255,6 +255,27 @@ class Scheduler:
         a, p = _u32(suffix)
         L.check(L.lib().mtn_sched_fork(self._h, parent_id, child_id, p, len(a), temperature, max_new_tokens))
 
+    def export_request(self, req_id: int) -> dict:
+        """Hand a decoding request over (KvHandoff): its pages, device_len and generated tokens."""
+        info = self.request_info(req_id)
+        npg, nout = max(info["n_pages"], 1), max(info["n_output"], 1)
+        pages, outs = (C.c_uint32 * npg)(), (C.c_uint32 * nout)()
+        n_p, n_o, dl = C.c_int64(npg), C.c_int64(nout), C.c_int64()
+        L.check(L.lib().mtn_sched_export(self._h, req_id, pages, C.byref(n_p), C.byref(dl), outs, C.byref(n_o)))
+        return {"pages": list(pages[:n_p.value]), "device_len": dl.value, "outputs": list(outs[:n_o.value])}
+
+    def import_request(self, req_id: int, input_ids, outputs, device_len: int, temperature: float = 0.0,
+                       max_new_tokens: int = 512) -> list[int]:
+        """Admit a handed-over request as Decoding; returns the pages to unpack its KV into."""
+        a, ap = _u32(input_ids)
+        o, op = _u32(outputs)
+        cap = (device_len + self.page_size - 1) // self.page_size
+        pages = (C.c_uint32 * max(cap, 1))()
+        n = C.c_int64(max(cap, 1))
+        L.check(L.lib().mtn_sched_import(self._h, req_id, ap, len(a), op, len(o), device_len, temperature,
+                                         max_new_tokens, pages, C.byref(n)))
+        return list(pages[:n.value])
+
     def page_refcount(self, page: int) -> int:
         return int(L.lib().mtn_sched_page_refcount(self._h, page))
 

@@ -72,8 +72,12 @@ class QwenPagedModel:
     """Qwen3_5Model (all layers full attention) over a PagedKVPool."""
 
     def __init__(self, shape: DecoderShape, weights: dict, num_pages: int, page_size: int = 16,
-                 device: torch.device | str = "cuda", split_bf16: bool = True):
+                 device: torch.device | str = "cuda", split_bf16: bool = True, dtype: torch.dtype = torch.float32,
+                 fused_prologue: bool = True):
         self.s = shape
+        # Dense weights and activations in `dtype` (f32: the reference's CPU
+        # path; bf16: the random-bf16 configs 3-5).  RoPE is applied in f32 and
+        # the attention kernels take f32 q/k/v either way.
         # The dense path is f32, like the reference's (model.rs:413-416
         # multiplies in f32): q and the softmax weights reach the tensor cores
         # as bf16 hi + lo pairs (MTN_ATTN_SPLIT_BF16) unless split_bf16=False;
@@ -81,7 +85,11 @@ class QwenPagedModel:
         self.split_dec = split_bf16
         self.split_pre = split_bf16 and shape.head_dim <= 128
         self.dev = torch.device(device)
-        self.w = {k: torch.as_tensor(v).to(self.dev, torch.float32) for k, v in weights.items()}
+        self.dt = dtype
+        # fused_prologue: q/k RMSNorm + RoPE + the K/V store in one kernel
+        # (mtn_qkv_prologue) instead of torch ops and a separate append.
+        self.fused = fused_prologue and shape.rotary_dim % 64 == 0
+        self.w = {k: torch.as_tensor(v).to(self.dev, dtype) for k, v in weights.items()}
         # RMSNorm scales (1 + w), formed once
         for k in [k for k in self.w if k.endswith("norm.weight")]:
             self.w[k] = self.w[k] + 1.0
@@ -92,10 +100,13 @@ class QwenPagedModel:
         inv = np.float32(1.0) / np.power(np.float32(shape.theta), np.float32(2.0) * i / np.float32(shape.rotary_dim),
                                          dtype=np.float32)
         self.inv_freq = torch.from_numpy(inv.astype(np.float32)).to(self.dev)
+        # (1 + w) of the q/k norms in f32 for the fused prologue
+        self.w32 = {k: v.float().contiguous() for k, v in self.w.items() if k.endswith(("q_norm.weight", "k_norm.weight"))}
         self.scale = shape.head_dim ** -0.5
         self._ws = None
         self._ws_seqs = 0
         self._pws = None
+        self._plan = None
         self._graphs: dict[int, _DecodeGraph] = {}
 
     # ------------------------------------------------------------ pieces
@@ -156,22 +167,40 @@ class QwenPagedModel:
             q, gate = qp.view(T, s.hq, s.head_dim), None
         k = (h @ w[f"{m}.k_proj.weight"].T).view(T, s.hkv, s.head_dim)
         v = (h @ w[f"{m}.v_proj.weight"].T).view(T, s.hkv, s.head_dim)
-        if s.qk_norm:
-            q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
-            k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
-        q, k = self._rope(q, cs), self._rope(k, cs)
         attn = torch.empty((T, s.hq, s.head_dim), dtype=torch.float32, device=self.dev)
         tp = meta["tp"]
+        if self.fused:
+            # q/k norms, RoPE and every row's K/V store in one launch; the
+            # attention kernels then find the step's rows in the pool
+            q = torch.empty((T, s.hq, s.head_dim), dtype=torch.float32, device=self.dev)
+            qp = qp.contiguous()
+            kc, vc = k.contiguous(), v.contiguous()
+            qw, kw = (self.w32.get(f"{m}.q_norm.weight"), self.w32.get(f"{m}.k_norm.weight")) if s.qk_norm else (None, None)
+            L.check(L.lib().mtn_qkv_prologue(
+                paged.C.byref(self.pool.layout), li, qp.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                paged._dtype_code(self.dt), qp.shape[1], s.hkv * s.head_dim, s.hkv * s.head_dim, int(s.gated_q), s.hq,
+                None if qw is None else qw.data_ptr(), None if kw is None else kw.data_ptr(), s.eps,
+                self.inv_freq.data_ptr(), s.rotary_dim, meta["pos"].data_ptr(), meta["slots_all"].data_ptr(), T,
+                q.data_ptr(), paged._stream(None)))
+            k_new = v_new = None
+        else:
+            v = v.float()
+            if s.qk_norm:
+                q = _rms(q, w[f"{m}.q_norm.weight"], s.eps)
+                k = _rms(k, w[f"{m}.k_norm.weight"], s.eps)
+            q, k = self._rope(q.float(), cs), self._rope(k.float(), cs)
+            if tp:
+                self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
+            k_new, v_new = (k[tp:].contiguous(), v[tp:].contiguous()) if T > tp else (None, None)
         if tp:
-            self.pool.append(li, k[:tp].contiguous(), v[:tp].contiguous(), meta["slots"])
             paged.paged_prefill(self.pool, li, q[:tp].contiguous(), meta["qo_p"], meta["kv_p"],
                                 meta["kv_indices"], meta["len_p"], meta["max_q"], scale=self.scale, phantom=s.phantom,
                                 out=attn[:tp], workspace=meta["pws"], split_bf16=self.split_pre)
         if T > tp:
             paged.paged_decode(self.pool, li, q[tp:].contiguous(), meta["kv_d"], meta["kv_indices"], meta["len_d"],
-                               scale=self.scale, phantom=s.phantom, k_new=k[tp:].contiguous(), v_new=v[tp:].contiguous(),
-                               out=attn[tp:], workspace=meta["ws"], split_bf16=self.split_dec)
-        o = attn.view(T, s.hq * s.head_dim)
+                               scale=self.scale, phantom=s.phantom, k_new=k_new, v_new=v_new,
+                               out=attn[tp:], workspace=meta["ws"], split_bf16=self.split_dec, plan=meta.get("plan"))
+        o = attn.view(T, s.hq * s.head_dim).to(self.dt)
         if gate is not None:
             o = torch.sigmoid(gate) * o
         return o @ w[f"{m}.o_proj.weight"].T
@@ -183,7 +212,9 @@ class QwenPagedModel:
         n, npf = b.n_reqs, b.n_prefill
         qo = b.qo_indptr
         tp = int(qo[npf])
-        meta = {"tp": tp, "kv_indices": torch.from_numpy(np.ascontiguousarray(b.kv_indices, np.int32)).to(dev)}
+        meta = {"tp": tp, "kv_indices": torch.from_numpy(np.ascontiguousarray(b.kv_indices, np.int32)).to(dev),
+                "qo_all": torch.from_numpy(np.ascontiguousarray(qo, np.int32)).to(dev),
+                "kv_all": torch.from_numpy(np.ascontiguousarray(b.kv_indptr, np.int32)).to(dev)}
         if npf:
             meta["qo_p"] = torch.from_numpy(np.ascontiguousarray(qo[:npf + 1], np.int32)).to(dev)
             meta["kv_p"] = torch.from_numpy(np.ascontiguousarray(b.kv_indptr[:npf + 1], np.int32)).to(dev)
@@ -197,6 +228,10 @@ class QwenPagedModel:
             meta["kv_d"] = torch.from_numpy(np.ascontiguousarray(b.kv_indptr[npf:], np.int32)).to(dev)
             meta["len_d"] = torch.from_numpy(np.ascontiguousarray(b.seq_lens[npf:], np.int32)).to(dev)
             meta["ws"] = self._decode_ws(n - npf)
+            # one host-made work plan serves the decode rows of every layer
+            if self._plan is None:
+                self._plan = paged.DecodePlan(self.s.head_dim, dev)
+            meta["plan"] = self._plan.build(b.kv_indptr[npf:], b.seq_lens[npf:], self.pool.page_size, self.s.hkv)
         return meta
 
     def _cow(self, b) -> None:
@@ -208,13 +243,19 @@ class QwenPagedModel:
         """The device part of the forward: every launch depends only on tensors, so it can be captured."""
         s, w = self.s, self.w
         x = w["embedding.weight"][ids]  # the vocab-split lookup of model.rs:159-183 is a plain lookup
-        cs = self._rope_tables(pos)
+        if self.fused:
+            # every row's pool slot (prefill chunks and decode tokens alike)
+            meta = dict(meta, pos=pos, slots_all=paged.build_slot_mapping(meta["qo_all"], pos, meta["kv_all"],
+                                                                         meta["kv_indices"], self.pool.page_size))
+            cs = None
+        else:
+            cs = self._rope_tables(pos)
         for li in range(s.layers):
             p = f"layers.{li}"
             x = x + self._attention(li, _rms(x, w[f"{p}.norm.weight"], s.eps), cs, meta)
             x = x + self._mlp(_rms(x, w[f"{p}.ffn_norm.weight"], s.eps), p)
         h = _rms(x[last], w["norm.weight"], s.eps)
-        return (h @ w["embedding.weight"].T).contiguous()  # tied LM head (model.rs:262-276)
+        return (h @ w["embedding.weight"].T).float().contiguous()  # tied LM head (model.rs:262-276)
 
     @torch.no_grad()
     def forward(self, b) -> torch.Tensor:
@@ -259,8 +300,10 @@ class _DecodeGraph:
         self.kv_indices = torch.zeros(max(model.pool.num_pages, 1), dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(n, dtype=torch.int32, device=dev)
         self.last = torch.arange(n, dtype=torch.int64, device=dev)
+        self.plan = paged.DecodePlan(model.s.head_dim, dev)
         self.meta = {"tp": 0, "kv_indices": self.kv_indices, "kv_d": self.kv_indptr, "len_d": self.seq_lens,
-                     "ws": paged.DecodeWorkspace.for_shape(model.pool, n, model.s.hq)}
+                     "qo_all": torch.arange(n + 1, dtype=torch.int32, device=dev), "kv_all": self.kv_indptr,
+                     "ws": paged.DecodeWorkspace.for_shape(model.pool, n, model.s.hq), "plan": self.plan}
         self.graph = None
         self.out = None
 
@@ -273,6 +316,7 @@ class _DecodeGraph:
         self.kv_indptr.copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indptr, np.int32)))
         self.kv_indices[:nk].copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indices[:nk], np.int32)))
         self.seq_lens.copy_(torch.from_numpy(np.ascontiguousarray(b.seq_lens, np.int32)))
+        self.plan.build(b.kv_indptr, b.seq_lens, self.model.pool.page_size, self.model.s.hkv)
 
     def run(self, b) -> torch.Tensor:
         self._fill(b)

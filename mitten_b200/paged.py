@@ -9,6 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import math
 
+import numpy as np
 import torch
 
 from . import _lib as L
@@ -142,17 +143,51 @@ class DecodeWorkspace:
         return cls(nb, pool.device)
 
 
+class DecodePlan:
+    """Host-made work plan for paged_decode (mtn_paged_decode_plan): each CTA's tile range and start,
+    balanced by cost, from host copies of the batch's kv_indptr and seq_lens.  build() fills the pinned
+    host copy and queues its upload on `stream`; one plan serves every layer of a step."""
+
+    def __init__(self, head_dim: int, device):
+        self.head_dim = head_dim
+        self.nbytes = int(L.lib().mtn_paged_decode_plan_bytes(head_dim))
+        if self.nbytes == 0:
+            raise ValueError(f"head_dim {head_dim} has no decode plan")
+        self.host = torch.empty(self.nbytes, dtype=torch.uint8).pin_memory()
+        self.dev = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+
+    def build(self, kv_indptr, seq_lens, page_size: int, num_kv_heads: int, stream=None) -> "DecodePlan":
+        ip = np.ascontiguousarray(np.asarray(kv_indptr), dtype=np.int32)
+        ln = np.ascontiguousarray(np.asarray(seq_lens), dtype=np.int32)
+        if ip.size != ln.size + 1:
+            raise ValueError("kv_indptr must have n_seqs + 1 entries")
+        i32 = C.POINTER(C.c_int32)
+        L.check(L.lib().mtn_paged_decode_plan(ip.ctypes.data_as(i32), ln.ctypes.data_as(i32), ln.size, page_size,
+                                              num_kv_heads, self.head_dim, self.host.data_ptr(), self.nbytes))
+        s = stream if stream is not None else torch.cuda.current_stream(self.dev.device)
+        with torch.cuda.stream(s):
+            self.dev.copy_(self.host, non_blocking=True)
+        return self
+
+    def words(self) -> np.ndarray:
+        """The host copy as int32 words (for tests)."""
+        return self.host.numpy().view(np.int32).copy()
+
+
 def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torch.Tensor,
                  kv_indices: torch.Tensor, seq_lens: torch.Tensor, scale: float | None = None,
                  phantom: bool = False, k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-                 workspace: DecodeWorkspace | None = None, stream=None, split_bf16: bool = False) -> torch.Tensor:
+                 workspace: DecodeWorkspace | None = None, stream=None, split_bf16: bool = False,
+                 plan: DecodePlan | None = None) -> torch.Tensor:
     """Decode attention for q [n_seqs, num_q_heads, head_dim] over the paged cache.
 
     With k_new/v_new [n_seqs, kv_heads, head_dim] the step's token is first
     stored at position seq_lens[r]-1 of each sequence (fused KV append).
     `split_bf16` passes Q and P to the tensor cores as bf16 hi + lo pairs
     (MTN_ATTN_SPLIT_BF16): f32-level products at no extra tensor-core work.
+    `plan` (DecodePlan built for these kv_indptr / seq_lens) replaces the
+    kernel's own scan and even split of the tiles.
     """
     if q.dim() != 3 or not q.is_contiguous():
         raise ValueError("q must be a contiguous [n_seqs, heads, head_dim] tensor")
@@ -173,10 +208,12 @@ def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torc
             raise ValueError("k_new/v_new shape or dtype mismatch")
         new_code = _dtype_code(k_new.dtype)
     flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_SPLIT_BF16 if split_bf16 else 0)
-    L.check(L.lib().mtn_paged_decode(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype), _ptr(out),
-                                     _dtype_code(out.dtype), _ptr(k_new), _ptr(v_new), new_code, n, hq,
-                                     _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)), _ptr(_i32(seq_lens)),
-                                     float(scale), flags, _ptr(workspace.buf), workspace.nbytes, _stream(stream)))
+    L.check(L.lib().mtn_paged_decode_with_plan(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype),
+                                               _ptr(out), _dtype_code(out.dtype), _ptr(k_new), _ptr(v_new), new_code,
+                                               n, hq, _ptr(_i32(kv_indptr)), _ptr(_i32(kv_indices)),
+                                               _ptr(_i32(seq_lens)), float(scale), flags,
+                                               None if plan is None else plan.dev.data_ptr(), _ptr(workspace.buf),
+                                               workspace.nbytes, _stream(stream)))
     return out
 
 
@@ -218,6 +255,27 @@ def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: tor
                                       _ptr(_i32(seq_lens)), max_q_len, float(scale), flags, _ptr(workspace),
                                       0 if workspace is None else workspace.numel(), _stream(stream)))
     return out
+
+
+def pack_pages(pool: PagedKVPool, pages: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Pages (every layer, K and V) into a flat [n_pages, layers, 2, kv_heads, page_size, head_dim] bf16
+    buffer (mtn_kv_pages_pack): device memory, or pinned host memory for offload."""
+    n = pages.numel()
+    shape = (n, pool.num_layers, 2, pool.num_kv_heads, pool.page_size, pool.head_dim)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=pool.device)
+    if out.numel() * 2 < L.lib().mtn_kv_pages_bytes(C.byref(pool.layout), n) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous buffer of mtn_kv_pages_bytes bytes")
+    L.check(L.lib().mtn_kv_pages_pack(C.byref(pool.layout), _ptr(_i32(pages)), n, out.data_ptr(), _stream(stream)))
+    return out
+
+
+def unpack_pages(pool: PagedKVPool, src: torch.Tensor, pages: torch.Tensor, stream=None) -> None:
+    """The reverse of pack_pages: src's pages into the listed pool pages (mtn_kv_pages_unpack)."""
+    n = pages.numel()
+    if src.numel() * src.element_size() < L.lib().mtn_kv_pages_bytes(C.byref(pool.layout), n) or not src.is_contiguous():
+        raise ValueError("src must be a contiguous buffer of mtn_kv_pages_bytes bytes")
+    L.check(L.lib().mtn_kv_pages_unpack(C.byref(pool.layout), src.data_ptr(), _ptr(_i32(pages)), n, _stream(stream)))
 
 
 def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:

@@ -281,3 +281,42 @@ def test_random_streams_no_leak(seed):
     assert all(e.s.request_info(r)["state"] in (_lib.MTN_REQ_DONE, _lib.MTN_REQ_ABORTED) for r in e.ids)
     tree = e.s.tree_pages()
     assert e.s.free_pages() + len(set(tree)) == num_pages
+
+
+def test_export_import_handoff():
+    """Prefill -> decode handoff (KvHandoff): a decoding request exported from
+    one scheduler leaves it with its references returned, and an import into
+    another admits it straight into Decoding on fresh pages, which then grow
+    as it decodes; both schedulers keep their page invariants."""
+    a, b = Engine(64, 4), Engine(64, 4)
+    a.add(1, list(range(30, 41)), max_new=6)  # 11 prompt tokens: 3 pages
+    a.step()  # prefill: first token out, Decoding
+    info = a.s.request_info(1)
+    assert info["state"] == _lib.MTN_REQ_DECODING and info["device_len"] == 11
+    h = a.s.export_request(1)
+    assert h["device_len"] == 11 and len(h["pages"]) == 3 and h["outputs"] == [7]
+    assert a.s.request_info(1)["state"] == _lib.MTN_REQ_DONE and a.s.request_pages(1) == []
+    a.invariants()
+    assert a.s.free_pages() + len(a.s.tree_pages()) == 64
+    pages = b.s.import_request(1, list(range(30, 41)), h["outputs"], h["device_len"], 0.0, 6)
+    b.ids.append(1)
+    assert len(pages) == 3 and b.s.request_info(1)["state"] == _lib.MTN_REQ_DECODING
+    b.invariants()
+    seen = []
+    while (bt := b.step()) is not None:
+        seen.append((int(bt.seq_lens[0]), int(bt.input_ids[0]), int(bt.position_ids[0])))
+    assert seen[0] == (12, 7, 11)  # the handed-over token is decoded at position 11
+    assert b.s.request_output(1) == [7] * 6 and b.s.free_pages() + len(b.s.tree_pages()) == 64
+
+
+def test_export_import_rejections():
+    a = Engine(8, 4)
+    a.add(1, [1, 2, 3], max_new=3)
+    with pytest.raises(_lib.MittenError, match="not decoding"):
+        a.s.export_request(1)
+    with pytest.raises(_lib.MittenError, match="inconsistent"):
+        a.s.import_request(2, [1, 2, 3], [5], 9, 0.0, 3)  # device_len past prompt + outputs
+    with pytest.raises(_lib.OutOfKvPages):
+        a.s.import_request(3, list(range(40)), [5], 40, 0.0, 3)  # 10 pages in an 8-page pool
+    a.invariants()
+    assert a.s.free_pages() == 8
