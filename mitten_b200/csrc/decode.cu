@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int sb = min(p.n_seqs, tid * chunk), se = min(p.n_seqs, sb + chunk);
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1 || i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
+      mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1) ? 4 : (i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
     *abort_flag = 0;
     *start_s = -1;
     fence_barrier_init();
@@ -510,16 +510,20 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     for (int k = 0; k < C::kStages; ++k)
       if (k < n_local && apos[k] >= 0) load_rows(asrc[k], ak[k], av[k]);
     bool run = true;
-    // Stage slot st of round i0 is tile i0 + st: unrolled so the ring
-    // registers are indexed with constants.
+    // Stage slot st of round i0 is tile i0 + st.  At two CTAs per SM (head_dim
+    // 64) the loop body is kept rolled (the smaller code measured faster
+    // there) and the ring registers rotate by one slot per tile, so tile i's
+    // values are always slot 0 and the fetch fills the last slot: constant
+    // indices keep the ring in registers (indexed by st it lived in local
+    // memory; rotating measured 2-4 % faster at 64-1024 sequences).  At
+    // head_dim >= 128 the body is unrolled and slot st holds tile i0 + st
+    // (config 5: 0.80 vs 0.74 of HBM for the rolled loop).
+    constexpr bool kRot = C::kCtasPerSm > 1;
     for (int i0 = 0; run && i0 < n_local; i0 += C::kStages) {
-      // At two CTAs per SM (head_dim 64) the loop body is kept rolled: the
-      // smaller code measured faster there (32.2 vs 33.2 us per config-2
-      // step), while the unrolled body with register-resident ring slots is
-      // faster at head_dim 128 (config 5: 0.80 vs 0.74 of HBM).
-#pragma unroll (C::kCtasPerSm > 1 ? 1 : C::kStages)
+#pragma unroll (kRot ? 1 : C::kStages)
       for (int st = 0; st < C::kStages; ++st) {
         const int i = i0 + st;
+        const int rs = kRot ? 0 : st;  // ring slot of tile i
         if (!run || i >= n_local) break;
         const bool first = (i == 0) || w.j == 0;
         if (first) {
@@ -575,15 +579,15 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             break;
           }
         }
-        if (apos[st] >= 0) {
+        if (apos[rs] >= 0) {
           // Fused KV append: store this step's row at position len-1, then
           // order it before the async-proxy (TMA) read of the same page.
-          if (apg[st] < 0 || apg[st] >= p.num_pages) {
+          if (apg[rs] < 0 || apg[rs] >= p.num_pages) {
             if (lane == 0) record_error(p.err, kDevErrBadPage, w.s);
           } else if (lane < D / 8) {
-            const int64_t arow = (static_cast<int64_t>(apg[st]) * p.hkv + w.g) * p.ps + apos[st];
-            *reinterpret_cast<uint4*>(p.pool + (p.row_k + arow) * D + lane * 8) = ak[st];
-            *reinterpret_cast<uint4*>(p.pool + (p.row_v + arow) * D + lane * 8) = av[st];
+            const int64_t arow = (static_cast<int64_t>(apg[rs]) * p.hkv + w.g) * p.ps + apos[rs];
+            *reinterpret_cast<uint4*>(p.pool + (p.row_k + arow) * D + lane * 8) = ak[rs];
+            *reinterpret_cast<uint4*>(p.pool + (p.row_v + arow) * D + lane * 8) = av[rs];
             asm volatile("fence.proxy.async.global;" ::: "memory");
           }
           __syncwarp();
@@ -592,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           // Items 4i..4i+3 of the ring: K blocks 0-1, K blocks 2-3, V blocks
           // 0-1, V blocks 2-3; item n sits in slot n % 6, refilled once the
           // MMA that read item n - 6 is done.
-          int64_t page = lane < tile_pages ? pg[st] : 0;
+          int64_t page = lane < tile_pages ? pg[rs] : 0;
           if (lane < tile_pages && (page < 0 || page >= p.num_pages)) {
             record_error(p.err, kDevErrBadPage, w.s);
             page = 0;  // past the sequence's last page: reload a valid page (masked)
@@ -625,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         if (lane == 0) mbar_arrive_expect_tx(&bars[kKVFull0 + st], 2 * C::kKVBytes);
         __syncwarp();
         if (lane < tile_pages) {
-          int64_t page = pg[st];
+          int64_t page = pg[rs];
           if (page < 0 || page >= p.num_pages) {
             record_error(p.err, kDevErrBadPage, w.s);
             page = 0;  // past the sequence's last page: reload a valid page (masked)
@@ -642,8 +646,20 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           }
         }
         }
+        if constexpr (kRot) {
+#pragma unroll
+          for (int k = 0; k + 1 < C::kStages; ++k) {
+            pg[k] = pg[k + 1];
+            apg[k] = apg[k + 1];
+            apos[k] = apos[k + 1];
+            asrc[k] = asrc[k + 1];
+            ak[k] = ak[k + 1];
+            av[k] = av[k + 1];
+          }
+        }
         if (i + C::kStages < n_local) {
-          fetch(pg[st], apg[st], apos[st], asrc[st], ak[st], av[st], true);  // wp is at tile i + kStages
+          const int fs = kRot ? C::kStages - 1 : st;  // wp is at tile i + kStages
+          fetch(pg[fs], apg[fs], apos[fs], asrc[fs], ak[fs], av[fs], true);
           if (i + C::kStages + 1 < n_local) wp.next(p);
         }
         if (i + 1 < n_local) w.next(p);
@@ -917,9 +933,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
                 __float2bfloat16_rn(sv[h] - __bfloat162float(hi));
         }
       }
+      // One arrival per softmax warp instead of 128 on one mbarrier word:
+      // each lane fences its P^T stores to the async proxy, the warp
+      // converges, lane 0 arrives.
       fence_proxy_async_shared();
       tc::fence_before_sync();
-      tc::mbar_arrive(&bars[kPFull0 + (i & 1)]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[kPFull0 + (i & 1)]);
 
       if (last) {
         // ---- segment epilogue: O^T of (s, g) over this CTA's tiles.
