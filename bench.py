@@ -440,7 +440,7 @@ def run_append_and_copy(st, pool, device, stream) -> dict:
 
     t = timed(cp)
     nbytes = 2 * n_pg * 2 * PS * HKV * D * 2 + 8 * n_pg
-    res["copy"] = {"kernel": "page_copy_kernel", "pages_per_call": n_pg, "bytes_per_call": nbytes,
+    res["copy"] = {"kernel": "page_copy_bulk_kernel", "pages_per_call": n_pg, "bytes_per_call": nbytes,
                    "us_per_call": 1e6 * t, "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / peak,
                    "peak_gbs": peak}
     return res

@@ -158,7 +158,10 @@ MTN_API int mtn_kv_append(const mtn_kv_layout* pool, int32_t layer,
                   const int64_t* slots, int64_t n_tokens, void* stream);
 
 /* Page copy for copy-on-write and prefix forks: for i < n_pages copy page
- * src[i] onto page dst[i] in every layer, K and V, every head. */
+ * src[i] onto page dst[i] in every layer, K and V, every head.  Pairs with
+ * src[i] == dst[i] are skipped; a page id outside the pool is recorded as
+ * device error 1 (detail = i) and its pair skipped.  Pages of up to 16 KB
+ * per (layer, K|V) move as whole slabs with 1-D bulk copies. */
 MTN_API int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages,
                   const int32_t* dst_pages, int64_t n_pages, void* stream);
 

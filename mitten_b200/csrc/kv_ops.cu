@@ -7,6 +7,7 @@
 // All are HBM-bound byte movers: 16-byte vector accesses, several loads in
 // flight per thread before the matching stores, grids sized in multiples of
 // the SM count.
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -178,6 +179,83 @@ __global__ void __launch_bounds__(kThreads) page_copy_kernel(__nv_bfloat16* __re
       if (to[u] >= 0) p4[to[u]] = val[u];
     }
   }
+}
+
+// Page copy with 1-D bulk copies.  Every (pair, layer, K|V) unit is one
+// contiguous slab of page_bytes at the source and the destination page.  A
+// CTA (one warp) takes up to 32 consecutive units: its lanes fetch their
+// units' page ids together, then lane 0 moves the slabs global -> shared ->
+// global (cp.async.bulk both ways) through a ring of `slots` buffers, so up
+// to `slots` slabs are in flight for a handful of instructions each.  A slot
+// is reloaded once the store that read it two steps earlier has read its
+// source (bulk_wait_read<2>), so loads run slots - 2 units ahead.
+constexpr int kCopyMaxSlots = 8;
+constexpr int kCopyLag = 2;
+constexpr int kCopyUnitsPerCta = 32;
+constexpr int64_t kCopyBulkMaxBytes = 16384;  // larger slabs take the vector kernel
+
+__global__ void __launch_bounds__(32) page_copy_bulk_kernel(uint8_t* __restrict__ pool, int64_t num_pages,
+                                                           int num_layers, int64_t page_bytes,
+                                                           const int32_t* __restrict__ src,
+                                                           const int32_t* __restrict__ dst, int64_t n_pairs,
+                                                           int units_per_cta, int slots, int* err) {
+  pdl_enter();
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ int64_t from_s[kCopyUnitsPerCta], to_s[kCopyUnitsPerCta];  // byte offsets, -1 = nothing to copy
+  const int lane = threadIdx.x;
+  const int64_t per_pair = static_cast<int64_t>(num_layers) * 2;
+  const int64_t units = n_pairs * per_pair;
+  const int64_t u0 = static_cast<int64_t>(blockIdx.x) * units_per_cta;
+  const int n = static_cast<int>(u0 < units ? std::min<int64_t>(units_per_cta, units - u0) : 0);
+  if (lane < n) {
+    const int64_t u = u0 + lane;
+    const int64_t pair = u / per_pair, lk = u - pair * per_pair;  // lk = layer * 2 + (K|V)
+    const int64_t s = src[pair], t = dst[pair];
+    from_s[lane] = -1;
+    to_s[lane] = -1;
+    if (s < 0 || s >= num_pages || t < 0 || t >= num_pages) {
+      record_error(err, kDevErrBadPage, static_cast<int>(pair));
+    } else if (s != t) {
+      from_s[lane] = (lk * num_pages + s) * page_bytes;
+      to_s[lane] = (lk * num_pages + t) * page_bytes;
+    }
+  }
+  __syncwarp();
+  if (lane != 0) return;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);  // [kCopyMaxSlots]
+  uint8_t* buf = smem_raw + 128;
+  for (int k = 0; k < slots; ++k) mbar_init(&full[k], 1);
+  fence_barrier_init();
+  auto load = [&](int i) {  // unit i of this CTA into slot i % slots
+    const int k = i % slots;
+    if (to_s[i] >= 0) {
+      mbar_arrive_expect_tx(&full[k], static_cast<uint32_t>(page_bytes));
+      bulk_g2s(buf + k * page_bytes, pool + from_s[i], static_cast<uint32_t>(page_bytes), &full[k]);
+    } else {
+      mbar_arrive_plain(&full[k]);  // nothing to copy: complete the slot's phase without bytes
+    }
+  };
+  int loaded = 0;  // units whose load is issued
+  for (; loaded < n && loaded < slots; ++loaded) load(loaded);
+  for (int j = 0; j < n; ++j) {
+    const int k = j % slots;
+    if (!mbar_wait_bounded(&full[k], static_cast<uint32_t>((j / slots) & 1), err, 40)) {
+      // Gave up (error recorded): wait, bounded, for the other loads still
+      // in flight into this CTA's shared memory before leaving.
+      for (int i = j + 1; i < loaded; ++i)
+        mbar_wait_bounded(&full[i % slots], static_cast<uint32_t>((i / slots) & 1), err, 41);
+      break;
+    }
+    if (to_s[j] >= 0) bulk_s2g(pool + to_s[j], buf + k * page_bytes, static_cast<uint32_t>(page_bytes));
+    bulk_commit_group();  // one group per step, empty for skipped units, so the lag counts steps
+    const int r = j - kCopyLag + slots;  // the unit that reuses slot (j - kCopyLag) % slots
+    if (j >= kCopyLag && r < n) {
+      bulk_wait_read<kCopyLag>();
+      load(r);
+      loaded = r + 1;
+    }
+  }
+  bulk_wait_all();
 }
 
 // Pages between the pool and a flat buffer [n_pages][layers][2 (K, V)]
@@ -424,6 +502,33 @@ int mtn_page_copy(const mtn_kv_layout* pool, const int32_t* src_pages, const int
   const bool narrow = work + static_cast<int64_t>(grid) * mtn::kThreads * mtn::kUnroll < (int64_t(1) << 31);
   auto* base = static_cast<__nv_bfloat16*>(pool->base);
   auto s = static_cast<cudaStream_t>(stream);
+  const int64_t page_bytes = page_vecs * 16;
+  if (page_bytes <= mtn::kCopyBulkMaxBytes) {
+    // Bulk path: ring slots of whole slabs, about 32 KB of shared memory per CTA.
+    const int slots = static_cast<int>(std::min<int64_t>(mtn::kCopyMaxSlots, std::max<int64_t>(4, 32768 / page_bytes)));
+    const int smem = 128 + slots * static_cast<int>(page_bytes);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      MTN_CUDA_TRY(cudaFuncSetAttribute(mtn::page_copy_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        128 + mtn::kCopyMaxSlots * mtn::kCopyBulkMaxBytes),
+                   "cudaFuncSetAttribute(page_copy_bulk_kernel)");
+      configured[dev] = true;
+    }
+    // Units spread over the resident CTAs (up to 32 each; more CTAs queue).
+    const int64_t units = n_pages * pool->num_layers * 2;
+    const int per_sm = std::max(1, std::min(8, (200 * 1024) / smem));
+    const int64_t resident = static_cast<int64_t>(mtn::sm_count()) * per_sm;
+    const int upc = static_cast<int>(
+        std::min<int64_t>(mtn::kCopyUnitsPerCta, std::max<int64_t>(1, (units + resident - 1) / resident)));
+    const int64_t grid = (units + upc - 1) / upc;
+    MTN_CHECK_ARG(grid < (int64_t(1) << 31), "mtn_page_copy: %lld pages too many", static_cast<long long>(n_pages));
+    return mtn::launch_pdl(mtn::page_copy_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(32),
+                           static_cast<size_t>(smem), s, "page_copy_bulk_kernel", reinterpret_cast<uint8_t*>(base),
+                           pool->num_pages, pool->num_layers, page_bytes, src_pages, dst_pages, n_pages, upc, slots,
+                           mtn::device_error_ptr());
+  }
   if (narrow)
     return mtn::launch_pdl(mtn::page_copy_kernel<uint32_t>, dim3(grid), dim3(mtn::kThreads), 0, s, "page_copy_kernel",
                            base, pool->num_pages, pool->num_layers, page_vecs, src_pages, dst_pages, n_pages,

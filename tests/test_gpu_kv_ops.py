@@ -78,6 +78,49 @@ def test_page_copy_all_layers(cuda_device):
     assert torch.equal(pool.storage.view(torch.int16), want.view(torch.int16))
 
 
+@pytest.mark.parametrize("layers,ps,hkv,d", [(2, 16, 2, 64), (1, 8, 1, 64), (2, 16, 4, 128), (1, 16, 1, 256),
+                                             (1, 32, 8, 128)])
+def test_page_copy_many_pairs(cuda_device, layers, ps, hkv, d):
+    """Slabs of 1-16 KB take the bulk-copy kernel (several units per CTA, so
+    every ring wraps); 64 KB slabs the vector kernel.  Bit-exact, including a
+    pair whose source is its destination."""
+    pages = 2048
+    pool = paged.PagedKVPool(layers, pages, ps, hkv, d, device=cuda_device)
+    pool.storage.copy_(torch.randn_like(pool.storage, dtype=torch.float32).to(torch.bfloat16))
+    before = pool.storage.clone()
+    rng = np.random.default_rng(ps * hkv + d)
+    perm = rng.permutation(pages)
+    n = 700
+    src_l, dst_l = perm[:n].tolist(), perm[n:2 * n].tolist()
+    dst_l[5] = src_l[5]
+    src = torch.tensor(src_l, dtype=torch.int32, device=cuda_device)
+    dst = torch.tensor(dst_l, dtype=torch.int32, device=cuda_device)
+    paged.device_error(0, clear=True)
+    pool.page_copy(src, dst)
+    torch.cuda.synchronize()
+    want = before.clone()
+    want[:, :, torch.tensor(dst_l)] = before[:, :, torch.tensor(src_l)]
+    assert torch.equal(pool.storage.view(torch.int16), want.view(torch.int16))
+    assert paged.device_error(0) == (0, 0)
+
+
+def test_page_copy_bad_page_is_flagged_not_faulted(cuda_device):
+    pool = paged.PagedKVPool(1, 64, 16, 2, 64, device=cuda_device)
+    pool.storage.copy_(torch.randn_like(pool.storage, dtype=torch.float32).to(torch.bfloat16))
+    before = pool.storage.clone()
+    src = torch.tensor([1, 2, 10 ** 6], dtype=torch.int32, device=cuda_device)
+    dst = torch.tensor([3, 4, 5], dtype=torch.int32, device=cuda_device)
+    paged.device_error(0, clear=True)
+    pool.page_copy(src, dst)
+    torch.cuda.synchronize()
+    code, detail = paged.device_error(0, clear=True)
+    assert code == 1 and detail == 2
+    want = before.clone()
+    want[:, :, 3] = before[:, :, 1]
+    want[:, :, 4] = before[:, :, 2]
+    assert torch.equal(pool.storage.view(torch.int16), want.view(torch.int16))
+
+
 def test_slot_mapping_matches_python(cuda_device):
     rng = np.random.default_rng(5)
     ps = 16
