@@ -812,6 +812,159 @@ def run_cfg3(args, local) -> dict:
             "cow_page_copy_us_per_128_pages": 1e6 * t_cow, "gpu_launches": steps}
 
 
+def run_cfg3_engine(args, local) -> dict:
+    """BASELINE config 3 through the engine: the Qwen2.5-7B-shaped model (random N(0,0.02) bf16 weights),
+    a parent request holding a 1032-token random prefix (seed 5) and 128 children forked off it
+    (mtn_sched_fork: each shares the prefix pages, the partial last page included), each with its own
+    random suffix of U[64, 512] tokens (lengths seed 6, tokens seed 7).  A child's first write into the
+    shared partial page copies it (copy-on-write).  Once every request decodes, `steps` (at most 32)
+    decode-only engine iterations of the 129-request batch are timed with CUDA events around the loop
+    (scheduler, copies, the forward replayed from a CUDA graph, device argmax, token hand-back).
+    Checked: exactly 128 copy-on-write copies of the partial page."""
+    import torch
+
+    from mitten_b200 import host, model as M
+
+    dev = torch.device("cuda", local)
+    shape = M.DecoderShape(**QWEN7B)
+    n, prefix_len, ps = 128, 1032, 16
+    timed = max(1, min(args.steps, 32))
+    out_tokens = timed + 24  # the children decode during the later prefill iterations too
+    prefix = np.random.default_rng(5).integers(0, shape.vocab, prefix_len).astype(np.uint32)
+    suf_lens = np.random.default_rng(6).integers(64, 513, size=n)
+    tok = np.random.default_rng(7)
+    suffixes = [tok.integers(0, shape.vocab, int(k)).astype(np.uint32) for k in suf_lens]
+    num_pages = (prefix_len + ps - 1) // ps + 1 + sum((int(k) + out_tokens + 2 * ps) // ps for k in suf_lens) + 64
+    w = model_weights(shape, dev, seed=0)
+    model = M.QwenPagedModel(shape, w, num_pages, ps, device=dev, split_bf16=False, dtype=torch.bfloat16)
+    del w
+    torch.cuda.empty_cache()
+    sched = host.Scheduler(num_pages, ps, max_prefill_tokens_per_iter=8192, max_decode_batch_size=n + 1,
+                           eos_token_ids=(shape.vocab,))
+    sched.add_request(0, prefix, temperature=0.0, max_new_tokens=out_tokens + 32)
+    eng = M.Engine(model, sched, cuda_graphs=True)
+    cows, it = 0, 0
+    t0 = time.perf_counter()
+    while True:  # prefill: the parent, then the children's suffixes (their own pages, the partial page copied)
+        b = sched.schedule()
+        cows += len(b.cow_src)
+        lg = model.forward(b)
+        sched.process_tokens(M.paged.argmax_rows(lg).cpu().numpy().astype(np.uint32))
+        if it == 0:
+            for k, suf in enumerate(suffixes):
+                sched.fork(0, k + 1, suf, temperature=0.0, max_new_tokens=out_tokens)
+        it += 1
+        if all(sched.request_info(r)["state"] == 2 for r in range(n + 1)):
+            break
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
+    eng.step()  # first decode-only batch: eager run + capture of the batch's CUDA graph
+    torch.cuda.synchronize(dev)
+    done0 = sum(len(sched.request_output(r)) for r in range(n + 1))
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(timed):
+        eng.step()
+    e.record()
+    e.synchronize()
+    t = a.elapsed_time(e) * 1e-3
+    tokens = sum(len(sched.request_output(r)) for r in range(n + 1)) - done0
+    code, detail = M.paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail}) in the config-3 engine run")
+    if cows != n:
+        raise SystemExit(f"config-3 engine run: {cows} copy-on-write copies, expected {n}")
+    return {"metric": "config 3 engine decode tokens/s (Qwen2.5-7B shape, shared 1032-token prefix, CoW)",
+            "value": tokens / t, "unit": "tokens/s", "n_gpus": 1, "steps": timed, "warmup": 1,
+            "ms_per_step": 1e3 * t / timed, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (random N(0,0.02) bf16 weights seed 0, random tokens seeds 5-7)",
+            "config": {"workload": "BASELINE config 3 through the engine: 128 children forked off a 1032-token "
+                                   "prefix (64 full pages + 1 partial, refcounted), suffix U[64,512], "
+                                   f"{timed} decode steps timed (trimmed from 128)", "requests": n + 1},
+            "prefill_s": prefill_s, "prefill_iterations": it, "cow_copies": cows,
+            "decode_tokens": tokens, "gpu_launches": None}
+
+
+def run_cfg4_engine(args, local) -> dict:
+    """BASELINE config 4 through the engine: the Gemma-2B-shaped model (MQA 8 q / 1 kv head, head_dim 256,
+    GeGLU 16384, vocab 256000, random N(0,0.02) bf16 weights), continuous batching.  96 requests with
+    prompts U[512, 8192] (seed 7) are prefilled first, under the same per-iteration token budget as the
+    timed part (2048 prefill tokens plus the decode rows).  Then every timed iteration four new
+    512-token requests arrive (tokens seed 8), so each iteration is one mixed batch: the decoding
+    requests (96 at the start, four more each iteration) plus four 512-token prefill chunks through one
+    forward (paged prefill and decode attention), device argmax, token hand-back.  Timed with CUDA
+    events around 24 iterations (trimmed), host scheduling and launches included."""
+    import torch
+
+    from mitten_b200 import host, model as M
+
+    dev = torch.device("cuda", local)
+    shape = M.GEMMA_2B
+    n_dec, n_new, chunk, ps = 96, 4, 512, 16
+    timed = max(1, min(args.steps, 24))
+    lens = np.random.default_rng(7).integers(512, 8193, size=n_dec)
+    tok = np.random.default_rng(8)
+    prompts = [tok.integers(0, shape.vocab, int(k)).astype(np.uint32) for k in lens]
+    arrivals = [[tok.integers(0, shape.vocab, chunk).astype(np.uint32) for _ in range(n_new)] for _ in range(timed + 1)]
+    max_dec = n_dec + n_new * (timed + 1)
+    budget = n_new * chunk + max_dec
+    out_cap = 512
+    num_pages = sum((int(k) + out_cap + ps) // ps for k in lens)
+    num_pages += (timed + 1) * n_new * ((chunk + out_cap + ps) // ps) + 64
+    w = model_weights(shape, dev, seed=0)
+    model = M.QwenPagedModel(shape, w, num_pages, ps, device=dev, split_bf16=False, dtype=torch.bfloat16)
+    del w
+    torch.cuda.empty_cache()
+    sched = host.Scheduler(num_pages, ps, max_prefill_tokens_per_iter=budget, max_decode_batch_size=max_dec,
+                           eos_token_ids=(shape.vocab,))
+    for r in range(n_dec):
+        sched.add_request(r, prompts[r], temperature=0.0, max_new_tokens=out_cap)
+    eng = M.Engine(model, sched, cuda_graphs=False)
+    t0 = time.perf_counter()
+    while any(sched.request_info(r)["state"] in (0, 1) for r in range(n_dec)):  # waiting or prefilling
+        eng.step()
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
+    nxt = n_dec
+
+    def arrive(k):
+        nonlocal nxt
+        for pr in arrivals[k]:
+            sched.add_request(nxt, pr, temperature=0.0, max_new_tokens=out_cap)
+            nxt += 1
+
+    arrive(0)
+    eng.step()  # warm-up: one mixed iteration
+    torch.cuda.synchronize(dev)
+    rows, pf_tokens = [], 0
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(timed):
+        arrive(k + 1)
+        b = sched.schedule()
+        rows.append((b.n_reqs - b.n_prefill, b.n_prefill))
+        pf_tokens += int(b.qo_indptr[b.n_prefill])
+        lg = model.forward(b)
+        sched.process_tokens(M.paged.argmax_rows(lg).cpu().numpy().astype(np.uint32))
+    e.record()
+    e.synchronize()
+    t = a.elapsed_time(e) * 1e-3
+    code, detail = M.paged.device_error(local)
+    if code:
+        raise SystemExit(f"device error {code} (detail {detail}) in the config-4 engine run")
+    dec_rows = sum(r[0] for r in rows)
+    return {"metric": "config 4 engine decode tokens/s (Gemma-2B shape, continuous batching)",
+            "value": dec_rows / t, "unit": "tokens/s", "n_gpus": 1, "steps": timed, "warmup": 1,
+            "ms_per_step": 1e3 * t / timed, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (random N(0,0.02) bf16 weights seed 0, random tokens seeds 7-8)",
+            "config": {"workload": "BASELINE config 4 through the engine: decode rows (96, +4 per iteration) + 4 "
+                                   "prefill chunks of 512 tokens per iteration (new requests), contexts "
+                                   f"U[512, 8192], {timed} mixed iterations timed (trimmed)"},
+            "prefill_tokens_per_s": pf_tokens / t,
+            "decode_rows_first_last": [rows[0][0], rows[-1][0]], "prefill_rows_per_iteration": rows[0][1],
+            "initial_prefill_s": prefill_s, "gpu_launches": None}
+
+
 def run_cfg4(args, local) -> dict:
     """BASELINE config 4's attention layer (Gemma-2B shapes: 8 q / 1 kv head, head_dim 256): per step
     96 decoding sequences with context U[512, 8192] (seed 7) plus 4 prefill chunks of 512 tokens whose
@@ -1127,9 +1280,9 @@ def main(argv=None) -> int:
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-engine", action="store_true", help="skip the whole-box config-5 engine leg")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "cfg3e", "cfg4e"], default="cfg2",
                     help="cfg2 (default) is the headline; cfg3 / cfg4 / cfg5 time those configs' attention "
-                         "layers; cfg1 runs config 1's model through the engine")
+                         "layers; cfg1, cfg3e and cfg4e run configs 1, 3 and 4 through the engine")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
@@ -1142,7 +1295,8 @@ def main(argv=None) -> int:
         return 0
     rank, world, local, pg = dist_setup(args.gpus)
     if args.workload != "cfg2":
-        res = {"cfg1": run_cfg1, "cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5}[args.workload](args, local)
+        res = {"cfg1": run_cfg1, "cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5, "cfg3e": run_cfg3_engine,
+               "cfg4e": run_cfg4_engine}[args.workload](args, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if pg is not None:

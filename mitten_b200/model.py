@@ -297,6 +297,8 @@ class _DecodeGraph:
         self.ids = torch.zeros(n, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(n, dtype=torch.int32, device=dev)
         self.kv_indptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+        # Page-table entries of the batch: with shared prefix pages a batch
+        # lists more entries than the pool has pages, so this grows on demand.
         self.kv_indices = torch.zeros(max(model.pool.num_pages, 1), dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(n, dtype=torch.int32, device=dev)
         self.last = torch.arange(n, dtype=torch.int64, device=dev)
@@ -310,7 +312,12 @@ class _DecodeGraph:
     def _fill(self, b) -> None:
         nk = int(b.kv_indptr[-1])
         if nk > self.kv_indices.numel():
-            raise ValueError("decode batch lists more pages than the pool holds")
+            # A bigger static table: the captured graph holds the old one's
+            # address, so it is dropped and captured again on this batch.
+            self.kv_indices = torch.zeros(2 * nk, dtype=torch.int32, device=self.model.dev)
+            self.meta["kv_indices"] = self.kv_indices
+            self.graph = None
+            self.out = None
         self.ids.copy_(torch.from_numpy(b.input_ids.astype(np.int64)))
         self.pos.copy_(torch.from_numpy(np.ascontiguousarray(b.position_ids, np.int32)))
         self.kv_indptr.copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indptr, np.int32)))

@@ -98,3 +98,38 @@ def test_forked_prefix_copy_on_write_through_engine(cuda_device):
     tree = s.tree_pages()
     assert all(s.page_refcount(p) == 1 for p in tree)
     assert s.free_pages() + len(tree) == num_pages
+
+
+def test_forked_prefix_decode_graph_lists_more_table_entries_than_pages(cuda_device):
+    """The decode CUDA graph's page-table buffer holds the batch's table
+    entries, which with shared prefix pages outnumber the pool's pages: nine
+    requests list the 65 prefix pages each (585 entries) in a pool of 256
+    pages.  The graph-replayed engine must emit the oracle model's tokens."""
+    w = R.random_weights(CFG, seed=5)
+    rng = np.random.default_rng(15)
+    prefix = rng.integers(0, CFG.vocab, PREFIX).astype(np.uint32)
+    suffixes = [rng.integers(0, CFG.vocab, 20).astype(np.uint32) for _ in range(8)]
+    num_pages = 256
+    model = M.QwenPagedModel(_shape(CFG), w, num_pages, PS)
+    s = host.Scheduler(num_pages, PS, max_prefill_tokens_per_iter=4096, max_decode_batch_size=16,
+                       eos_token_ids=(CFG.vocab,))
+    s.add_request(0, prefix, temperature=0.0, max_new_tokens=STEPS)
+    eng = M.Engine(model, s, cuda_graphs=True)
+    eng.step()  # the parent's prefill
+    for k, suf in enumerate(suffixes):
+        s.fork(0, k + 1, suf, temperature=0.0, max_new_tokens=STEPS)
+    entries = 0
+    while s.num_active():
+        b = s.schedule()
+        assert b is not None
+        if not b.n_prefill:
+            entries = max(entries, int(b.kv_indptr[-1]))
+        lg = model.decode_step(b)
+        s.process_tokens(M.paged.argmax_rows(lg).cpu().numpy().astype(np.uint32))
+    assert entries > num_pages
+    assert M.paged.device_error(0) == (0, 0)
+    ref = R.RefModel(CFG, w, kv_round=True)
+    prompts = [prefix.astype(np.int64)] + [np.concatenate([prefix, suf]).astype(np.int64) for suf in suffixes]
+    want = R.generate(ref, prompts, STEPS)
+    got = [s.request_output(r) for r in range(9)]
+    assert got == want
