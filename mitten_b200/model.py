@@ -73,7 +73,7 @@ class QwenPagedModel:
 
     def __init__(self, shape: DecoderShape, weights: dict, num_pages: int, page_size: int = 16,
                  device: torch.device | str = "cuda", split_bf16: bool = True, dtype: torch.dtype = torch.float32,
-                 fused_prologue: bool = True):
+                 fused_prologue: bool = True, decode_plan: bool = True):
         self.s = shape
         # Dense weights and activations in `dtype` (f32: the reference's CPU
         # path; bf16: the random-bf16 configs 3-5).  RoPE is applied in f32 and
@@ -107,6 +107,9 @@ class QwenPagedModel:
         self._ws_seqs = 0
         self._pws = None
         self._plan = None
+        # decode_plan: pass the decode kernel a host-made work plan
+        # (mtn_paged_decode_plan) instead of letting it split the tiles itself.
+        self.use_plan = decode_plan
         self._graphs: dict[int, _DecodeGraph] = {}
 
     # ------------------------------------------------------------ pieces
@@ -229,9 +232,11 @@ class QwenPagedModel:
             meta["len_d"] = torch.from_numpy(np.ascontiguousarray(b.seq_lens[npf:], np.int32)).to(dev)
             meta["ws"] = self._decode_ws(n - npf)
             # one host-made work plan serves the decode rows of every layer
-            if self._plan is None:
-                self._plan = paged.DecodePlan(self.s.head_dim, dev)
-            meta["plan"] = self._plan.build(b.kv_indptr[npf:], b.seq_lens[npf:], self.pool.page_size, self.s.hkv)
+            if self.use_plan:
+                if self._plan is None:
+                    self._plan = paged.DecodePlan(self.s.head_dim, dev)
+                meta["plan"] = self._plan.build(b.kv_indptr[npf:], b.seq_lens[npf:], self.pool.page_size,
+                                                self.s.hkv)
         return meta
 
     def _cow(self, b) -> None:
@@ -302,7 +307,7 @@ class _DecodeGraph:
         self.kv_indices = torch.zeros(max(model.pool.num_pages, 1), dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(n, dtype=torch.int32, device=dev)
         self.last = torch.arange(n, dtype=torch.int64, device=dev)
-        self.plan = paged.DecodePlan(model.s.head_dim, dev)
+        self.plan = paged.DecodePlan(model.s.head_dim, dev) if model.use_plan else None
         self.meta = {"tp": 0, "kv_indices": self.kv_indices, "kv_d": self.kv_indptr, "len_d": self.seq_lens,
                      "qo_all": torch.arange(n + 1, dtype=torch.int32, device=dev), "kv_all": self.kv_indptr,
                      "ws": paged.DecodeWorkspace.for_shape(model.pool, n, model.s.hq), "plan": self.plan}
@@ -323,7 +328,8 @@ class _DecodeGraph:
         self.kv_indptr.copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indptr, np.int32)))
         self.kv_indices[:nk].copy_(torch.from_numpy(np.ascontiguousarray(b.kv_indices[:nk], np.int32)))
         self.seq_lens.copy_(torch.from_numpy(np.ascontiguousarray(b.seq_lens, np.int32)))
-        self.plan.build(b.kv_indptr, b.seq_lens, self.model.pool.page_size, self.model.s.hkv)
+        if self.plan is not None:
+            self.plan.build(b.kv_indptr, b.seq_lens, self.model.pool.page_size, self.model.s.hkv)
 
     def run(self, b) -> torch.Tensor:
         self._fill(b)
