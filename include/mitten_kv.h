@@ -295,6 +295,31 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
                      const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
                      float scale, uint32_t flags, void* stream);
 
+/* Decode over a prefix that every sequence of the batch shares (the
+ * refcounted prefix pages of the radix cache, radix_cache.rs:64-117; config
+ * 3's shared prompt head).  No counterpart call in the reference, which
+ * attends over each request's own cache (qwen model.rs:394-416): the result
+ * equals mtn_paged_decode over the block tables prefix_pages ++ own pages,
+ * up to f32 rounding.  Sequence r's keys are the n_prefix_pages full pages
+ * prefix_pages[] (n_prefix_pages * page_size tokens, read-only) followed by
+ * its own pages kv_indices[kv_indptr[r] ..] holding seq_lens[r] tokens
+ * (k_new/v_new, if given, are stored at own position seq_lens[r]-1).  The
+ * prefix part runs once for all sequences (prefill kernel, non-causal), the
+ * own part through the decode kernel, then the two are combined by their
+ * log-sum-exps; MTN_ATTN_PHANTOM_ZERO_SLOT counts the zero row once.
+ * workspace: mtn_paged_decode_shared_prefix_workspace_bytes(...) bytes,
+ * 256-byte aligned, zeroed once before first use, one stream at a time
+ * (zero it again after a call that reports a device timeout). */
+MTN_API size_t mtn_paged_decode_shared_prefix_workspace_bytes(int32_t n_seqs, int32_t num_q_heads,
+                                                      int32_t num_kv_heads, int32_t head_dim);
+MTN_API int mtn_paged_decode_shared_prefix(const mtn_kv_layout* pool, int32_t layer,
+                     const void* q, int32_t q_dtype, void* o, int32_t o_dtype,
+                     const void* k_new, const void* v_new, int32_t new_dtype,
+                     int32_t n_seqs, int32_t num_q_heads,
+                     const int32_t* prefix_pages, int32_t n_prefix_pages,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens,
+                     float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Chunked-prefill attention over paged KV (tcgen05 / TMEM tensor cores).
  *   q: [total_q][num_q_heads][head_dim] (q_dtype: bf16, or f32 rounded to
  *   bf16 -- or split into bf16 hi + lo with MTN_ATTN_SPLIT_BF16 -- on

@@ -105,6 +105,11 @@ SIGNATURES: dict[str, tuple] = {
     "mtn_paged_decode_noalloc": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
                                            C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_uint32, C.c_void_p]),
+    "mtn_paged_decode_shared_prefix_workspace_bytes": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "mtn_paged_decode_shared_prefix": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
+                                                 C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
+                                                 C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                                 C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p]),
     "mtn_paged_prefill_workspace_bytes": (C.c_size_t, [C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int32]),
     "mtn_paged_prefill": (C.c_int, [C.POINTER(KvLayout), C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
                                     C.c_int32,

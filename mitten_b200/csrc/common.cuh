@@ -69,6 +69,21 @@ int validate_layout(const mtn_kv_layout* pool, int layer, const char* who);
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Internal forms of mtn_paged_prefill / mtn_paged_decode_with_plan for the
+// shared-prefix decode: `lse` (or null) receives each (row, query head)'s
+// log2-domain log-sum-exp; `noncausal` lets every prefill query see every
+// key of its sequence.
+int paged_prefill_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                       int32_t o_dtype, int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
+                       const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+                       const int32_t* seq_lens, int32_t max_q_len, float scale, uint32_t flags, void* workspace,
+                       size_t workspace_bytes, void* stream, int noncausal, float* lse);
+int paged_decode_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                      int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
+                      int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,
+                      const int32_t* seq_lens, float scale, uint32_t flags, const void* plan, void* workspace,
+                      size_t workspace_bytes, void* stream, float* lse);
+
 // Device error codes (written by kernels, read by mtn_device_error).
 enum DevErr : int {
   kDevErrNone = 0,
@@ -179,6 +194,19 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 // Every bulk group of this thread complete (its global writes performed).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Log2-domain log-sum-exp of a softmax row kept as a running max m and sum
+// l = sum 2^(s - m) (scores s already scaled into log2 units), with the
+// reference's all-zero phantom key (score 0) folded in when `phantom` is
+// set: log2(2^m * l [+ 1]).  -inf for a row with no key at all.
+__device__ __forceinline__ float row_lse(int phantom, float m, float l) {
+  if (phantom) {
+    const float mf = fmaxf(m, 0.0f);  // m == -inf (no real keys) gives mf = 0
+    const float a = m == -INFINITY ? 0.0f : exp2f(m - mf);
+    return mf + log2f(l * a + exp2f(-mf));
+  }
+  return l > 0.0f ? m + log2f(l) : -INFINITY;
+}
 
 // bf16x2 (packed in a 32-bit word, low half = element 0) -> two floats.
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {

@@ -96,6 +96,7 @@ struct DecodeParams {
   unsigned int* ws_cnt;  // [n_seqs][hkv]      arrival tickets (left at zero)
   int* err;
   const int32_t* plan;   // host-made work plan (mtn_paged_decode_plan) or null
+  float* lse;            // [n_seqs][hq] log2-domain log-sum-exp of each row, or null
 };
 
 template <int D>
@@ -417,6 +418,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if ((len + kTile - 1) / kTile == 0) {
         const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
         for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
+        if (p.lse != nullptr)
+          for (int h = 0; h < p.hq; ++h) p.lse[static_cast<int64_t>(s) * p.hq + h] = row_lse(p.phantom, -INFINITY, 0.0f);
       }
     }
   };
@@ -980,6 +983,11 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
                 store_out(p, (head0 + h) * D + d_base + mb * 128,
                           finalize(ov[mb][h], l_cta[h], m_ref[h], p.phantom));
           }
+          if (p.lse != nullptr) {
+#pragma unroll
+            for (int h = 0; h < NREP; ++h)
+              if (t == h) p.lse[head0 + h] = row_lse(p.phantom, m_ref[h], l_cta[h]);  // one thread per head
+          }
         } else {
           // Partial: slot (cta, 0) if the segment is this CTA's first, else (cta, 1).
           const int which = (cta == ca && t0 != s_start) ? 1 : 0;
@@ -1110,7 +1118,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
 #pragma unroll
       for (int q = 0; q < kElems; ++q) {
         const int e = t + q * 128;
-        if (e < NREP * D) store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
+        if (e < NREP * D) {
+          store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
+          if (p.lse != nullptr && e % D == 0) p.lse[head0 + e / D] = row_lse(p.phantom, mrun[q], lrun[q]);
+        }
       }
       if (t == 0) p.ws_cnt[pd.x] = 0u;  // ready for the next call on this workspace
     }
@@ -1308,6 +1319,18 @@ int mtn_paged_decode_with_plan(const mtn_kv_layout* pool, int32_t layer, const v
                                int32_t n_seqs, int32_t num_q_heads, const int32_t* kv_indptr,
                                const int32_t* kv_indices, const int32_t* seq_lens, float scale, uint32_t flags,
                                const void* plan, void* workspace, size_t workspace_bytes, void* stream) {
+  return mtn::paged_decode_impl(pool, layer, q, q_dtype, o, o_dtype, k_new, v_new, new_dtype, n_seqs, num_q_heads,
+                                kv_indptr, kv_indices, seq_lens, scale, flags, plan, workspace, workspace_bytes,
+                                stream, nullptr);
+}
+
+}  // extern "C"
+
+int mtn::paged_decode_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                           int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
+                           int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,
+                           const int32_t* seq_lens, float scale, uint32_t flags, const void* plan, void* workspace,
+                           size_t workspace_bytes, void* stream, float* lse) {
   int st = mtn::validate_layout(pool, layer, "mtn_paged_decode");
   if (st != MTN_OK) return st;
   MTN_CHECK_ARG(n_seqs >= 0, "mtn_paged_decode: n_seqs < 0");
@@ -1371,6 +1394,7 @@ int mtn_paged_decode_with_plan(const mtn_kv_layout* pool, int32_t layer, const v
   prm.err = mtn::device_error_ptr();
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(plan) & 15) == 0, "mtn_paged_decode: plan must be 16-byte aligned");
   prm.plan = static_cast<const int32_t*>(plan);
+  prm.lse = lse;
   const int nrep = num_q_heads / pool->num_kv_heads;
   auto s = static_cast<cudaStream_t>(stream);
   const bool prec = (flags & MTN_ATTN_SPLIT_BF16) != 0;
@@ -1380,6 +1404,8 @@ int mtn_paged_decode_with_plan(const mtn_kv_layout* pool, int32_t layer, const v
     default: return mtn::dispatch_prec<256>(prec, nrep, tkv, tq, prm, s);
   }
 }
+
+extern "C" {
 
 int mtn_paged_decode(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
                      int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,

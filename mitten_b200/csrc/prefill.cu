@@ -58,6 +58,12 @@ struct PrefillParams {
   float qscale;
   int phantom;
   int* err;
+  // Used only by the shared-prefix decode (one-tile kernel): noncausal = every
+  // query row sees every key of its sequence (the queries are other
+  // sequences' tokens, all after the shared keys); lse = per (row, head)
+  // log2-domain log-sum-exp of the row's softmax, [total_q][hq], or null.
+  int noncausal;
+  float* lse;
   // Split of long units, for launches with few units: a (query tile, head,
   // sequence) unit is cut into k <= kMaxPieces pieces of consecutive kv
   // tiles, run by CTAs blockIdx.z = piece * n_seqs + sequence (pieces in the
@@ -130,9 +136,9 @@ __device__ __forceinline__ int64_t split_piece_len(const PrefillParams& p, int b
     const int q0 = p.qo_indptr[s];
     const int ql = p.qo_indptr[s + 1] - q0;
     if (ql <= 0) continue;
-    const int64_t kl = max(static_cast<int64_t>(p.seq_lens[s]), static_cast<int64_t>(ql));
+    const int64_t kl = max(static_cast<int64_t>(p.seq_lens[s]), static_cast<int64_t>(p.noncausal ? 1 : ql));
     for (int qt = 0; qt * kBM < ql; ++qt) {
-      t += (kl - ql + min(ql, (qt + 1) * kBM) - 1) / bn + 1;
+      t += p.noncausal ? (kl + bn - 1) / bn : (kl - ql + min(ql, (qt + 1) * kBM) - 1) / bn + 1;
       ++u;
     }
   }
@@ -325,14 +331,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.split) __syncthreads();
   if (scan_warp) load_meta();
   if (tile * kBM >= q_len) return;
-  if (kv_len < q_len || kv_len > npages * p.ps) {
+  const int min_kv = p.noncausal ? 1 : q_len;  // non-causal rows need at least one key
+  if (kv_len < min_kv || kv_len > npages * p.ps) {
     if (tile == 0 && h == 0 && piece == 0 && threadIdx.x == 0) record_error(p.err, kDevErrBadSeqLen, s);
-    kv_len = max(q_len, min(kv_len, npages * p.ps));
+    kv_len = max(min_kv, min(kv_len, npages * p.ps));
     if (kv_len > npages * p.ps) return;  // not even the chunk fits its pages
   }
   const int nrows = min(kBM, q_len - tile * kBM);
-  const int pos0 = kv_len - q_len + tile * kBM;  // position of row 0
-  const int last_pos = pos0 + nrows - 1;
+  // Position of row 0 and of the last row; non-causal rows all sit after
+  // the last key, so only keys past kv_len are masked.
+  const int pos0 = p.noncausal ? kv_len - 1 : kv_len - q_len + tile * kBM;
+  const int last_pos = p.noncausal ? kv_len - 1 : pos0 + nrows - 1;
   const int n_tiles = last_pos / C::kBN + 1;
   const int g = h / (p.hq / p.hkv);
   const int pages_per_tile = C::kBN / p.ps;
@@ -563,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool all_ok = !tc::named_sync_or(1, kBM, !ok);
     if (all_ok && k == 1) {
       const float inv = finish(m_ref, l_run);
+      if (p.lse != nullptr && valid) p.lse[orow] = row_lse(p.phantom, m_ref, l_run);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
@@ -615,6 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           L += li[i] * mi[i];
         }
         const float inv = finish(M, L);
+        if (p.lse != nullptr && valid) p.lse[orow] = row_lse(p.phantom, M, L);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
@@ -997,6 +1008,20 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, i
                       int32_t n_seqs, int64_t total_q, int32_t num_q_heads, const int32_t* qo_indptr,
                       const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* seq_lens, int32_t max_q_len,
                       float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return mtn::paged_prefill_impl(pool, layer, q, q_dtype, o, o_dtype, n_seqs, total_q, num_q_heads, qo_indptr,
+                                 kv_indptr, kv_indices, seq_lens, max_q_len, scale, flags, workspace, workspace_bytes,
+                                 stream, 0, nullptr);
+}
+
+}  // extern "C"
+
+namespace mtn {
+
+int paged_prefill_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
+                       int32_t o_dtype, int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
+                       const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+                       const int32_t* seq_lens, int32_t max_q_len, float scale, uint32_t flags, void* workspace,
+                       size_t workspace_bytes, void* stream, int noncausal, float* lse) {
   int st = mtn::validate_layout(pool, layer, "mtn_paged_prefill");
   if (st != MTN_OK) return st;
   MTN_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65535, "mtn_paged_prefill: n_seqs %d outside [0, 65535]", n_seqs);
@@ -1038,6 +1063,8 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, i
   prm.qscale = scale * mtn::kLog2e;
   prm.phantom = (flags & MTN_ATTN_PHANTOM_ZERO_SLOT) ? 1 : 0;
   prm.err = mtn::device_error_ptr();
+  prm.noncausal = noncausal;
+  prm.lse = lse;
   const int n_tiles = (max_q_len + mtn::kBM - 1) / mtn::kBM;
   MTN_CHECK_ARG(n_tiles <= 65535 * 32, "mtn_paged_prefill: max_q_len too large");
   // Launches whose units (bounded by (total_q / 128 + n_seqs) x heads) leave
@@ -1062,7 +1089,7 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, i
   }
   // Many query tiles (at least two per SM): two tiles per CTA at head_dim
   // <= 128, sharing every K/V tile (bf16 queries).
-  if (!prm.split && D <= 128 && !prm.q_f32 && !(flags & MTN_ATTN_PREFILL_ONE_TILE) &&
+  if (!prm.split && !noncausal && lse == nullptr && D <= 128 && !prm.q_f32 && !(flags & MTN_ATTN_PREFILL_ONE_TILE) &&
       (total_q / mtn::kBM) * num_q_heads >= 2 * static_cast<int64_t>(mtn::sm_count())) {
     return D == 64 ? mtn::launch_prefill_pair<64>(tkv, prm, n_tiles, n_seqs, s)
                    : mtn::launch_prefill_pair<128>(tkv, prm, n_tiles, n_seqs, s);
@@ -1074,4 +1101,4 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, i
   }
 }
 
-}  // extern "C"
+}  // namespace mtn

@@ -217,6 +217,54 @@ def paged_decode(pool: PagedKVPool, layer: int, q: torch.Tensor, kv_indptr: torc
     return out
 
 
+def shared_prefix_workspace(pool: PagedKVPool, n_seqs: int, num_q_heads: int) -> torch.Tensor:
+    """Zeroed workspace for paged_decode_shared_prefix (reusable; zero it again after a device timeout)."""
+    nb = L.lib().mtn_paged_decode_shared_prefix_workspace_bytes(n_seqs, num_q_heads, pool.num_kv_heads,
+                                                                 pool.head_dim)
+    if nb == 0:
+        raise ValueError("no shared-prefix decode for this shape")
+    return torch.zeros(nb, dtype=torch.uint8, device=pool.device)
+
+
+def paged_decode_shared_prefix(pool: PagedKVPool, layer: int, q: torch.Tensor, prefix_pages: torch.Tensor,
+                               kv_indptr: torch.Tensor, kv_indices: torch.Tensor, seq_lens: torch.Tensor,
+                               scale: float | None = None, phantom: bool = False, k_new: torch.Tensor | None = None,
+                               v_new: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                               out_dtype: torch.dtype = torch.bfloat16, workspace: torch.Tensor | None = None,
+                               stream=None, split_bf16: bool = False) -> torch.Tensor:
+    """paged_decode for sequences that all start with the same full pages `prefix_pages`.
+
+    Sequence r attends over the prefix pages followed by its own pages
+    kv_indices[kv_indptr[r]:kv_indptr[r+1]] holding seq_lens[r] tokens (the
+    step's token, with k_new/v_new, at own position seq_lens[r] - 1); the
+    prefix is read once for the whole batch instead of once per sequence.
+    """
+    if q.dim() != 3 or not q.is_contiguous():
+        raise ValueError("q must be a contiguous [n_seqs, heads, head_dim] tensor")
+    n, hq, d = q.shape
+    if d != pool.head_dim:
+        raise ValueError("head_dim mismatch")
+    if scale is None:
+        scale = d ** -0.5
+    if out is None:
+        out = torch.empty((n, hq, d), dtype=out_dtype, device=q.device)
+    if workspace is None:
+        workspace = shared_prefix_workspace(pool, n, hq)
+    new_code = 0
+    if k_new is not None or v_new is not None:
+        if k_new is None or v_new is None or not k_new.is_contiguous() or not v_new.is_contiguous():
+            raise ValueError("k_new and v_new must both be contiguous [n_seqs, kv_heads, head_dim] tensors")
+        new_code = _dtype_code(k_new.dtype)
+    pp = _i32(prefix_pages)
+    flags = (L.MTN_ATTN_PHANTOM_ZERO_SLOT if phantom else 0) | (L.MTN_ATTN_SPLIT_BF16 if split_bf16 else 0)
+    L.check(L.lib().mtn_paged_decode_shared_prefix(C.byref(pool.layout), layer, _ptr(q), _dtype_code(q.dtype),
+                                                   _ptr(out), _dtype_code(out.dtype), _ptr(k_new), _ptr(v_new),
+                                                   new_code, n, hq, _ptr(pp), pp.numel(), _ptr(_i32(kv_indptr)),
+                                                   _ptr(_i32(kv_indices)), _ptr(_i32(seq_lens)), float(scale), flags,
+                                                   _ptr(workspace), workspace.numel(), _stream(stream)))
+    return out
+
+
 def paged_prefill(pool: PagedKVPool, layer: int, q: torch.Tensor, qo_indptr: torch.Tensor,
                   kv_indptr: torch.Tensor, kv_indices: torch.Tensor, seq_lens: torch.Tensor, max_q_len: int,
                   scale: float | None = None, phantom: bool = False, out: torch.Tensor | None = None,
