@@ -769,8 +769,14 @@ def run_cfg3(args, local) -> dict:
                 nxt += 1
             tables.append(own)
         indptr = np.concatenate([[0], np.cumsum([len(t) for t in tables])]).astype(np.int32)
+        n_full = prefix // ps  # the full prefix pages every table starts with
+        own = [t[n_full:] for t in tables]
+        own_ptr = np.concatenate([[0], np.cumsum([len(t) for t in own])]).astype(np.int32)
         copies.append({"indptr": torch.from_numpy(indptr).to(dev),
-                       "indices": torch.from_numpy(np.concatenate(tables).astype(np.int32)).to(dev)})
+                       "indices": torch.from_numpy(np.concatenate(tables).astype(np.int32)).to(dev),
+                       "prefix": torch.tensor(shared[:n_full], dtype=torch.int32, device=dev),
+                       "own_indptr": torch.from_numpy(own_ptr).to(dev),
+                       "own_indices": torch.from_numpy(np.concatenate(own).astype(np.int32)).to(dev)})
     assert nxt <= num_pages
     # copy-on-write of every sequence's partial prefix page (128 pages per copy of the workload)
     src_t = torch.tensor(cow_src[:n], dtype=torch.int32, device=dev)
@@ -793,6 +799,23 @@ def run_cfg3(args, local) -> dict:
     for j in range(args.warmup):
         step(j)()
     t = _graph_steps([step(args.warmup + j) for j in range(steps)], stream)
+    # The same steps with the prefix's 64 full pages attended once for the
+    # whole batch (mtn_paged_decode_shared_prefix), each sequence's own part
+    # (the copied partial page and its suffix) by the decode kernel.
+    n_full = prefix // ps
+    own_lens = [l - n_full * ps for l in lens]
+    sp_ws = paged.shared_prefix_workspace(pool, n, hq)
+    out_sp = torch.empty_like(out)
+
+    def step_sp(j):
+        c = copies[j % n_copies]
+        return lambda: paged.paged_decode_shared_prefix(pool, 0, q, c["prefix"], c["own_indptr"], c["own_indices"],
+                                                        own_lens[j], k_new=kn, v_new=vn, out=out_sp,
+                                                        workspace=sp_ws)
+
+    for j in range(args.warmup):
+        step_sp(j)()
+    t_sp = _graph_steps([step_sp(args.warmup + j) for j in range(steps)], stream)
     b_tok = 2 * hkv * d * 2
     logical = float(sum((prefix + suf + 1).astype(np.int64))) * b_tok
     unique = (prefix + float(np.sum(suf + 1))) * b_tok
@@ -809,7 +832,11 @@ def run_cfg3(args, local) -> dict:
                        "l2": "3 disjoint copies of the workload rotate step to step"},
             "logical_kv_gbs": logical / (t / steps) / 1e9, "unique_kv_gbs": unique / (t / steps) / 1e9,
             "unique_frac_of_hbm": unique / (t / steps) / 1e9 / peak,
-            "cow_page_copy_us_per_128_pages": 1e6 * t_cow, "gpu_launches": steps}
+            "cow_page_copy_us_per_128_pages": 1e6 * t_cow, "gpu_launches": steps,
+            "shared_prefix": {"call": "mtn_paged_decode_shared_prefix (prefix once per batch, LSE combine)",
+                              "ms_per_step": 1e3 * t_sp / steps, "tokens_per_s": n * steps / t_sp,
+                              "speedup": t / t_sp, "unique_kv_gbs": unique / (t_sp / steps) / 1e9,
+                              "launches_per_step": 4}}
 
 
 def run_cfg3_engine(args, local) -> dict:

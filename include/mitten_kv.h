@@ -306,7 +306,8 @@ MTN_API int mtn_paged_decode_noalloc(const mtn_kv_layout* pool, int32_t layer,
  * (k_new/v_new, if given, are stored at own position seq_lens[r]-1).  The
  * prefix part runs once for all sequences (prefill kernel, non-causal), the
  * own part through the decode kernel, then the two are combined by their
- * log-sum-exps; MTN_ATTN_PHANTOM_ZERO_SLOT counts the zero row once.
+ * log-sum-exps; MTN_ATTN_PHANTOM_ZERO_SLOT counts the zero row once
+ * (MTN_ATTN_SPLIT_BF16 is rejected).
  * workspace: mtn_paged_decode_shared_prefix_workspace_bytes(...) bytes,
  * 256-byte aligned, zeroed once before first use, one stream at a time
  * (zero it again after a call that reports a device timeout). */

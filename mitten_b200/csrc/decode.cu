@@ -269,7 +269,9 @@ __device__ __forceinline__ int64_t cta_of(const int32_t* bnd, int64_t x, int64_t
 // most 8 query heads, so the lo rows ride in rows 8..15 of the same Q^T and
 // P^T operands: S^T columns h and h + 8 (and O^T columns h and h + 8) are
 // the hi and lo products of head h, summed in f32 -- no extra MMA.
-template <int D, int NREP, bool PREC>
+// LSE: also store each row's log-sum-exp in p.lse (the shared-prefix decode);
+// a separate instantiation, so the plain decode's code is untouched.
+template <int D, int NREP, bool PREC, bool LSE = false>
 __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ DecodeParams p) {
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if ((len + kTile - 1) / kTile == 0) {
         const float z = finalize(0.0f, 0.0f, -INFINITY, p.phantom);
         for (int e = 0; e < p.hq * D; ++e) store_out(p, static_cast<int64_t>(s) * p.hq * D + e, z);
-        if (p.lse != nullptr)
+        if constexpr (LSE)
           for (int h = 0; h < p.hq; ++h) p.lse[static_cast<int64_t>(s) * p.hq + h] = row_lse(p.phantom, -INFINITY, 0.0f);
       }
     }
@@ -983,7 +985,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
                 store_out(p, (head0 + h) * D + d_base + mb * 128,
                           finalize(ov[mb][h], l_cta[h], m_ref[h], p.phantom));
           }
-          if (p.lse != nullptr) {
+          if constexpr (LSE) {
 #pragma unroll
             for (int h = 0; h < NREP; ++h)
               if (t == h) p.lse[head0 + h] = row_lse(p.phantom, m_ref[h], l_cta[h]);  // one thread per head
@@ -1120,7 +1122,9 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         const int e = t + q * 128;
         if (e < NREP * D) {
           store_out(p, head0 * D + e, finalize(orun[q], lrun[q], mrun[q], p.phantom));
-          if (p.lse != nullptr && e % D == 0) p.lse[head0 + e / D] = row_lse(p.phantom, mrun[q], lrun[q]);
+          if constexpr (LSE) {
+            if (e % D == 0) p.lse[head0 + e / D] = row_lse(p.phantom, mrun[q], lrun[q]);
+          }
         }
       }
       if (t == 0) p.ws_cnt[pd.x] = 0u;  // ready for the next call on this workspace
@@ -1135,10 +1139,10 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
 }
 
-template <int D, int NREP, bool PREC>
+template <int D, int NREP, bool PREC, bool LSE = false>
 int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm, cudaStream_t stream) {
   using C = DCfg<D>;
-  auto kern = paged_decode_kernel<D, NREP, PREC>;
+  auto kern = paged_decode_kernel<D, NREP, PREC, LSE>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1166,18 +1170,18 @@ int launch_decode(const CUtensorMap& tkv, const CUtensorMap& tq, const DecodePar
   return check_launch("paged_decode_kernel");
 }
 
-template <int D, bool PREC>
+template <int D, bool PREC, bool LSE = false>
 int dispatch_nrep(int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm,
                   cudaStream_t stream) {
   switch (nrep) {
-    case 1: return launch_decode<D, 1, PREC>(tkv, tq, prm, stream);
-    case 2: return launch_decode<D, 2, PREC>(tkv, tq, prm, stream);
-    case 3: return launch_decode<D, 3, PREC>(tkv, tq, prm, stream);
-    case 4: return launch_decode<D, 4, PREC>(tkv, tq, prm, stream);
-    case 5: return launch_decode<D, 5, PREC>(tkv, tq, prm, stream);
-    case 6: return launch_decode<D, 6, PREC>(tkv, tq, prm, stream);
-    case 7: return launch_decode<D, 7, PREC>(tkv, tq, prm, stream);
-    case 8: return launch_decode<D, 8, PREC>(tkv, tq, prm, stream);
+    case 1: return launch_decode<D, 1, PREC, LSE>(tkv, tq, prm, stream);
+    case 2: return launch_decode<D, 2, PREC, LSE>(tkv, tq, prm, stream);
+    case 3: return launch_decode<D, 3, PREC, LSE>(tkv, tq, prm, stream);
+    case 4: return launch_decode<D, 4, PREC, LSE>(tkv, tq, prm, stream);
+    case 5: return launch_decode<D, 5, PREC, LSE>(tkv, tq, prm, stream);
+    case 6: return launch_decode<D, 6, PREC, LSE>(tkv, tq, prm, stream);
+    case 7: return launch_decode<D, 7, PREC, LSE>(tkv, tq, prm, stream);
+    case 8: return launch_decode<D, 8, PREC, LSE>(tkv, tq, prm, stream);
     default: return set_error(MTN_EINVAL, "paged decode: query heads per kv head %d not in [1,8]", nrep);
   }
 }
@@ -1185,6 +1189,8 @@ int dispatch_nrep(int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const
 template <int D>
 int dispatch_prec(bool prec, int nrep, const CUtensorMap& tkv, const CUtensorMap& tq, const DecodeParams& prm,
                   cudaStream_t stream) {
+  if (prm.lse != nullptr)  // shared-prefix decode: bf16 operands only (checked by the caller)
+    return dispatch_nrep<D, false, true>(nrep, tkv, tq, prm, stream);
   return prec ? dispatch_nrep<D, true>(nrep, tkv, tq, prm, stream) : dispatch_nrep<D, false>(nrep, tkv, tq, prm, stream);
 }
 

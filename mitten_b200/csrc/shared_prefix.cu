@@ -109,6 +109,8 @@ int mtn_paged_decode_shared_prefix(const mtn_kv_layout* pool, int32_t layer, con
   MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_decode_shared_prefix: bad o dtype");
   MTN_CHECK_ARG((reinterpret_cast<uintptr_t>(o) & 15) == 0, "mtn_paged_decode_shared_prefix: o must be 16-byte aligned");
   MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads <= 65535, "mtn_paged_decode_shared_prefix: bad num_q_heads");
+  MTN_CHECK_ARG(!(flags & MTN_ATTN_SPLIT_BF16),
+                "mtn_paged_decode_shared_prefix: MTN_ATTN_SPLIT_BF16 is not supported (bf16 operands only)");
   MTN_CHECK_ARG(n_seqs <= (1 << 24), "mtn_paged_decode_shared_prefix: n_seqs %d too large", n_seqs);
   const int64_t prefix_len = static_cast<int64_t>(n_prefix_pages) * pool->page_size;
   MTN_CHECK_ARG(prefix_len < (int64_t(1) << 31), "mtn_paged_decode_shared_prefix: prefix too long");
