@@ -836,7 +836,7 @@ def run_cfg3(args, local) -> dict:
             "shared_prefix": {"call": "mtn_paged_decode_shared_prefix (prefix once per batch, LSE combine)",
                               "ms_per_step": 1e3 * t_sp / steps, "tokens_per_s": n * steps / t_sp,
                               "speedup": t / t_sp, "unique_kv_gbs": unique / (t_sp / steps) / 1e9,
-                              "launches_per_step": 4}}
+                              "launches_per_step": 3}}
 
 
 def run_cfg3_engine(args, local) -> dict:

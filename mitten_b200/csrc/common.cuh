@@ -77,7 +77,7 @@ int paged_prefill_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, 
                        int32_t o_dtype, int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                        const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
                        const int32_t* seq_lens, int32_t max_q_len, float scale, uint32_t flags, void* workspace,
-                       size_t workspace_bytes, void* stream, int noncausal, float* lse);
+                       size_t workspace_bytes, void* stream, int noncausal, float* lse, int nc_pages);
 int paged_decode_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, int32_t q_dtype, void* o,
                       int32_t o_dtype, const void* k_new, const void* v_new, int32_t new_dtype, int32_t n_seqs,
                       int32_t num_q_heads, const int32_t* kv_indptr, const int32_t* kv_indices,

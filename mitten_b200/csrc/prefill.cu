@@ -64,6 +64,10 @@ struct PrefillParams {
   // log2-domain log-sum-exp of the row's softmax, [total_q][hq], or null.
   int noncausal;
   float* lse;
+  // Non-causal launches have one pseudo-sequence given by scalars: nc_q_len
+  // query rows over the nc_pages pages kv_indices[0 ..] (all tokens valid).
+  int nc_q_len;
+  int nc_pages;
   // Split of long units, for launches with few units: a (query tile, head,
   // sequence) unit is cut into k <= kMaxPieces pieces of consecutive kv
   // tiles, run by CTAs blockIdx.z = piece * n_seqs + sequence (pieces in the
@@ -132,7 +136,13 @@ enum Bar {
 // ceil(n / plen) < T / plen + U <= S).  0 when the units fill the SMs.
 __device__ __forceinline__ int64_t split_piece_len(const PrefillParams& p, int bn, int lane) {
   int64_t t = 0, u = 0;
-  for (int s = lane; s < p.n_seqs; s += 32) {
+  if (p.noncausal) {
+    if (lane == 0) {
+      u = (p.nc_q_len + kBM - 1) / kBM;
+      t = u * ((static_cast<int64_t>(p.nc_pages) * p.ps + bn - 1) / bn);
+    }
+  }
+  for (int s = lane; !p.noncausal && s < p.n_seqs; s += 32) {
     const int q0 = p.qo_indptr[s];
     const int ql = p.qo_indptr[s + 1] - q0;
     if (ql <= 0) continue;
@@ -150,7 +160,10 @@ __device__ __forceinline__ int64_t split_piece_len(const PrefillParams& p, int b
   t *= p.hq;
   u *= p.hq;
   if (u >= p.split_target) return 0;
-  return max(static_cast<int64_t>(kMinPiece), (t + (p.split_target - u) - 1) / (p.split_target - u));
+  // Non-causal launches (the shared-prefix part: few units, short) cut down
+  // to 2-tile pieces; causal ones keep kMinPiece.
+  const int64_t min_piece = p.noncausal ? 2 : kMinPiece;
+  return max(min_piece, (t + (p.split_target - u) - 1) / (p.split_target - u));
 }
 
 // 1 / l for a row whose softmax has max m (log2 units) and sum l, with the
@@ -321,6 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   int q0 = 0, q_len = 0, kv_beg = 0, npages = 0, kv_len = 0;
   auto load_meta = [&]() {
+    if (p.noncausal) {
+      q0 = 0;
+      q_len = p.nc_q_len;
+      kv_beg = 0;
+      npages = p.nc_pages;
+      kv_len = p.nc_pages * p.ps;
+      return;
+    }
     q0 = p.qo_indptr[s];
     q_len = p.qo_indptr[s + 1] - q0;
     kv_beg = p.kv_indptr[s];
@@ -1010,7 +1031,7 @@ int mtn_paged_prefill(const mtn_kv_layout* pool, int32_t layer, const void* q, i
                       float scale, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
   return mtn::paged_prefill_impl(pool, layer, q, q_dtype, o, o_dtype, n_seqs, total_q, num_q_heads, qo_indptr,
                                  kv_indptr, kv_indices, seq_lens, max_q_len, scale, flags, workspace, workspace_bytes,
-                                 stream, 0, nullptr);
+                                 stream, 0, nullptr, 0);
 }
 
 }  // extern "C"
@@ -1021,13 +1042,18 @@ int paged_prefill_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, 
                        int32_t o_dtype, int32_t n_seqs, int64_t total_q, int32_t num_q_heads,
                        const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
                        const int32_t* seq_lens, int32_t max_q_len, float scale, uint32_t flags, void* workspace,
-                       size_t workspace_bytes, void* stream, int noncausal, float* lse) {
+                       size_t workspace_bytes, void* stream, int noncausal, float* lse, int nc_pages) {
+  // noncausal: one pseudo-sequence (n_seqs must be 1) of total_q query rows
+  // over the pages kv_indices[0 .. nc_pages); qo_indptr, kv_indptr and
+  // seq_lens are not read.
   int st = mtn::validate_layout(pool, layer, "mtn_paged_prefill");
   if (st != MTN_OK) return st;
   MTN_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65535, "mtn_paged_prefill: n_seqs %d outside [0, 65535]", n_seqs);
   MTN_CHECK_ARG(total_q >= 0 && total_q < (int64_t(1) << 31), "mtn_paged_prefill: bad total_q");
   if (n_seqs == 0 || total_q == 0) return MTN_OK;
-  MTN_CHECK_ARG(q && o && qo_indptr && kv_indptr && kv_indices && seq_lens, "mtn_paged_prefill: null pointer");
+  MTN_CHECK_ARG(q && o && kv_indices && (noncausal || (qo_indptr && kv_indptr && seq_lens)),
+                "mtn_paged_prefill: null pointer");
+  MTN_CHECK_ARG(!noncausal || (n_seqs == 1 && nc_pages > 0), "mtn_paged_prefill: bad non-causal launch");
   MTN_CHECK_ARG(q_dtype == MTN_DTYPE_BF16 || q_dtype == MTN_DTYPE_F32, "mtn_paged_prefill: bad q dtype");
   MTN_CHECK_ARG(o_dtype == MTN_DTYPE_BF16 || o_dtype == MTN_DTYPE_F32, "mtn_paged_prefill: bad o dtype");
   MTN_CHECK_ARG(num_q_heads > 0 && num_q_heads <= 65535 && num_q_heads % pool->num_kv_heads == 0,
@@ -1065,6 +1091,8 @@ int paged_prefill_impl(const mtn_kv_layout* pool, int32_t layer, const void* q, 
   prm.err = mtn::device_error_ptr();
   prm.noncausal = noncausal;
   prm.lse = lse;
+  prm.nc_q_len = static_cast<int>(total_q);
+  prm.nc_pages = nc_pages;
   const int n_tiles = (max_q_len + mtn::kBM - 1) / mtn::kBM;
   MTN_CHECK_ARG(n_tiles <= 65535 * 32, "mtn_paged_prefill: max_q_len too large");
   // Launches whose units (bounded by (total_q / 128 + n_seqs) x heads) leave

@@ -23,7 +23,7 @@ namespace mtn {
 namespace {
 
 struct SpLayout {
-  size_t dec = 0, off_pf = 0, pf = 0, off_op = 0, off_os = 0, off_lp = 0, off_ls = 0, off_meta = 0, bytes = 0;
+  size_t dec = 0, off_pf = 0, pf = 0, off_op = 0, off_os = 0, off_lp = 0, off_ls = 0, bytes = 0;
 };
 
 size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -40,21 +40,8 @@ SpLayout sp_layout(int32_t n_seqs, int32_t hq, int32_t hkv, int32_t d) {
   w.off_os = w.off_op + o_bytes;
   w.off_lp = w.off_os + o_bytes;
   w.off_ls = w.off_lp + l_bytes;
-  w.off_meta = w.off_ls + l_bytes;
-  w.bytes = w.off_meta + 256;
+  w.bytes = w.off_ls + l_bytes;
   return w;
-}
-
-// CSR of the prefix part: one pseudo-sequence with n_seqs query rows over
-// the n_prefix shared pages.  meta = {qo_indptr[2], kv_indptr[2], seq_len}.
-__global__ void shared_prefix_meta_kernel(int32_t* meta, int32_t n_seqs, int32_t n_prefix, int32_t prefix_len) {
-  if (threadIdx.x == 0) {
-    meta[0] = 0;
-    meta[1] = n_seqs;
-    meta[2] = 0;
-    meta[3] = n_prefix;
-    meta[4] = prefix_len;
-  }
 }
 
 // out[r][:] = (o1[r] w1 + o2[r] w2) / (w1 + w2) with w = 2^(lse - max lse);
@@ -62,6 +49,7 @@ __global__ void shared_prefix_meta_kernel(int32_t* meta, int32_t n_seqs, int32_t
 __global__ void lse_combine_kernel(const float4* __restrict__ o1, const float* __restrict__ l1,
                                    const float4* __restrict__ o2, const float* __restrict__ l2, void* out,
                                    int out_f32, int64_t rows, int d4) {
+  pdl_enter();  // launched as a dependent of the decode part
   const int64_t n = rows * d4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -126,15 +114,12 @@ int mtn_paged_decode_shared_prefix(const mtn_kv_layout* pool, int32_t layer, con
   float* o_s = reinterpret_cast<float*>(w + wl.off_os);
   float* l_p = reinterpret_cast<float*>(w + wl.off_lp);
   float* l_s = reinterpret_cast<float*>(w + wl.off_ls);
-  int32_t* meta = reinterpret_cast<int32_t*>(w + wl.off_meta);
   auto s = static_cast<cudaStream_t>(stream);
-  mtn::shared_prefix_meta_kernel<<<1, 32, 0, s>>>(meta, n_seqs, n_prefix_pages, static_cast<int32_t>(prefix_len));
-  st = mtn::check_launch("shared_prefix_meta_kernel");
-  if (st != MTN_OK) return st;
-  // 1. prefix part (phantom row counted here, once)
-  st = mtn::paged_prefill_impl(pool, layer, q, q_dtype, o_p, MTN_DTYPE_F32, 1, n_seqs, num_q_heads, meta, meta + 2,
-                               prefix_pages, meta + 4, n_seqs, scale, flags & ~MTN_ATTN_PREFILL_ONE_TILE,
-                               wl.pf ? w + wl.off_pf : nullptr, wl.pf, stream, 1, l_p);
+  // 1. prefix part (phantom row counted here, once): one pseudo-sequence of
+  //    n_seqs query rows over the prefix pages
+  st = mtn::paged_prefill_impl(pool, layer, q, q_dtype, o_p, MTN_DTYPE_F32, 1, n_seqs, num_q_heads, nullptr, nullptr,
+                               prefix_pages, nullptr, n_seqs, scale, flags & ~MTN_ATTN_PREFILL_ONE_TILE,
+                               wl.pf ? w + wl.off_pf : nullptr, wl.pf, stream, 1, l_p, n_prefix_pages);
   if (st != MTN_OK) return st;
   // 2. suffix part: each sequence's own pages, with the step's append
   st = mtn::paged_decode_impl(pool, layer, q, q_dtype, o_s, MTN_DTYPE_F32, k_new, v_new, new_dtype, n_seqs,
@@ -146,10 +131,10 @@ int mtn_paged_decode_shared_prefix(const mtn_kv_layout* pool, int32_t layer, con
   const int64_t rows = static_cast<int64_t>(n_seqs) * num_q_heads;
   const int64_t n4 = rows * (D / 4);
   const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(mtn::sm_count()) * 16));
-  mtn::lse_combine_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(o_p), l_p,
-                                               reinterpret_cast<const float4*>(o_s), l_s, o,
-                                               o_dtype == MTN_DTYPE_F32, rows, D / 4);
-  return mtn::check_launch("lse_combine_kernel");
+  return mtn::launch_pdl(mtn::lse_combine_kernel, dim3(grid), dim3(256), 0, s, "lse_combine_kernel",
+                         reinterpret_cast<const float4*>(o_p), static_cast<const float*>(l_p),
+                         reinterpret_cast<const float4*>(o_s), static_cast<const float*>(l_s), o,
+                         static_cast<int>(o_dtype == MTN_DTYPE_F32), rows, D / 4);
 }
 
 }  // extern "C"
