@@ -20,11 +20,12 @@
 // segments are cut into 128-token tiles, laid end to end, and every CTA
 // takes an equal contiguous range of tiles (computed on the device from
 // seq_lens), so the producer streams TMA loads across segment boundaries
-// without bubbles.  6 warps per CTA:
+// without bubbles.  10 warps per CTA:
 //   warps 0-3  softmax: TMEM lane = token; online softmax in the exp2 domain
 //              against a CTA-wide reference max that moves only when a tile
-//              exceeds it by 2^8 (lazy rescale), P^T (bf16) to shared memory,
-//              segment epilogues.
+//              exceeds it by 2^8 (lazy rescale), P^T (bf16) to shared memory;
+//              at a segment's end they hand its row sums and maxima to the
+//              epilogue warps and go on with the next segment's tiles.
 //   warp 4     producer: per segment the Q^T operand, per tile one TMA box
 //              per page per 64-wide head-dim block straight from the block
 //              table into a 3-stage ring (at head_dim 256: a 6-slot ring of
@@ -33,6 +34,9 @@
 //              next tile's QK^T overlaps this tile's softmax; O^T
 //              double-buffered per segment so an epilogue overlaps the next
 //              segment.
+//   warps 6-9  segment epilogues: O^T out of TMEM once the segment's last
+//              P V is done, normalised outputs or partials, merge tickets
+//              and the merges.
 // A segment cut by CTA boundaries leaves (m, l, O) partials in per-CTA
 // workspace slots.  After its last tile each CTA takes a ticket for the (at
 // most two) segments it only holds part of; the last CTA to arrive merges
@@ -64,7 +68,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int32_t kPlanMagic = 0x504e544d;  // "MTNP"
 constexpr int kPlanEntry = 8;
 constexpr int kTile = 128;    // tokens per tile = MMA1 M = TMEM lanes
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 10 warps: softmax 0-3, producer 4, MMA 5, epilogue 6-9
+constexpr int kEpiWarp0 = 6;
 constexpr int kN = 16;        // query heads per KV head, padded (MMA N)
 // P is exponentiated against a reference max that moves only when a tile's
 // max exceeds it by more than 2^8, so P <= 256 and O^T is rarely rescaled.
@@ -115,11 +120,12 @@ struct DCfg {
   static constexpr int kKVBytes = kTile * D * 2;           // one of K or V per stage
   static constexpr int kPBytes = kN * kTile * 2;           // P^T operand: 16 rows x 128 tokens
   // Small state first, then the 1 KiB-aligned operand area.
-  static constexpr int kOffBar = 0;                        // 16 mbarriers
-  static constexpr int kOffMisc = kOffBar + 24 * 8;        // tmem base, abort, last flag, start info
-  static constexpr int kOffRed = kOffMisc + 64;            // [2][4][16] maxima, [4][16] sums
-  static constexpr int kOffScan = kOffRed + (2 * 4 * kN + 4 * kN) * 4;  // [6] warp totals
-  static constexpr int kOffPend = kOffScan + 64;                         // [2] int4 deferred merges
+  static constexpr int kOffBar = 0;                        // 28 mbarriers
+  static constexpr int kOffMisc = kOffBar + 28 * 8;        // tmem base, abort, last flag, start info
+  // [2][4][16] tile maxima; per O^T buffer [2][4][16] warp row sums and [2][16] reference maxima
+  static constexpr int kOffRed = kOffMisc + 64;
+  static constexpr int kOffScan = kOffRed + (2 * 4 * kN + 2 * 4 * kN + 2 * kN) * 4;  // [10] warp totals
+  static constexpr int kOffPend = kOffScan + (kThreads / 32) * 8;                   // [2] int4 deferred merges
   static constexpr int kSmallBytes = kOffPend + 32 + 16;
   static constexpr int kOffQ = 0;                          // [2] relative to the aligned operand area
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
@@ -142,9 +148,13 @@ enum Bar {
   kODone0 = 16,   // [2] P V of tile i done: P^T buffer i&1 free, O^T current
   kQFull0 = 18,   // [2]
   kQEmpty0 = 20,  // [2]
-  kOFree0 = 22,   // [2]
-  kNumBars = 24
+  kOFree0 = 22,   // [2] O^T buffer read out by the epilogue (and its sums slot free)
+  kEFull0 = 24,   // [2] softmax state of the segment in O^T buffer b handed to the epilogue
+  kOSeg0 = 26,    // [2] last P V of the segment in O^T buffer b done
+  kNumBars = 28
 };
+static_assert(kNumBars * 8 <= DCfg<64>::kOffMisc, "mbarrier area");
+static_assert(DCfg<64>::kOffPend % 16 == 0 && DCfg<128>::kOffPend % 16 == 0, "int4 alignment");
 
 // A segment's arrival ticket: one atomic add at gpu scope with acquire and
 // release semantics.  Release: the partials this CTA's threads wrote before
@@ -285,7 +295,8 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   int* start_len = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 32);
   int* start_pbeg = reinterpret_cast<int*>(smem_raw + C::kOffMisc + 36);
   float* red_max = reinterpret_cast<float*>(smem_raw + C::kOffRed);  // [2][4][16]
-  float* red_sum = red_max + 2 * 4 * kN;                             // [4][16]
+  float* red_l = red_max + 2 * 4 * kN;                               // [2][4][16]
+  float* red_m = red_l + 2 * 4 * kN;                                 // [2][16]
   int64_t* scan = reinterpret_cast<int64_t*>(smem_raw + C::kOffScan);  // [6]
   int4* pend = reinterpret_cast<int4*>(smem_raw + C::kOffPend);        // [2] (segment, ca, cb, wa)
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem_raw + C::kOffPend + 32);  // [2]
@@ -320,7 +331,9 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   const int sb = min(p.n_seqs, tid * chunk), se = min(p.n_seqs, sb + chunk);
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1) ? 4 : (i == kOFree0 || i == kOFree0 + 1) ? 128 : 1);
+      mbar_init(&bars[i], (i == kPFull0 || i == kPFull0 + 1 || i == kEFull0 || i == kEFull0 + 1) ? 4
+                          : (i == kOFree0 || i == kOFree0 + 1)                              ? 128
+                                                                                            : 1);
     *abort_flag = 0;
     *start_s = -1;
     fence_barrier_init();
@@ -436,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
   }
 
   uint8_t* p_s = big + C::kOffP;
-  if (warp != 4) {
+  if (warp < 4 || warp == 5) {
     // The zeroed P^T operand (rows >= NREP stay zero) for the MMA and
     // softmax roles; the producer starts loading meanwhile.
     const int tid160 = warp == 5 ? 128 + lane : tid;
@@ -779,6 +792,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           if (!ok) break;
         }
         const bool first = (i == 0) || wo.j == 0;
+        const bool last_o = (i == n_local - 1) || wo.j == wo.T - 1;
         if (first) {
           ++o_seg;
           if (o_seg >= 2 &&
@@ -805,6 +819,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           tc::mma_commit(&bars[kODone0 + (i & 1)]);
           tc::mma_commit(&bars[kKVEmpty0 + s2]);
           tc::mma_commit(&bars[kKVEmpty0 + s3]);
+          if (last_o) tc::mma_commit(&bars[kOSeg0 + (o_seg & 1)]);
           if (i + 1 < n_local) wo.next(p);
           continue;
         }
@@ -822,24 +837,18 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         }
         tc::mma_commit(&bars[kODone0 + (i & 1)]);
         tc::mma_commit(&bars[kKVEmpty0 + st]);
+        if (last_o) tc::mma_commit(&bars[kOSeg0 + (o_seg & 1)]);
         if (i + 1 < n_local) wo.next(p);
       }
     }
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------ softmax
     const int t = tid;  // token row of the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    // Rows of O^T this thread holds: M=64 puts row d in lane (d % 16) + 32 (d / 16);
-    // M=128 puts row d in lane d; D = 256 uses two M=128 blocks 16 columns apart.
-    const bool holds = (C::kMO == 64) ? (lane < 16) : true;
-    const int d_base = (C::kMO == 64) ? warp * 16 + lane : warp * 32 + lane;
     Walker w;
     w.start(p, s0, pre0, t0, len0, pbeg0);
     float m_ref[NREP], l_tok[NREP];
     int seg = -1;
-    int n_pend = 0;  // partial segments written (at most the first and the last)
-    bool early = false;             // pend[0] already holds its ticket (thread 0)
-    unsigned int early_ticket = 0;  // that ticket
     bool ok = true;
     for (int i = 0; i < n_local; ++i) {
       const bool first = (i == 0) || w.j == 0;
@@ -947,10 +956,65 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       if (lane == 0) tc::mbar_arrive(&bars[kPFull0 + (i & 1)]);
 
       if (last) {
-        // ---- segment epilogue: O^T of (s, g) over this CTA's tiles.
-        ok = tc::wait_bounded(&bars[kODone0 + (i & 1)], (i >> 1) & 1, abort_flag, p.err, 32);
+        // ---- hand the segment to the epilogue warps: per-warp row sums and
+        // the reference maxima into slot seg & 1.  The slot (and O^T buffer
+        // seg & 1) is free once the epilogue of segment seg - 2 has read it.
+        if (seg >= 2) {
+          bool fr = true;
+          if (lane == 0) fr = tc::wait_bounded(&bars[kOFree0 + (seg & 1)], ((seg >> 1) - 1) & 1, abort_flag, p.err, 34);
+          ok = __shfl_sync(0xffffffffu, fr, 0);
+          if (!ok) break;
+        }
+        float* rl = red_l + (seg & 1) * 4 * kN;
+#pragma unroll
+        for (int h = 0; h < NREP; ++h) {
+          const float wsum = warp_sum(l_tok[h]);
+          if (lane == 0) rl[warp * kN + h] = wsum;
+        }
+        if (warp == 0 && lane == 0) {
+#pragma unroll
+          for (int h = 0; h < NREP; ++h) red_m[(seg & 1) * kN + h] = m_ref[h];
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[kEFull0 + (seg & 1)]);
+      }
+      if (i + 1 < n_local) w.next(p);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Warps 6-9: warp w reads TMEM lanes 32 (w % 4) .. +31, so the four
+    // cover O^T's 128 lanes.  Segment k's epilogue waits for its softmax
+    // state (kEFull) and its last P V (kOSeg), reads O^T, then frees the
+    // buffer (kOFree) before the global stores.
+    const int t = tid - kEpiWarp0 * 32;  // 0 .. 127
+    const int quarter = warp & 3;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    // Rows of O^T this thread holds: M=64 puts row d in lane (d % 16) + 32 (d / 16);
+    // M=128 puts row d in lane d; D = 256 uses two M=128 blocks 16 columns apart.
+    const bool holds = (C::kMO == 64) ? (lane < 16) : true;
+    const int d_base = (C::kMO == 64) ? quarter * 16 + lane : quarter * 32 + lane;
+    grid_wait();
+    empty_outputs();
+    Walker w;
+    w.start(p, s0, pre0, t0, len0, pbeg0);
+    int seg = -1;
+    int n_pend = 0;  // partial segments written (at most the first and the last)
+    bool early = false;             // pend[0] already holds its ticket (thread 0)
+    unsigned int early_ticket = 0;  // that ticket
+    bool ok = true;
+    for (int i = 0; i < n_local; ++i) {
+      const bool first = (i == 0) || w.j == 0;
+      const bool last = (i == n_local - 1) || w.j == w.T - 1;
+      if (first) ++seg;
+      if (last) {
+        const int b = seg & 1;
+        bool good = tc::wait_bounded(&bars[kEFull0 + b], (seg >> 1) & 1, abort_flag, p.err, 40) &&
+                    tc::wait_bounded(&bars[kOSeg0 + b], (seg >> 1) & 1, abort_flag, p.err, 41);
+        good = __all_sync(0xffffffffu, good);  // warp-uniform for tcgen05.ld
+        ok = !tc::named_sync_or(3, 128, !good);  // and uniform over the four warps
+        if (!ok) break;
         tc::fence_after_sync();
-        if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform for tcgen05.ld
+        const uint32_t o_col = C::kTmemO + b * 32;
         float ov[D / C::kMO][16];
 #pragma unroll
         for (int mb = 0; mb < D / C::kMO; ++mb) {
@@ -960,19 +1024,15 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             for (int h = 0; h < NREP; ++h) ov[mb][h] += ov[mb][h + 8];  // V.P_hi + V.P_lo
           }
         }
-        tc::fence_before_sync();
-        tc::mbar_arrive(&bars[kOFree0 + (seg & 1)]);  // O^T buffer reusable two segments on
+        float l_cta[NREP], m_seg[NREP];
+        const float* rl = red_l + b * 4 * kN;
 #pragma unroll
         for (int h = 0; h < NREP; ++h) {
-          const float wsum = warp_sum(l_tok[h]);
-          if (lane == 0) red_sum[warp * kN + h] = wsum;
+          l_cta[h] = rl[h] + rl[kN + h] + rl[2 * kN + h] + rl[3 * kN + h];
+          m_seg[h] = red_m[b * kN + h];
         }
-        tc::named_sync(1, 128);
-        float l_cta[NREP];
-#pragma unroll
-        for (int h = 0; h < NREP; ++h)
-          l_cta[h] = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] + red_sum[3 * kN + h];
-        tc::named_sync(1, 128);  // red_sum is reused by the next segment
+        tc::fence_before_sync();
+        tc::mbar_arrive(&bars[kOFree0 + b]);  // O^T buffer and sums slot reusable two segments on
         const int64_t head0 = static_cast<int64_t>(w.s) * p.hq + w.g * NREP;
         const int64_t s_start = w.seg_start(p);
         const int64_t ca = cta_of(bnd, s_start, U, ctas), cb = cta_of(bnd, s_start + w.T - 1, U, ctas);
@@ -983,12 +1043,12 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
 #pragma unroll
               for (int h = 0; h < NREP; ++h)
                 store_out(p, (head0 + h) * D + d_base + mb * 128,
-                          finalize(ov[mb][h], l_cta[h], m_ref[h], p.phantom));
+                          finalize(ov[mb][h], l_cta[h], m_seg[h], p.phantom));
           }
           if constexpr (LSE) {
 #pragma unroll
             for (int h = 0; h < NREP; ++h)
-              if (t == h) p.lse[head0 + h] = row_lse(p.phantom, m_ref[h], l_cta[h]);  // one thread per head
+              if (t == h) p.lse[head0 + h] = row_lse(p.phantom, m_seg[h], l_cta[h]);  // one thread per head
           }
         } else {
           // Partial: slot (cta, 0) if the segment is this CTA's first, else (cta, 1).
@@ -1003,7 +1063,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
 #pragma unroll
           for (int h = 0; h < NREP; ++h) {
             if (t == h) {  // static register indexing: one thread per head
-              p.ws_ml[(slot + h) * 2 + 0] = m_ref[h];
+              p.ws_ml[(slot + h) * 2 + 0] = m_seg[h];
               p.ws_ml[(slot + h) * 2 + 1] = l_cta[h];
             }
           }
@@ -1017,7 +1077,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             // take the ticket now (those CTAs arrive later), so that at most
             // one merge is left for the end.  Only thread 0 waits on the fence;
             // the ticket value is first needed after the last tile.
-            tc::named_sync(1, 128);  // every thread's partial is written
+            tc::named_sync(3, 128);  // every thread's partial is written
             if (t == 0) early_ticket = ticket_add(&p.ws_cnt[seg_id]);
             early = true;
           }
@@ -1031,7 +1091,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     // (both in one round trip); the last CTA to arrive merges the pieces in
     // CTA order.
     if (ok && n_pend > 0) {
-      tc::named_sync(1, 128);  // pend[] and this CTA's partials are complete
+      tc::named_sync(3, 128);  // pend[] and this CTA's partials are complete
       if (t < n_pend) {
         const int4 pd = pend[t];
         unsigned int ticket;
@@ -1042,7 +1102,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         }
         last_flag[t] = (ticket == static_cast<unsigned int>(pd.z - pd.y)) ? 1 : 0;
       }
-      tc::named_sync(1, 128);
+      tc::named_sync(3, 128);
     }
     for (int pi = 0; ok && pi < n_pend; ++pi) {
       if (!last_flag[pi]) continue;
@@ -1051,7 +1111,9 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
       const int64_t head0 = static_cast<int64_t>(s) * p.hq + g * NREP;
       const int ca = pd.y, np = pd.z - pd.y + 1, wa = pd.w;
       constexpr int kElems = (NREP * D + 127) / 128;
-      constexpr int kChunk = 4;                       // pieces per round: one round trip each
+      // Pieces per round (one round trip each); 2 at 16 elements per thread,
+      // so the merge stays within the registers of a 320-thread CTA.
+      constexpr int kChunk = kElems > 8 ? 2 : 4;
       float* stage = reinterpret_cast<float*>(p_s);  // [kChunk][16][2] (m, l) in the idle P^T buffer
       float mrun[kElems], orun[kElems], lrun[kElems];
 #pragma unroll
@@ -1089,7 +1151,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           stage[(mk_ * kN + mh) * 2 + 0] = ml.x;
           stage[(mk_ * kN + mh) * 2 + 1] = ml.y;
         }
-        tc::named_sync(1, 128);
+        tc::named_sync(3, 128);
 #pragma unroll
         for (int q = 0; q < kElems; ++q) {
           const int e = t + q * 128;
@@ -1115,7 +1177,7 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
             lrun[q] += stage[(u * kN + h) * 2 + 1] * a;
           }
         }
-        tc::named_sync(1, 128);  // the stage is rewritten by the next round
+        tc::named_sync(3, 128);  // the stage is rewritten by the next round
       }
 #pragma unroll
       for (int q = 0; q < kElems; ++q) {
