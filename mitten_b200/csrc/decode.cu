@@ -74,6 +74,8 @@ constexpr int kN = 16;        // query heads per KV head, padded (MMA N)
 // P is exponentiated against a reference max that moves only when a tile's
 // max exceeds it by more than 2^8, so P <= 256 and O^T is rarely rescaled.
 constexpr float kRescaleLog2 = 8.0f;
+// Page id of a box position past its sequence's last page (never a valid id).
+constexpr int kPastEnd = -0x40000000;
 
 struct DecodeParams {
   int64_t num_pages;
@@ -102,6 +104,7 @@ struct DecodeParams {
   int* err;
   const int32_t* plan;   // host-made work plan (mtn_paged_decode_plan) or null
   float* lse;            // [n_seqs][hq] log2-domain log-sum-exp of each row, or null
+  int oob_row;           // a pool-view row past the tensor (its boxes read as zeros), or -1
 };
 
 template <int D>
@@ -505,7 +508,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
     auto fetch = [&](int& pg_o, int& apg_o, int& apos_o, int64_t& asrc_o, uint4& ak_o, uint4& av_o, bool rows) {
       const int npg = (wp.len + p.ps - 1) / p.ps;
       pg_o = 0;
-      if (lane < tile_pages) pg_o = p.kv_indices[wp.pbeg + min(wp.j * tile_pages + lane, npg - 1)];
+      // Box positions past the sequence's last page take no page id: their
+      // boxes are loaded from p.oob_row, which the TMA unit fills with zeros
+      // without reading memory (kPastEnd); the softmax masks those tokens.
+      if (lane < tile_pages) {
+        const int pi = wp.j * tile_pages + lane;
+        pg_o = (pi >= npg && p.oob_row >= 0) ? kPastEnd : p.kv_indices[wp.pbeg + min(pi, npg - 1)];
+      }
       apos_o = -1;  // no append
       apg_o = 0;
       ak_o = make_uint4(0u, 0u, 0u, 0u);
@@ -615,12 +624,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
           // 0-1, V blocks 2-3; item n sits in slot n % 6, refilled once the
           // MMA that read item n - 6 is done.
           int64_t page = lane < tile_pages ? pg[rs] : 0;
-          if (lane < tile_pages && (page < 0 || page >= p.num_pages)) {
+          const bool past = page == kPastEnd;
+          if (lane < tile_pages && !past && (page < 0 || page >= p.num_pages)) {
             record_error(p.err, kDevErrBadPage, w.s);
-            page = 0;  // past the sequence's last page: reload a valid page (masked)
+            page = 0;  // reload a valid page instead (masked)
           }
-          const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
-          const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
+          const int64_t rk = past ? p.oob_row : p.row_k + (page * p.hkv + w.g) * p.ps;
+          const int64_t rv = past ? p.oob_row : p.row_v + (page * p.hkv + w.g) * p.ps;
           for (int hh = 0; hh < 4; ++hh) {
             const int n = 4 * i + hh;
             const int slot = n % C::kRingSlots;
@@ -648,12 +658,13 @@ __global__ void __launch_bounds__(kThreads, DCfg<D>::kCtasPerSm)
         __syncwarp();
         if (lane < tile_pages) {
           int64_t page = pg[rs];
-          if (page < 0 || page >= p.num_pages) {
+          const bool past = page == kPastEnd;
+          if (!past && (page < 0 || page >= p.num_pages)) {
             record_error(p.err, kDevErrBadPage, w.s);
-            page = 0;  // past the sequence's last page: reload a valid page (masked)
+            page = 0;  // reload a valid page instead (masked)
           }
-          const int64_t rk = p.row_k + (page * p.hkv + w.g) * p.ps;
-          const int64_t rv = p.row_v + (page * p.hkv + w.g) * p.ps;
+          const int64_t rk = past ? p.oob_row : p.row_k + (page * p.hkv + w.g) * p.ps;
+          const int64_t rv = past ? p.oob_row : p.row_v + (page * p.hkv + w.g) * p.ps;
           uint8_t* kst = big + C::kOffK + st * C::kKVBytes;
           uint8_t* vst = big + C::kOffV + st * C::kKVBytes;
 #pragma unroll
@@ -1439,6 +1450,12 @@ int mtn::paged_decode_impl(const mtn_kv_layout* pool, int32_t layer, const void*
   prm.row_v = (static_cast<int64_t>(layer) * 2 + 1) * rows_per_block;
   prm.pool = static_cast<__nv_bfloat16*>(pool->base);
   prm.num_pages = pool->num_pages;
+  {
+    // Boxes of pool_rows .. + page_size - 1 lie past the tensor (zero fill);
+    // kept only while those coordinates fit TMA's signed 32-bit range.
+    const int64_t rows = pool_rows(pool);
+    prm.oob_row = rows + pool->page_size < (int64_t(1) << 31) ? static_cast<int>(rows) : -1;
+  }
   prm.hkv = pool->num_kv_heads;
   prm.ps = pool->page_size;
   prm.hq = num_q_heads;
