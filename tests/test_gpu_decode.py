@@ -88,6 +88,21 @@ def test_decode_many_sequences_mixed_lengths(cuda_device):
     check(case, 14, 64, q, qu, out)
 
 
+@pytest.mark.parametrize("hq,hkv,d", [(14, 2, 64), (28, 4, 128), (8, 1, 256)])
+def test_decode_many_short_segments_per_cta(cuda_device, hq, hkv, d):
+    """Several one- or two-tile segments per CTA, some cut by CTA boundaries:
+    the softmax warps hand each segment to the epilogue warps through
+    per-O^T-buffer barriers while the next segments stream, so every
+    buffer's barriers go through many phases in one launch."""
+    rng = np.random.default_rng(d + hq)
+    lens = [int(x) for x in rng.integers(1, 260, size=600 if d == 64 else 300)]
+    lens[::37] = [1] * len(lens[::37])
+    case = make_case(lens, hkv, d, seed=d + 3)
+    q, qu, out = run_decode(case, hq, d)
+    check(case, hq, d, q, qu, out)
+    assert paged.device_error(0) == (0, 0)
+
+
 def test_decode_deterministic_and_workspace_reuse(cuda_device):
     lens = [3000, 2000, 1000, 50, 7000]
     case = make_case(lens, 2, 64, seed=4)
