@@ -1,6 +1,6 @@
 """The paged decode kernel's mbarrier protocol, replayed on the CPU.
 
-`mitten_b200/csrc/decode.cu` (`paged_decode_kernel`) runs five roles per
+`mitten_b200/csrc/decode.cu` (`paged_decode_kernel`) runs four roles per
 CTA -- producer (warp 4), MMA issuer (warp 5), softmax (warps 0-3), segment
 epilogue (warps 6-9) -- that synchronise only through mbarriers waited on by
 phase parity.  A parity wait for phase k returns once k has completed, but
