@@ -362,8 +362,8 @@ def run_ours(args, rank, world, local, pg):
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
                 "path": "per step: Q/K/V/seq_lens packed in one pinned host buffer -> one H2D copy -> "
-                        "mtn_paged_decode (C ABI) -> D2H output; steps in groups of 4: group g+1's H2D and "
-                        "group g-1's D2H overlap group g's kernels (upload/download streams, 8 staging and 8 "
+                        "mtn_paged_decode (C ABI) -> D2H output; steps in groups of 8: group g+1's H2D and "
+                        "group g-1's D2H overlap group g's kernels (upload/download streams, 16 staging and 16 "
                         "output buffers, only a group's first launch waits on copy events), batches rotating "
                         "as above"},
         "gpu_launches": args.steps,
@@ -452,10 +452,10 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
 
     Each step's Q, new K/V and seq_lens are packed in one pinned host buffer and copied in with one
     H2D copy; O comes back with one D2H copy.  Copies overlap the kernels: the steps run in groups
-    of G = 4; the uploads of group g+1 (on an upload stream) and the downloads of group g-1 (on a
+    of G = 8; the uploads of group g+1 (on an upload stream) and the downloads of group g-1 (on a
     download stream) run while group g's kernels run, through 2G device staging and 2G output
     buffers.  Only the first launch of a group waits (by events) for its group's uploads and for
-    the downloads that free its output buffers, so the other three keep the kernel-to-kernel edge
+    the downloads that free its output buffers, so the other seven keep the kernel-to-kernel edge
     that lets a decode launch start while the previous one finishes (an event wait in front of
     every launch measured ~3 us more per step).  All K steps are captured in one CUDA graph and
     replayed between two events.
@@ -468,7 +468,7 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
 
     lib = _lib.lib()
     steps = args.steps
-    G = 4
+    G = 8
     NB = 2 * G  # staging and output buffers
     gen = torch.Generator()
     gen.manual_seed(5)
