@@ -447,6 +447,35 @@ def run_append_and_copy(st, pool, device, stream) -> dict:
     return res
 
 
+def e2e_schedule(n: int, group: int = 8) -> list:
+    """Host issue order of run_e2e's pipeline for n steps: (op, step, deps) with op one of
+    "upload" (host -> staging buffer step % 2group, upload stream), "kernel" (the decode of that
+    step, compute stream) or "download" (its output buffer step % 2group -> host, download stream);
+    deps are the (op, step) events the op's stream waits for first.  Groups of `group` steps: the
+    uploads of group g+2 are issued once group g's kernels are, each waiting for the kernel that
+    last read its staging buffer; only a group's first kernel waits, for its group's uploads and
+    for the downloads of group g-2 (the last users of the output buffers the group writes)."""
+    nb = 2 * group
+    ops = []
+
+    def upload(j):
+        ops.append(("upload", j, [("kernel", j - nb)] if j >= nb else []))
+
+    for j in range(min(n, nb)):  # groups 0 and 1
+        upload(j)
+    for j in range(n):
+        deps = []
+        if j % group == 0:
+            deps = [("upload", u) for u in range(j, min(n, j + group))]
+            deps += [("download", u) for u in range(j - nb, j - nb + group) if u >= 0]
+        ops.append(("kernel", j, deps))
+        ops.append(("download", j, [("kernel", j)]))
+        if j % group == group - 1:
+            for u in range(j + 1 + group, min(n, j + 1 + nb)):
+                upload(u)
+    return ops
+
+
 def run_e2e(args, st, pool, ws, device, stream, total_steps):
     """Append + decode through the C ABI with host inputs/outputs copied inside the timed region.
 
@@ -506,39 +535,21 @@ def run_e2e(args, st, pool, ws, device, stream, total_steps):
     def pipeline(first, n):
         """Steps first .. first+n-1 on the current (compute) stream with overlapped copies."""
         comp = torch.cuda.current_stream()
-        ev_in = [torch.cuda.Event() for _ in range(n)]
-        ev_k = [torch.cuda.Event() for _ in range(n)]
-        ev_out = [torch.cuda.Event() for _ in range(n)]
+        ev = {kind: [torch.cuda.Event() for _ in range(n)] for kind in ("upload", "kernel", "download")}
         up.wait_stream(comp)
         down.wait_stream(comp)
-
-        def upload(j):
-            with torch.cuda.stream(up):
-                if j >= NB:
-                    up.wait_event(ev_k[j - NB])  # kernel j-NB has read staging buffer j % NB
-                stage_d[j % NB].copy_(stage_h[first + j], non_blocking=True)
-                ev_in[j].record(up)
-
-        for j in range(min(n, 2 * G)):  # groups 0 and 1
-            upload(j)
-        for j in range(n):
-            if j % G == 0:
-                # the group's leader: its group's inputs are in, and the
-                # outputs it and the next three write have been downloaded
-                for u in range(j, min(n, j + G)):
-                    comp.wait_event(ev_in[u])
-                for u in range(j - NB, j - NB + G):
-                    if u >= 0:
-                        comp.wait_event(ev_out[u])
-            call(first + j, j % NB)
-            ev_k[j].record(comp)
-            with torch.cuda.stream(down):
-                down.wait_event(ev_k[j])
-                o_h[first + j].copy_(o_d[j % NB], non_blocking=True)
-                ev_out[j].record(down)
-            if j % G == G - 1:  # group j // G done: upload group j // G + 2
-                for u in range(j + 1 + G, min(n, j + 1 + 2 * G)):
-                    upload(u)
+        for op, j, deps in e2e_schedule(n, G):
+            strm = {"upload": up, "kernel": comp, "download": down}[op]
+            with torch.cuda.stream(strm):
+                for kind, u in deps:
+                    strm.wait_event(ev[kind][u])
+                if op == "upload":
+                    stage_d[j % NB].copy_(stage_h[first + j], non_blocking=True)
+                elif op == "kernel":
+                    call(first + j, j % NB)
+                else:
+                    o_h[first + j].copy_(o_d[j % NB], non_blocking=True)
+                ev[op][j].record(strm)
         comp.wait_stream(up)
         comp.wait_stream(down)
 
