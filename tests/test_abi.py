@@ -55,3 +55,31 @@ def test_required_bytes_kat():
     # kv_pool.rs:129-136
     assert lib.mtn_kv_required_bytes(1, 16, 1, 1, 1, 1) == 32
     assert lib.mtn_kv_required_bytes(512, 16, 28, 4, 128, 2) == 2 * 512 * 16 * 28 * 4 * 128 * 2
+
+
+def test_shared_prefix_decode_argument_checks():
+    """mtn_paged_decode_shared_prefix rejects bad arguments with MTN_EINVAL and a
+    message before it launches anything (the layout is never dereferenced)."""
+    import ctypes as C
+
+    lib = _lib.lib()
+    pool = _lib.KvLayout(0x100000, 64, 1, 16, 4, 128)  # aligned fake base
+    fake = C.c_void_p(0x200000)  # 16-byte aligned, never dereferenced
+
+    def call(prefix=fake, n_prefix=4, o=fake, o_dtype=_lib.MTN_DTYPE_BF16, flags=0, n_seqs=8, hq=28):
+        return lib.mtn_paged_decode_shared_prefix(C.byref(pool), 0, fake, _lib.MTN_DTYPE_BF16, o, o_dtype, None, None,
+                                                  _lib.MTN_DTYPE_BF16, n_seqs, hq, prefix, n_prefix, fake, fake, fake,
+                                                  0.1, flags, fake, 1 << 20, None)
+
+    cases = [
+        (dict(prefix=None), b"at least one page"),
+        (dict(n_prefix=0), b"at least one page"),
+        (dict(o_dtype=7), b"bad o dtype"),
+        (dict(o=C.c_void_p(0x200008)), b"16-byte aligned"),
+        (dict(flags=_lib.MTN_ATTN_SPLIT_BF16), b"MTN_ATTN_SPLIT_BF16"),
+        (dict(hq=0), b"num_q_heads"),
+    ]
+    for kw, msg in cases:
+        assert call(**kw) == _lib.MTN_EINVAL, kw
+        assert msg in lib.mtn_last_error(), (kw, lib.mtn_last_error())
+    assert call(n_seqs=0) == _lib.MTN_OK  # nothing to do
